@@ -1,0 +1,190 @@
+/*
+ * starling_b200 -- C ABI of the B200 (sm_100a) Granite greedy-decode library.
+ *
+ * The reference (sims1253/starling) is pure Python: its decode step is a
+ * Python loop over HF Granite modules, cuBLAS GEMMs (nn.Linear) and four
+ * Triton glue kernels, captured into CUDA graphs.  Each entry point below
+ * replaces one of those call sites; the reference location is cited beside
+ * it.  Conventions:
+ *
+ *   - every pointer is a device pointer unless its comment says "host";
+ *   - bf16 tensors are passed as uint16_t*; token ids are int64 like the
+ *     reference's static_input_ids (llm_mega.py:123);
+ *   - every call is asynchronous on `stream`, allocates nothing, never
+ *     synchronises and never reads host memory after it returns, so it can be
+ *     captured into a CUDA graph;
+ *   - every call returns 0 on success, else an SB_ERR_* code or a
+ *     cudaError_t value; sb_last_error() gives the message.
+ */
+#ifndef STARLING_B200_H
+#define STARLING_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* sb_stream_t; /* a cudaStream_t */
+
+/* error codes (cudaError_t values pass through unchanged; ours start at 1000) */
+#define SB_OK 0
+#define SB_ERR_ARG 1001     /* bad shape / pointer / format */
+#define SB_ERR_CONFIG 1002  /* shape not supported by any kernel configuration */
+
+/* weight formats (weight-only; activations stay bf16) */
+#define SB_FMT_BF16 0  /* bf16 weights, as nn.Linear holds them */
+#define SB_FMT_FP8 1   /* e4m3 + fp32 per-output-row scale */
+#define SB_FMT_INT8 2  /* symmetric int8 + fp32 per-output-row scale */
+#define SB_FMT_NVFP4 3 /* e2m1 + e4m3 scale per 16 K-elements + fp32 tensor scale */
+
+/*
+ * One packed linear layer y = x W^T (W logical [n, k]).  Packed layout
+ * (written by starling_b200/pack.py): rows padded to n_pad = ceil(n/16)*16;
+ * w = [n_pad/16 row tiles][k / kg kgroups][32 lanes][16 bytes], where a
+ * kgroup is 64 (nvfp4), 32 (fp8/int8) or 16 (bf16) K elements and each lane's
+ * 16 bytes are its mma.m16n8k16 A-fragments for those K elements.
+ * scale: fp8/int8 -> float[n_pad]; nvfp4 -> e4m3 bytes
+ * [n_pad/16][k/64][8 row pairs][8] ; bf16 -> NULL.
+ */
+typedef struct SbLinear {
+  int32_t fmt;
+  int32_t n;
+  int32_t k;
+  int32_t n_pad;
+  const void* w;
+  const void* scale;
+  float global_scale; /* nvfp4 per-tensor scale, else 1 */
+  int32_t _pad;
+} SbLinear;
+
+/* One decoder layer.  qkv rows are [q heads | k heads | v heads] with the
+ * two RoPE halves of every q/k head interleaved (packed row 2j = dim j,
+ * 2j+1 = dim j+64); gate_up rows interleave gate row i (2i) and up row i
+ * (2i+1).  Caches are [max_batch, n_kv, max_len, 128] bf16, the StaticLayer
+ * layout (transformers cache_utils.py:286-295). */
+typedef struct SbLayer {
+  const uint16_t* in_norm;
+  const uint16_t* post_norm;
+  SbLinear qkv;
+  SbLinear o;
+  SbLinear gate_up;
+  SbLinear down;
+  uint16_t* k_cache;
+  uint16_t* v_cache;
+} SbLayer;
+
+typedef struct SbModel {
+  int32_t hidden, n_q, n_kv, head_dim, inter, vocab, n_layers;
+  int32_t max_len;    /* static cache length (max_cache_len) */
+  int32_t max_batch;  /* cache batch dimension */
+  int32_t rope_max_pos;
+  float eps, attn_mult, emb_mult, res_mult, logits_mult; /* logits_mult = 1/logits_scaling */
+  const uint16_t* embed;      /* bf16 [vocab, hidden] (tied with lm_head) */
+  const uint16_t* final_norm; /* bf16 [hidden] */
+  const uint16_t* rope_cos;   /* bf16 [rope_max_pos, 64]: cos(pos * inv_freq[j]) */
+  const uint16_t* rope_sin;
+  SbLinear lm_head;
+  const SbLayer* layers; /* HOST array of n_layers */
+} SbModel;
+
+/* Per-forward state.  All dynamic values live in device memory so one
+ * captured graph serves every replay. */
+#define SB_CTRL_SLOT 0    /* cache slot of token 0 of the next forward */
+#define SB_CTRL_PADLEN 1  /* padded prompt length T (right-padded batches) */
+#define SB_CTRL_ACCEPT 2  /* verify: accepted prefix length (output) */
+#define SB_CTRL_WORDS 8
+
+#define SB_MODE_DECODE 0  /* argmax -> out_ids[step], feed back to ids, slot += M */
+#define SB_MODE_VERIFY 1  /* argmax per token -> out_ids[0..M), accept length vs ids[1..M) */
+#define SB_MODE_FIRST 2   /* as DECODE without advancing the slot (prefill's first token) */
+
+typedef struct SbState {
+  int32_t batch;    /* B streams */
+  int32_t m;        /* tokens per stream in this forward (1 = decode, L = verify) */
+  int32_t mode;     /* SB_MODE_* */
+  int32_t use_pdl;  /* launch with programmatic dependent launch */
+  int64_t eos_id;
+  int64_t pad_id;
+  int64_t* ids;             /* [B*m] input token ids */
+  int32_t* ctrl;            /* [SB_CTRL_WORDS] */
+  const int32_t* prompt_len; /* [B] real prompt lengths, or NULL (no padding) */
+  const int32_t* rope_off;   /* [B] RoPE position offset (T - T_b), or NULL */
+  int32_t* finished;         /* [B] EOS flags (batched decode), or NULL */
+  int64_t* out_ids;          /* DECODE: [steps][B]; VERIFY: [m] */
+  uint16_t* hidden;  /* [B*m, hidden] residual stream */
+  uint16_t* q;       /* [B*m, n_q*128] */
+  uint16_t* attn;    /* [B*m, n_q*128] */
+  uint16_t* act;     /* [B*m, inter] */
+  uint16_t* logits;  /* [B*m, vocab] or NULL */
+  void* workspace;   /* scratch, >= sb_workspace_bytes() bytes, zeroed once */
+  size_t workspace_bytes;
+} SbState;
+
+/* ---- library ------------------------------------------------------------ */
+const char* sb_last_error(void);
+int sb_version(void);
+/* scratch bytes an SbState needs for (model, batch*m tokens) */
+size_t sb_workspace_bytes(const SbModel* model, int32_t tokens);
+
+/* ---- fused decode step ---------------------------------------------------
+ * One full forward of state->m new tokens per stream through every layer,
+ * lm_head and argmax, i.e. FusedLLMMega._decode_step_eager
+ * (src/starling/granite/llm_mega.py:493-589) plus the in-graph argmax /
+ * feedback / position advance of MultiStepLLMMega._captured_step
+ * (src/starling/granite/multistep.py:157-188); with m > 1 it is the verify
+ * forward SpeculativeDecoder._verify_step_fused (speculative.py:598-680) with
+ * the acceptance compare of speculative.py:430-459 fused on device.
+ * `step` indexes out_ids in DECODE mode.  About 5 launches per layer. */
+int sb_decode_step(const SbModel* model, const SbState* state, int32_t step, sb_stream_t stream);
+
+/* Launch ONE kernel of the decode step on its own (profiling / live timing
+ * of a single kernel with the step's exact configuration): op = SB_OP_*,
+ * layer ignored for SB_OP_LM_HEAD.  No reference counterpart (the reference
+ * step has no separable kernels of this kind). */
+#define SB_OP_QKV 0
+#define SB_OP_ATTN 1
+#define SB_OP_O 2
+#define SB_OP_GATE_UP 3
+#define SB_OP_DOWN 4
+#define SB_OP_LM_HEAD 5
+int sb_decode_op(const SbModel* model, const SbState* state, int32_t layer, int32_t op, int32_t step,
+                 sb_stream_t stream);
+
+/* final RMSNorm + lm_head + argmax over state->hidden (B rows, before the
+ * final norm): the prefill tail `lm_head(norm(hidden))/logits_scaling` +
+ * `.argmax(-1)` (llm_mega.py:200-202, batched.py:275-276). */
+int sb_lm_head_argmax(const SbModel* model, const SbState* state, int32_t step, sb_stream_t stream);
+
+/* ---- single ops (each one replaces one reference call site) ------------- */
+/* y[m, :] = x[m, :] W^T, bf16 out: nn.Linear (llm_mega.py:534-536,560,572-573,579,588).
+ * Any m >= 1 (processed in blocks of 64 rows); y columns in packed row order. */
+int sb_linear(const SbLinear* lin, const uint16_t* x, uint16_t* y, int32_t m, int32_t use_pdl,
+              sb_stream_t stream);
+/* exact dequantisation of a packed layer to fp32 [n, k] (rows in packed order,
+ * padding rows dropped); the quantised formats have no reference counterpart */
+int sb_dequant_f32(const SbLinear* lin, float* out, sb_stream_t stream);
+/* same, rounded to bf16 (used for prefill GEMMs) */
+int sb_dequant_bf16(const SbLinear* lin, uint16_t* out, sb_stream_t stream);
+/* fused_rmsnorm (llm_kernels.py:124-139) */
+int sb_rmsnorm(const uint16_t* x, const uint16_t* w, uint16_t* y, int32_t rows, int32_t n, float eps,
+               sb_stream_t stream);
+/* fused_silu_mul (llm_kernels.py:267-285) */
+int sb_silu_mul(const uint16_t* gate, const uint16_t* up, uint16_t* out, int64_t count, sb_stream_t stream);
+/* fused_residual_scale (llm_kernels.py:320-336) */
+int sb_residual_scale(const uint16_t* x, const uint16_t* y, uint16_t* z, int64_t count, float alpha,
+                      sb_stream_t stream);
+/* RoPE of (llm_mega.py:539-543): x [rows, 128] bf16 in place, row r at position pos[r / heads] */
+int sb_rope(uint16_t* x, int32_t rows, int32_t heads, const int32_t* pos, const uint16_t* cos_tab,
+            const uint16_t* sin_tab, sb_stream_t stream);
+/* argmax over bf16 rows, lowest index on ties (torch semantics): static_logits.argmax(-1) */
+int sb_argmax_bf16(const uint16_t* x, int32_t rows, int32_t n, int64_t* out, sb_stream_t stream);
+/* decode attention for one layer (llm_mega.py:546-556 incl. StaticLayer.update and
+ * repeat_kv): q [B*m, n_q*128], caches as SbLayer, out [B*m, n_q*128] */
+int sb_attention(const SbModel* model, const SbState* state, int32_t layer, sb_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* STARLING_B200_H */

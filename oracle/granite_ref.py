@@ -267,8 +267,36 @@ def layer_forward(d: Dims, L: dict, kc: torch.Tensor, vc: torch.Tensor, hidden, 
     return residual_scale(residual, L["down"](act), d.res_mult)
 
 
+class DenseLinear(Linear):
+    """Linear over an already dequantised fp32 weight (quantised formats)."""
+
+    def __init__(self, w_f32: torch.Tensor, fmt: str):
+        self.fmt = fmt
+        self.N, self.K = w_f32.shape
+        self.w = w_f32
+        self.parts = None
+
+
+def _fused_quant(ws: list, fmt: str) -> list:
+    """Quantise the row-concatenation of ``ws`` as one tensor (the packed q|k|v
+    and gate|up matrices share one nvfp4 tensor scale), dequantise, split."""
+    w = torch.cat(ws, dim=0)
+    deq = torch.from_numpy(quant_ref.dequantize(fmt, quant_ref.quantize(fmt, w.float().numpy())))
+    return [DenseLinear(t.contiguous(), fmt) for t in deq.split([x.shape[0] for x in ws])]
+
+
 def make_layer(d: Dims, weights: dict, i: int, fmt: str = "bf16") -> dict:
     p = f"layers.{i}."
+    if fmt != "bf16":
+        q, k, v = _fused_quant([weights[p + "self_attn.q_proj.weight"], weights[p + "self_attn.k_proj.weight"],
+                                weights[p + "self_attn.v_proj.weight"]], fmt)
+        gate, up = _fused_quant([weights[p + "mlp.gate_proj.weight"], weights[p + "mlp.up_proj.weight"]], fmt)
+        return dict(
+            in_norm=weights[p + "input_layernorm.weight"],
+            post_norm=weights[p + "post_attention_layernorm.weight"],
+            q=q, k=k, v=v, o=Linear(weights[p + "self_attn.o_proj.weight"], fmt),
+            gate=gate, up=up, down=Linear(weights[p + "mlp.down_proj.weight"], fmt),
+        )
     return dict(
         in_norm=weights[p + "input_layernorm.weight"],
         post_norm=weights[p + "post_attention_layernorm.weight"],

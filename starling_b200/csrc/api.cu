@@ -1,0 +1,322 @@
+// C ABI of libstarling_b200 (declared in include/starling_b200.h) and the
+// host-side sequencing of one decode / verify forward.
+//
+// sb_decode_step issues, per layer, five launches on the caller's stream:
+//   1. q/k/v dequant-GEMV   RMSNorm prologue (layer 0: embedding x12 + RMSNorm),
+//                           RoPE + KV-cache write epilogue
+//   2. attention            cluster split over the context
+//   3. o dequant-GEMV       residual epilogue into the hidden rows
+//   4. gate/up GEMV         RMSNorm prologue, SiLU*up epilogue
+//   5. down GEMV            residual epilogue
+// and finally the lm_head GEMV with the final RMSNorm prologue and the fused
+// argmax / token feedback epilogue.  Every dynamic value (token ids, cache
+// slot, finished flags) is read from device memory, so the launches can be
+// captured once into a CUDA graph and replayed.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "attention.cuh"
+#include "gemv.cuh"
+#include "glue.cuh"
+
+using namespace sb;
+
+static thread_local char g_err[1024] = "";
+
+static int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+#define SB_TRY(expr)                                                                                   \
+  do {                                                                                                 \
+    int _rc = (expr);                                                                                  \
+    if (_rc != 0) {                                                                                    \
+      if (_rc < 1000) return fail(_rc, "%s: %s", #expr, cudaGetErrorString(static_cast<cudaError_t>(_rc))); \
+      return _rc;                                                                                      \
+    }                                                                                                  \
+  } while (0)
+
+static bool lin_ok(const SbLinear& l) {
+  if (!l.w || l.n <= 0 || l.k <= 0 || l.n_pad < l.n || (l.n_pad % 16) != 0) return false;
+  if (l.fmt < SB_FMT_BF16 || l.fmt > SB_FMT_NVFP4) return false;
+  if (l.k % kgroup_elems(l.fmt) != 0 || l.k % 64 != 0) return false;
+  if (l.fmt != SB_FMT_BF16 && !l.scale) return false;
+  return true;
+}
+
+static GemvParams base_params(const SbLinear& l, int m) {
+  GemvParams p;
+  memset(&p, 0, sizeof(p));
+  p.w = static_cast<const uint8_t*>(l.w);
+  p.scale = static_cast<const uint8_t*>(l.scale);
+  p.gscale = l.global_scale;
+  p.n = l.n;
+  p.k = l.k;
+  p.n_tiles = l.n_pad / 16;
+  p.kg_total = l.k / kgroup_elems(l.fmt);
+  p.m = m;
+  return p;
+}
+
+static int run_gemv(GemvParams& p, int fmt, bool pdl, cudaStream_t s) {
+  const GemvCfg c = gemv_pick(fmt, p.n_tiles * 16, p.k, p.m < 64 ? p.m : 64);
+  p.rt = c.rt;
+  p.ck = c.ck;
+  if (p.k % (c.ck * kgroup_elems(fmt)) != 0) return fail(SB_ERR_CONFIG, "k=%d not divisible for ck=%d", p.k, c.ck);
+  const int rc = gemv_launch(p, c, fmt, pdl, s);
+  if (rc == SB_ERR_CONFIG)
+    return fail(rc, "no gemv configuration for n=%d k=%d m=%d (smem %zu)", p.n, p.k, p.m, gemv_smem_bytes(c, p.k, p.m < 64 ? p.m : 64));
+  if (rc != 0) return fail(rc, "gemv launch (n=%d k=%d m=%d): %s", p.n, p.k, p.m, cudaGetErrorString((cudaError_t)rc));
+  return 0;
+}
+
+static int attn_split(int max_len) {
+  int s = (max_len + 63) / 64;
+  return s < 1 ? 1 : (s > 8 ? 8 : s);
+}
+
+static int check_state(const SbModel* md, const SbState* st) {
+  if (!md || !st) return fail(SB_ERR_ARG, "null model/state");
+  if (st->batch < 1 || st->m < 1 || st->batch * st->m > 64)
+    return fail(SB_ERR_ARG, "batch*m must be in [1, 64] (batch=%d m=%d)", st->batch, st->m);
+  if (st->batch > md->max_batch) return fail(SB_ERR_ARG, "batch %d > model max_batch %d", st->batch, md->max_batch);
+  if (md->head_dim != 128) return fail(SB_ERR_ARG, "head_dim must be 128");
+  if (md->n_q % md->n_kv != 0 || (md->n_q / md->n_kv) * st->m > 128)
+    return fail(SB_ERR_ARG, "query rows per KV head (n_q/n_kv * m) must be <= 128");
+  if (!st->ids || !st->ctrl || !st->hidden || !st->q || !st->attn || !st->act || !st->workspace)
+    return fail(SB_ERR_ARG, "state buffer missing");
+  if (st->mode < SB_MODE_DECODE || st->mode > SB_MODE_FIRST) return fail(SB_ERR_ARG, "bad mode");
+  return 0;
+}
+
+struct LmWork {
+  float* val;
+  int* idx;
+  int* counter;
+  int n_ctas;
+  size_t bytes;
+};
+
+static LmWork lm_work(const SbModel* md, int tokens, void* base) {
+  const SbLinear& l = md->lm_head;
+  const GemvCfg c = gemv_pick(l.fmt, l.n_pad, l.k, tokens);
+  LmWork w;
+  w.n_ctas = gemv_grid(c, l.n_pad / 16) / c.ck;
+  const size_t pv = static_cast<size_t>(w.n_ctas) * tokens * 4;
+  char* b = static_cast<char*>(base);
+  w.counter = reinterpret_cast<int*>(b);
+  w.val = reinterpret_cast<float*>(b + 256);
+  w.idx = reinterpret_cast<int*>(b + 256 + ((pv + 255) & ~size_t(255)));
+  w.bytes = 256 + 2 * ((pv + 255) & ~size_t(255));
+  return w;
+}
+
+static int launch_lm_head(const SbModel* md, const SbState* st, int step, cudaStream_t s) {
+  const int T = st->batch * st->m;
+  LmWork w = lm_work(md, T, st->workspace);
+  if (w.bytes > st->workspace_bytes) return fail(SB_ERR_ARG, "workspace too small (%zu < %zu)", st->workspace_bytes, w.bytes);
+  GemvParams p = base_params(md->lm_head, T);
+  p.pro = PRO_RMSNORM;
+  p.x = st->hidden;
+  p.norm_w = md->final_norm;
+  p.eps = md->eps;
+  p.epi = EPI_ARGMAX;
+  p.logits = st->logits;
+  p.logits_mult = md->logits_mult;
+  p.part_val = w.val;
+  p.part_idx = w.idx;
+  p.counter = w.counter;
+  p.n_ctas = w.n_ctas;
+  p.mode = st->mode;
+  p.batch = st->batch;
+  p.step = step;
+  p.ids_io = st->ids;
+  p.out_ids = st->out_ids;
+  p.finished = st->finished;
+  p.eos_id = st->eos_id;
+  p.pad_id = st->pad_id;
+  p.ctrl = st->ctrl;
+  return run_gemv(p, md->lm_head.fmt, st->use_pdl != 0, s);
+}
+
+static int launch_attention(const SbModel* md, const SbState* st, int l, cudaStream_t s) {
+  const SbLayer& L = md->layers[l];
+  AttnParams a;
+  memset(&a, 0, sizeof(a));
+  a.q = st->q;
+  a.k_cache = L.k_cache;
+  a.v_cache = L.v_cache;
+  a.out = st->attn;
+  a.n_q = md->n_q;
+  a.n_kv = md->n_kv;
+  a.max_len = md->max_len;
+  a.m_per = st->m;
+  a.attn_mult = md->attn_mult;
+  a.ctrl = st->ctrl;
+  a.prompt_len = st->prompt_len;
+  a.split = attn_split(md->max_len);
+  a.chunk_cap = (md->max_len + a.split - 1) / a.split;
+  const int rc = attn_launch(a, st->batch, st->use_pdl != 0, s);
+  if (rc == SB_ERR_CONFIG) return fail(rc, "no attention configuration (rows=%d)", (md->n_q / md->n_kv) * st->m);
+  if (rc != 0) return fail(rc, "attention launch: %s", cudaGetErrorString((cudaError_t)rc));
+  return 0;
+}
+
+// One kernel of the step: op = SB_OP_* for layer l.
+static int launch_op(const SbModel* md, const SbState* st, int l, int op, int step, cudaStream_t s) {
+  const int T = st->batch * st->m;
+  const bool pdl = st->use_pdl != 0;
+  if (op == SB_OP_LM_HEAD) {
+    if (!lin_ok(md->lm_head)) return fail(SB_ERR_ARG, "bad lm_head");
+    return launch_lm_head(md, st, step, s);
+  }
+  if (op == SB_OP_ATTN) return launch_attention(md, st, l, s);
+  const SbLayer& L = md->layers[l];
+  if (!lin_ok(L.qkv) || !lin_ok(L.o) || !lin_ok(L.gate_up) || !lin_ok(L.down))
+    return fail(SB_ERR_ARG, "layer %d: bad packed linear", l);
+  if (op == SB_OP_QKV) {  // RMSNorm (layer 0: embedding x12) -> q/k/v -> RoPE + cache write
+    GemvParams p = base_params(L.qkv, T);
+    p.pro = l == 0 ? PRO_EMBED : PRO_RMSNORM;
+    p.x = st->hidden;
+    p.norm_w = L.in_norm;
+    p.eps = md->eps;
+    p.ids = st->ids;
+    p.embed = md->embed;
+    p.embed_rows = md->vocab;
+    p.emb_mult = md->emb_mult;
+    p.hidden_out = st->hidden;
+    p.epi = EPI_QKV;
+    p.q_out = st->q;
+    p.k_cache = L.k_cache;
+    p.v_cache = L.v_cache;
+    p.n_q = md->n_q;
+    p.n_kv = md->n_kv;
+    p.max_len = md->max_len;
+    p.m_per = st->m;
+    p.cos_tab = md->rope_cos;
+    p.sin_tab = md->rope_sin;
+    p.rope_max = md->rope_max_pos;
+    p.rope_off = st->rope_off;
+    p.ctrl = st->ctrl;
+    return run_gemv(p, L.qkv.fmt, pdl, s);
+  }
+  if (op == SB_OP_O || op == SB_OP_DOWN) {  // o / down -> residual scale-add into hidden
+    const SbLinear& lin = op == SB_OP_O ? L.o : L.down;
+    GemvParams p = base_params(lin, T);
+    p.pro = PRO_NONE;
+    p.x = op == SB_OP_O ? st->attn : st->act;
+    p.epi = EPI_RESID;
+    p.y = st->hidden;
+    p.res_mult = md->res_mult;
+    return run_gemv(p, lin.fmt, pdl, s);
+  }
+  // gate/up: RMSNorm -> interleaved gate|up -> SiLU(gate)*up
+  GemvParams p = base_params(L.gate_up, T);
+  p.pro = PRO_RMSNORM;
+  p.x = st->hidden;
+  p.norm_w = L.post_norm;
+  p.eps = md->eps;
+  p.epi = EPI_SWIGLU;
+  p.y = st->act;
+  return run_gemv(p, L.gate_up.fmt, pdl, s);
+}
+
+extern "C" {
+
+const char* sb_last_error(void) { return g_err; }
+int sb_version(void) { return 1; }
+
+size_t sb_workspace_bytes(const SbModel* md, int32_t tokens) {
+  if (!md || tokens < 1) return 0;
+  return lm_work(md, tokens, nullptr).bytes;
+}
+
+int sb_decode_step(const SbModel* md, const SbState* st, int32_t step, sb_stream_t stream) {
+  SB_TRY(check_state(md, st));
+  if (!md->layers || md->n_layers < 1) return fail(SB_ERR_ARG, "no layers");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  for (int l = 0; l < md->n_layers; ++l)
+    for (int op = SB_OP_QKV; op <= SB_OP_DOWN; ++op) SB_TRY(launch_op(md, st, l, op, step, s));
+  return launch_op(md, st, 0, SB_OP_LM_HEAD, step, s);
+}
+
+int sb_decode_op(const SbModel* md, const SbState* st, int32_t layer, int32_t op, int32_t step, sb_stream_t stream) {
+  SB_TRY(check_state(md, st));
+  if (!md->layers || layer < 0 || layer >= md->n_layers) return fail(SB_ERR_ARG, "bad layer %d", layer);
+  if (op < SB_OP_QKV || op > SB_OP_LM_HEAD) return fail(SB_ERR_ARG, "bad op %d", op);
+  return launch_op(md, st, layer, op, step, static_cast<cudaStream_t>(stream));
+}
+
+int sb_lm_head_argmax(const SbModel* md, const SbState* st, int32_t step, sb_stream_t stream) {
+  SB_TRY(check_state(md, st));
+  return launch_op(md, st, 0, SB_OP_LM_HEAD, step, static_cast<cudaStream_t>(stream));
+}
+
+int sb_linear(const SbLinear* lin, const uint16_t* x, uint16_t* y, int32_t m, int32_t use_pdl, sb_stream_t stream) {
+  if (!lin || !lin_ok(*lin) || !x || !y) return fail(SB_ERR_ARG, "sb_linear: bad arguments");
+  if (m < 1) return fail(SB_ERR_ARG, "sb_linear: m must be >= 1");
+  GemvParams p = base_params(*lin, m);
+  p.pro = PRO_NONE;
+  p.x = x;
+  p.epi = EPI_STORE;
+  p.y = y;
+  return run_gemv(p, lin->fmt, use_pdl != 0, static_cast<cudaStream_t>(stream));
+}
+
+int sb_dequant_f32(const SbLinear* lin, float* out, sb_stream_t stream) {
+  if (!lin || !lin_ok(*lin) || !out) return fail(SB_ERR_ARG, "sb_dequant_f32: bad arguments");
+  SB_TRY(dequant_launch(*lin, out, true, static_cast<cudaStream_t>(stream)));
+  return 0;
+}
+
+int sb_dequant_bf16(const SbLinear* lin, uint16_t* out, sb_stream_t stream) {
+  if (!lin || !lin_ok(*lin) || !out) return fail(SB_ERR_ARG, "sb_dequant_bf16: bad arguments");
+  SB_TRY(dequant_launch(*lin, out, false, static_cast<cudaStream_t>(stream)));
+  return 0;
+}
+
+int sb_rmsnorm(const uint16_t* x, const uint16_t* w, uint16_t* y, int32_t rows, int32_t n, float eps, sb_stream_t s) {
+  if (!x || !w || !y || rows < 1 || n < 1) return fail(SB_ERR_ARG, "sb_rmsnorm: bad arguments");
+  SB_TRY(rmsnorm_launch(x, w, y, rows, n, eps, static_cast<cudaStream_t>(s)));
+  return 0;
+}
+
+int sb_silu_mul(const uint16_t* g, const uint16_t* u, uint16_t* o, int64_t count, sb_stream_t s) {
+  if (!g || !u || !o || count < 0) return fail(SB_ERR_ARG, "sb_silu_mul: bad arguments");
+  if (count == 0) return 0;
+  SB_TRY(silu_mul_launch(g, u, o, count, static_cast<cudaStream_t>(s)));
+  return 0;
+}
+
+int sb_residual_scale(const uint16_t* x, const uint16_t* y, uint16_t* z, int64_t count, float alpha, sb_stream_t s) {
+  if (!x || !y || !z || count < 0) return fail(SB_ERR_ARG, "sb_residual_scale: bad arguments");
+  if (count == 0) return 0;
+  SB_TRY(residual_launch(x, y, z, count, alpha, static_cast<cudaStream_t>(s)));
+  return 0;
+}
+
+int sb_rope(uint16_t* x, int32_t rows, int32_t heads, const int32_t* pos, const uint16_t* cs, const uint16_t* sn,
+            sb_stream_t s) {
+  if (!x || !pos || !cs || !sn || rows < 1 || heads < 1) return fail(SB_ERR_ARG, "sb_rope: bad arguments");
+  SB_TRY(rope_launch(x, rows, heads, pos, cs, sn, static_cast<cudaStream_t>(s)));
+  return 0;
+}
+
+int sb_argmax_bf16(const uint16_t* x, int32_t rows, int32_t n, int64_t* out, sb_stream_t s) {
+  if (!x || !out || rows < 1 || n < 1) return fail(SB_ERR_ARG, "sb_argmax_bf16: bad arguments");
+  SB_TRY(argmax_launch(x, rows, n, out, static_cast<cudaStream_t>(s)));
+  return 0;
+}
+
+int sb_attention(const SbModel* md, const SbState* st, int32_t layer, sb_stream_t stream) {
+  SB_TRY(check_state(md, st));
+  if (layer < 0 || layer >= md->n_layers) return fail(SB_ERR_ARG, "bad layer");
+  return launch_attention(md, st, layer, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

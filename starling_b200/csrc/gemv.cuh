@@ -1,0 +1,75 @@
+// Dequant-GEMV ("skinny GEMM", m <= 64 token rows) with fused prologue and
+// epilogue.  See gemv.cu for the kernel and the design notes.
+#pragma once
+#include "common.cuh"
+
+namespace sb {
+
+enum { PRO_NONE = 0, PRO_RMSNORM = 1, PRO_EMBED = 2 };
+enum { EPI_STORE = 0, EPI_QKV = 1, EPI_RESID = 2, EPI_SWIGLU = 3, EPI_ARGMAX = 4 };
+
+struct GemvParams {
+  // packed weight
+  const uint8_t* w;
+  const uint8_t* scale;
+  float gscale;
+  int n;         // logical rows
+  int k;
+  int n_tiles;   // n_pad / 16
+  int kg_total;  // k / kgroup elements
+  // launch configuration
+  int rt;  // row tiles per CTA (cluster)
+  int ck;  // CTAs per cluster splitting K
+  int m;   // token rows (<= 64)
+  // prologue
+  int pro;
+  const uint16_t* x;       // [m][k] input rows (PRO_NONE / PRO_RMSNORM)
+  const uint16_t* norm_w;  // [k] RMSNorm weight
+  float eps;
+  const int64_t* ids;      // PRO_EMBED: token id per row
+  const uint16_t* embed;   // PRO_EMBED: [vocab][k]
+  int embed_rows;          // PRO_EMBED: vocab (ids are clamped into range)
+  float emb_mult;
+  uint16_t* hidden_out;    // PRO_EMBED: the embedded rows are written here
+  // epilogue
+  int epi;
+  uint16_t* y;  // STORE [m][n]; RESID hidden [m][n] (in place); SWIGLU act [m][n/2]
+  float res_mult;
+  // EPI_QKV
+  uint16_t* q_out;
+  uint16_t* k_cache;
+  uint16_t* v_cache;
+  int n_q, n_kv, max_len, m_per;  // m_per = tokens per stream
+  const uint16_t* cos_tab;
+  const uint16_t* sin_tab;
+  int rope_max;
+  const int32_t* rope_off;
+  int32_t* ctrl;
+  // EPI_ARGMAX
+  uint16_t* logits;
+  float logits_mult;
+  float* part_val;
+  int* part_idx;
+  int* counter;
+  int n_ctas;  // CTAs that produce argmax partials (= grid when ck == 1)
+  int mode;
+  int batch;
+  int step;
+  int64_t* ids_io;
+  int64_t* out_ids;
+  int32_t* finished;
+  int64_t eos_id;
+  int64_t pad_id;
+};
+
+struct GemvCfg {
+  int rt, ck, warps, nt;
+};
+
+int kgroup_elems(int fmt);
+GemvCfg gemv_pick(int fmt, int n_pad, int k, int m);
+size_t gemv_smem_bytes(const GemvCfg& c, int k, int m);
+int gemv_grid(const GemvCfg& c, int n_tiles);
+int gemv_launch(const GemvParams& p, const GemvCfg& c, int fmt, bool pdl, cudaStream_t stream);
+
+}  // namespace sb

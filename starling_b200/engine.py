@@ -1,0 +1,309 @@
+"""GraniteEngine: packed weights, static KV cache and device state for the
+native decode path, plus the (torch) prefill that fills the cache.
+
+The decode / verify forward itself is one C-ABI call per step
+(``sb_decode_step``) issuing the fused sm_100a kernels; everything it reads
+(token ids, cache slot, finished flags) lives in device tensors owned here, so
+a CUDA graph captured once is replayed for every chunk.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass, fields
+from typing import Optional
+
+import torch
+import torch.nn.functional as F
+
+from . import _lib
+from ._lib import SB_CTRL_PADLEN, SB_CTRL_SLOT, SB_CTRL_WORDS, SbLayer, SbModel, SbState, check, ptr
+from .config import LLM_EOS_TOKEN_ID, LLM_PAD_TOKEN_ID
+from .pack import PackedLinear, pack_gate_up, pack_matrix, pack_qkv
+from .rope import rope_tables
+
+BF16 = torch.bfloat16
+
+
+@dataclass(frozen=True)
+class GraniteDims:
+    hidden: int = 2048
+    n_q: int = 16
+    n_kv: int = 4
+    head_dim: int = 128
+    inter: int = 8192
+    vocab: int = 100352
+    layers: int = 40
+    eps: float = 1e-5
+    theta: float = 10000.0
+    attn_mult: float = 0.0078125
+    emb_mult: float = 12.0
+    res_mult: float = 0.22
+    logits_scaling: float = 8.0
+
+    @classmethod
+    def from_hf_config(cls, cfg) -> "GraniteDims":
+        rp = getattr(cfg, "rope_parameters", None) or {}
+        theta = rp.get("rope_theta", getattr(cfg, "rope_theta", 10000.0))
+        return cls(
+            hidden=cfg.hidden_size, n_q=cfg.num_attention_heads, n_kv=cfg.num_key_value_heads,
+            head_dim=getattr(cfg, "head_dim", None) or cfg.hidden_size // cfg.num_attention_heads,
+            inter=cfg.intermediate_size, vocab=cfg.vocab_size, layers=cfg.num_hidden_layers,
+            eps=cfg.rms_norm_eps, theta=float(theta), attn_mult=cfg.attention_multiplier,
+            emb_mult=cfg.embedding_multiplier, res_mult=cfg.residual_multiplier,
+            logits_scaling=cfg.logits_scaling,
+        )
+
+    @classmethod
+    def coerce(cls, d) -> "GraniteDims":
+        if isinstance(d, cls):
+            return d
+        names = {f.name for f in fields(cls)}
+        src = d if isinstance(d, dict) else d.__dict__
+        return cls(**{k: v for k, v in src.items() if k in names})
+
+
+def weights_from_hf(language_model, lm_head=None) -> dict:
+    """HF GraniteModel (+ lm_head) -> {HF parameter name: tensor}."""
+    w = {k: v for k, v in language_model.state_dict().items() if "rotary" not in k}
+    if lm_head is not None and lm_head.weight.data_ptr() != w["embed_tokens.weight"].data_ptr():
+        w["lm_head.weight"] = lm_head.weight
+    return w
+
+
+class EngineState:
+    """Device buffers and the C ``SbState`` for one forward shape (batch, m)."""
+
+    def __init__(self, eng: "GraniteEngine", batch: int, m: int, mode: int, out_steps: int = 1,
+                 finished: bool = False, prompt_len: Optional[torch.Tensor] = None,
+                 rope_off: Optional[torch.Tensor] = None, keep_logits: bool = True,
+                 use_pdl: bool = True):
+        d, dev = eng.dims, eng.device
+        T = batch * m
+        self.batch, self.m = batch, m
+        self.ids = torch.zeros(T, dtype=torch.int64, device=dev)
+        self.ctrl = torch.zeros(SB_CTRL_WORDS, dtype=torch.int32, device=dev)
+        self.prompt_len = None if prompt_len is None else prompt_len.to(dev, torch.int32).contiguous()
+        self.rope_off = None if rope_off is None else rope_off.to(dev, torch.int32).contiguous()
+        self.finished = torch.zeros(batch, dtype=torch.int32, device=dev) if finished else None
+        self.out_ids = torch.zeros(max(out_steps, 1) * max(batch, m), dtype=torch.int64, device=dev)
+        self.hidden = torch.zeros(T, d.hidden, dtype=BF16, device=dev)
+        self.q = torch.zeros(T, d.n_q * d.head_dim, dtype=BF16, device=dev)
+        self.attn = torch.zeros(T, d.n_q * d.head_dim, dtype=BF16, device=dev)
+        self.act = torch.zeros(T, d.inter, dtype=BF16, device=dev)
+        self.logits = torch.zeros(T, d.vocab, dtype=BF16, device=dev) if keep_logits else None
+        nbytes = eng.lib.sb_workspace_bytes(C.byref(eng.cmodel), T)
+        self.workspace = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=dev)
+        s = SbState()
+        s.batch, s.m, s.mode, s.use_pdl = batch, m, mode, int(use_pdl)
+        s.eos_id, s.pad_id = LLM_EOS_TOKEN_ID, LLM_PAD_TOKEN_ID
+        s.ids, s.ctrl = ptr(self.ids), ptr(self.ctrl)
+        s.prompt_len, s.rope_off, s.finished = ptr(self.prompt_len), ptr(self.rope_off), ptr(self.finished)
+        s.out_ids, s.hidden, s.q, s.attn, s.act = (ptr(self.out_ids), ptr(self.hidden), ptr(self.q),
+                                                   ptr(self.attn), ptr(self.act))
+        s.logits = ptr(self.logits)
+        s.workspace, s.workspace_bytes = ptr(self.workspace), self.workspace.numel()
+        self.c = s
+
+    def set_mode(self, mode: int) -> None:
+        self.c.mode = mode
+
+    def set_slot(self, slot: int, pad_len: Optional[int] = None) -> None:
+        self.ctrl[SB_CTRL_SLOT] = int(slot)
+        if pad_len is not None:
+            self.ctrl[SB_CTRL_PADLEN] = int(pad_len)
+
+
+class GraniteEngine:
+    def __init__(self, dims, weights: dict, fmt: str = "bf16", max_cache_len: int = 640,
+                 max_batch: int = 1, device="cuda", rope_max_pos: Optional[int] = None):
+        self.lib = _lib.load()
+        self.dims = d = GraniteDims.coerce(dims)
+        if d.head_dim != 128:
+            raise ValueError("the native kernels use head_dim 128")
+        self.fmt = fmt
+        self.device = torch.device(device)
+        self.max_cache_len = int(max_cache_len)
+        self.max_batch = int(max_batch)
+        dev = self.device
+
+        def W(name):
+            return weights[name].detach().to(dev, BF16)
+
+        self.embed = W("embed_tokens.weight").contiguous()
+        self.final_norm = W("norm.weight").contiguous()
+        head_w = weights.get("lm_head.weight", None)
+        self.lm_head = pack_matrix(self.embed if head_w is None else W("lm_head.weight"), fmt)
+        self.layers = []
+        for i in range(d.layers):
+            p = f"layers.{i}."
+            L = dict(
+                in_norm=W(p + "input_layernorm.weight").contiguous(),
+                post_norm=W(p + "post_attention_layernorm.weight").contiguous(),
+                qkv=pack_qkv(W(p + "self_attn.q_proj.weight"), W(p + "self_attn.k_proj.weight"),
+                             W(p + "self_attn.v_proj.weight"), d.n_q, d.n_kv, fmt),
+                o=pack_matrix(W(p + "self_attn.o_proj.weight"), fmt),
+                gate_up=pack_gate_up(W(p + "mlp.gate_proj.weight"), W(p + "mlp.up_proj.weight"), fmt),
+                down=pack_matrix(W(p + "mlp.down_proj.weight"), fmt),
+            )
+            self.layers.append(L)
+        # static KV cache: [layer][k|v][batch][n_kv][max_len][128] (StaticLayer layout per layer)
+        self.kv = torch.zeros(d.layers, 2, max_batch, d.n_kv, self.max_cache_len, d.head_dim, dtype=BF16, device=dev)
+        self.rope_max_pos = int(rope_max_pos or max(4096, self.max_cache_len))
+        cs, sn = rope_tables(d.head_dim, d.theta, self.rope_max_pos)
+        self.rope_cos, self.rope_sin = cs.to(dev), sn.to(dev)
+        self._build_c()
+
+    # ------------------------------------------------------------------ #
+    def _build_c(self) -> None:
+        d = self.dims
+        arr = (SbLayer * d.layers)()
+        for i, L in enumerate(self.layers):
+            arr[i].in_norm = ptr(L["in_norm"])
+            arr[i].post_norm = ptr(L["post_norm"])
+            arr[i].qkv = L["qkv"].c_struct()
+            arr[i].o = L["o"].c_struct()
+            arr[i].gate_up = L["gate_up"].c_struct()
+            arr[i].down = L["down"].c_struct()
+            arr[i].k_cache = ptr(self.kv[i, 0])
+            arr[i].v_cache = ptr(self.kv[i, 1])
+        m = SbModel()
+        m.hidden, m.n_q, m.n_kv, m.head_dim = d.hidden, d.n_q, d.n_kv, d.head_dim
+        m.inter, m.vocab, m.n_layers = d.inter, d.vocab, d.layers
+        m.max_len, m.max_batch, m.rope_max_pos = self.max_cache_len, self.max_batch, self.rope_max_pos
+        m.eps, m.attn_mult, m.emb_mult, m.res_mult = d.eps, d.attn_mult, d.emb_mult, d.res_mult
+        m.logits_mult = 1.0 / d.logits_scaling
+        m.embed, m.final_norm = ptr(self.embed), ptr(self.final_norm)
+        m.rope_cos, m.rope_sin = ptr(self.rope_cos), ptr(self.rope_sin)
+        m.lm_head = self.lm_head.c_struct()
+        m.layers = C.cast(arr, C.POINTER(SbLayer))
+        self._layer_arr = arr
+        self.cmodel = m
+
+    @property
+    def weight_bytes(self) -> int:
+        n = self.lm_head.nbytes
+        for L in self.layers:
+            n += sum(L[k].nbytes for k in ("qkv", "o", "gate_up", "down"))
+        return n
+
+    def new_state(self, batch: int = 1, m: int = 1, mode: int = _lib.SB_MODE_DECODE, **kw) -> EngineState:
+        if batch > self.max_batch:
+            raise ValueError(f"batch {batch} > engine max_batch {self.max_batch}")
+        return EngineState(self, batch, m, mode, **kw)
+
+    # ---- native calls ----------------------------------------------------- #
+    def decode_step(self, st: EngineState, step: int = 0) -> None:
+        if not 0 <= step < st.out_ids.numel() // max(st.batch, st.m):
+            raise ValueError(f"step {step} outside the state's output ring")
+        check(self.lib.sb_decode_step(C.byref(self.cmodel), C.byref(st.c), int(step), _lib.current_stream()),
+              "sb_decode_step")
+
+    def lm_head_argmax(self, st: EngineState, step: int = 0) -> None:
+        check(self.lib.sb_lm_head_argmax(C.byref(self.cmodel), C.byref(st.c), int(step), _lib.current_stream()),
+              "sb_lm_head_argmax")
+
+    def dequant(self, p: PackedLinear, f32: bool = True) -> torch.Tensor:
+        """Packed -> dense weight in LOGICAL row order (fp32 exact, or bf16)."""
+        out = torch.empty(p.n, p.k, dtype=torch.float32 if f32 else BF16, device=self.device)
+        fn = self.lib.sb_dequant_f32 if f32 else self.lib.sb_dequant_bf16
+        c = p.c_struct()
+        check(fn(C.byref(c), ptr(out), _lib.current_stream()), "sb_dequant")
+        if p.row_perm is not None:
+            out = out[self._inverse_perm(p)]
+        return out
+
+    # ---- prefill (torch on the GPU, the reference's eager semantics) -------- #
+    def linear(self, x: torch.Tensor, p: PackedLinear) -> torch.Tensor:
+        """y = x W^T through the native dequant-GEMV (any number of rows; fp32
+        accumulation over the exactly dequantised weight).  Output columns in
+        LOGICAL row order."""
+        shp = x.shape
+        x2 = x.reshape(-1, shp[-1]).to(BF16).contiguous()
+        y = torch.empty(x2.shape[0], p.n, dtype=BF16, device=self.device)
+        c = p.c_struct()
+        check(self.lib.sb_linear(C.byref(c), ptr(x2), ptr(y), x2.shape[0], 0, _lib.current_stream()), "sb_linear")
+        if p.row_perm is not None:
+            y = y[:, self._inverse_perm(p)]
+        return y.view(*shp[:-1], p.n)
+
+    def _inverse_perm(self, p: PackedLinear) -> torch.Tensor:
+        inv = getattr(p, "_inv", None)
+        if inv is None:
+            inv = torch.empty_like(p.row_perm)
+            inv[p.row_perm] = torch.arange(p.row_perm.numel(), device=p.row_perm.device)
+            p._inv = inv = inv.to(self.device)
+        return inv
+
+    @torch.inference_mode()
+    def prefill(self, inputs_embeds: torch.Tensor, prompt_lengths: Optional[torch.Tensor] = None,
+                chunk_streams: int = 8) -> torch.Tensor:
+        """Eager prefill over ``inputs_embeds`` (B, T, H) (before the x12
+        embedding multiplier), writing cache slots [0, T) of streams 0..B-1.
+        Mirrors ``GraniteModel.forward`` with a causal (+ right-padding) mask
+        (llm_mega.py:176-202, batched.py:222-276).  Returns the last real
+        position's hidden row per stream, before the final norm: (B, H)."""
+        d = self.dims
+        B, T, _ = inputs_embeds.shape
+        if T >= self.max_cache_len:
+            raise ValueError(f"prompt {T} >= max_cache_len {self.max_cache_len}")
+        dev = self.device
+        hidden = inputs_embeds.to(dev, BF16) * d.emb_mult
+        pl = None if prompt_lengths is None else prompt_lengths.to(dev).long()
+        cos = self.rope_cos[:T].repeat(1, 2)[None, None]  # (1,1,T,128)
+        sin = self.rope_sin[:T].repeat(1, 2)[None, None]
+        kpos = torch.arange(T, device=dev)
+        valid = kpos[None, :] <= kpos[:, None]  # (T q, T k)
+        valid = valid[None].expand(B, T, T)
+        if pl is not None:
+            valid = valid & (kpos[None, None, :] < pl[:, None, None])
+        neg = torch.finfo(BF16).min
+        mask = torch.zeros(B, 1, T, T, dtype=BF16, device=dev).masked_fill_(~valid[:, None], neg)
+        G = d.n_q // d.n_kv
+        half = d.head_dim // 2
+
+        def rot(x):
+            return torch.cat((-x[..., half:], x[..., :half]), dim=-1)
+
+        for li, L in enumerate(self.layers):
+            residual = hidden
+            xf = hidden.float()
+            normed = L["in_norm"] * (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + d.eps)).to(BF16)
+            qkv = self.linear(normed, L["qkv"])
+            q, k, v = qkv.split([d.n_q * 128, d.n_kv * 128, d.n_kv * 128], dim=-1)
+            q = q.reshape(B, T, d.n_q, 128).transpose(1, 2)
+            k = k.reshape(B, T, d.n_kv, 128).transpose(1, 2)
+            v = v.reshape(B, T, d.n_kv, 128).transpose(1, 2)
+            q = q * cos + rot(q) * sin
+            k = k * cos + rot(k) * sin
+            self.kv[li, 0, :B, :, :T] = k
+            self.kv[li, 1, :B, :, :T] = v
+            outs = []
+            for b0 in range(0, B, chunk_streams):
+                b1 = min(B, b0 + chunk_streams)
+                kr = k[b0:b1].repeat_interleave(G, dim=1)
+                vr = v[b0:b1].repeat_interleave(G, dim=1)
+                sc = torch.matmul(q[b0:b1], kr.transpose(2, 3)) * d.attn_mult + mask[b0:b1]
+                pr = F.softmax(sc, dim=-1, dtype=torch.float32).to(BF16)
+                outs.append(torch.matmul(pr, vr))
+            ao = torch.cat(outs).transpose(1, 2).reshape(B, T, d.n_q * 128)
+            hidden = residual + self.linear(ao, L["o"]) * d.res_mult
+            residual = hidden
+            xf = hidden.float()
+            normed = L["post_norm"] * (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + d.eps)).to(BF16)
+            gu = self.linear(normed, L["gate_up"])
+            act = F.silu(gu[..., : d.inter]) * gu[..., d.inter:]
+            hidden = residual + self.linear(act, L["down"]) * d.res_mult
+        if pl is None:
+            return hidden[:, -1, :].contiguous()
+        return hidden[torch.arange(B, device=dev), pl - 1, :].contiguous()
+
+    def load_cache_from(self, k_list, v_list, batch_index: int = 0) -> None:
+        """Copy externally computed K/V (per layer (n_kv, S, 128) or (B, n_kv, S, 128)) into slots [0, S)."""
+        for li, (k, v) in enumerate(zip(k_list, v_list)):
+            if k.dim() == 3:
+                k, v = k[None], v[None]
+            S = k.shape[2]
+            b1 = batch_index + k.shape[0]
+            self.kv[li, 0, batch_index:b1, :, :S] = k.to(self.device, BF16)
+            self.kv[li, 1, batch_index:b1, :, :S] = v.to(self.device, BF16)

@@ -1,0 +1,146 @@
+"""Packing of linear layers into the tensor-core fragment layout the
+dequant-GEMV streams (see include/starling_b200.h, ``SbLinear``).
+
+Logical weight ``W[N, K]`` (row = output feature).  Rows are padded to a
+multiple of 16; row tile ``t`` covers rows ``16t..16t+15``.  K is cut into
+kgroups of 16 bytes per lane (64 nvfp4, 32 fp8/int8, 16 bf16 elements).  For
+kgroup ``kg``, k-step ``ks`` (16 K-elements) and lane ``(g, c) = (lane//4,
+lane%4)`` the lane holds the eight ``mma.m16n8k16`` A-fragment elements
+
+    e0,e1 = (g,   2c..2c+1)   e2,e3 = (g+8, 2c..2c+1)
+    e4,e5 = (g,   2c+8..2c+9) e6,e7 = (g+8, 2c+8..2c+9)
+
+in that order (two e2m1 codes per byte, low nibble first).  nvfp4 block
+scales are stored per (tile, kgroup) as 8 lanes-groups x 8 bytes
+``[s(g,ks0), s(g+8,ks0), s(g,ks1), ...]``.
+
+Fused matrices: ``qkv`` = rows ``[q | k | v]`` where inside every q and k
+head the RoPE halves are interleaved (packed row ``2j`` = dim ``j``, ``2j+1`` =
+dim ``j+64``) so that the GEMV epilogue holds both operands of each RoPE pair;
+``gate_up`` interleaves gate row ``i`` (``2i``) and up row ``i`` (``2i+1``) for the
+SwiGLU epilogue.  Quantised fused matrices are quantised as one tensor.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from . import quant
+from ._lib import KGROUP_ELEMS, SB_FMT, SbLinear
+
+
+@dataclass
+class PackedLinear:
+    fmt: str
+    n: int
+    k: int
+    n_pad: int
+    w: torch.Tensor  # uint8, packed fragments
+    scale: Optional[torch.Tensor]  # fp32 [n_pad] (fp8/int8) or uint8 (nvfp4) or None
+    global_scale: float = 1.0
+    row_perm: Optional[torch.Tensor] = None  # packed row r holds logical row row_perm[r]
+
+    def c_struct(self) -> SbLinear:
+        s = SbLinear()
+        s.fmt = SB_FMT[self.fmt]
+        s.n, s.k, s.n_pad = self.n, self.k, self.n_pad
+        s.w = self.w.data_ptr()
+        s.scale = self.scale.data_ptr() if self.scale is not None else None
+        s.global_scale = float(self.global_scale)
+        return s
+
+    @property
+    def nbytes(self) -> int:
+        return self.w.numel() * self.w.element_size() + (
+            0 if self.scale is None else self.scale.numel() * self.scale.element_size()
+        )
+
+
+def _frag_order(q: torch.Tensor, kge: int) -> torch.Tensor:
+    """[n_pad, K] elements -> [tiles, kgroups, lane(g,c), ks, e] order (flattened)."""
+    n_pad, k = q.shape
+    T, KG, KS = n_pad // 16, k // kge, kge // 16
+    # n = t*16 + hr*8 + g ; k = kg*kge + ks*16 + hk*8 + c*2 + lo
+    v = q.reshape(T, 2, 8, KG, KS, 2, 4, 2)
+    # -> (T, KG, g, c, KS, hk, hr, lo): e = hk*4 + hr*2 + lo
+    v = v.permute(0, 3, 2, 6, 4, 5, 1, 7)
+    return v.reshape(-1)
+
+
+def pack_matrix(w: torch.Tensor, fmt: str) -> PackedLinear:
+    """Quantise (if needed) and pack a logical weight [N, K] (bf16 or fp32)."""
+    n, k = w.shape
+    kge = KGROUP_ELEMS[fmt]
+    if k % 64:
+        raise ValueError(f"K={k} must be a multiple of 64")
+    n_pad = (n + 15) // 16 * 16
+    dev = w.device
+    if fmt == "bf16":
+        q = w.to(torch.bfloat16).view(torch.int16)
+        if n_pad != n:
+            q = torch.cat([q, torch.zeros(n_pad - n, k, dtype=torch.int16, device=dev)])
+        packed = _frag_order(q, kge).contiguous().view(torch.uint8)
+        return PackedLinear(fmt, n, k, n_pad, packed, None)
+    parts = quant.quantize(fmt, w)
+    if fmt in ("fp8", "int8"):
+        q, s = parts
+        q = q.view(torch.uint8)
+        if n_pad != n:
+            q = torch.cat([q, torch.zeros(n_pad - n, k, dtype=torch.uint8, device=dev)])
+            s = torch.cat([s, torch.ones(n_pad - n, dtype=torch.float32, device=dev)])
+        packed = _frag_order(q, kge).contiguous()
+        return PackedLinear(fmt, n, k, n_pad, packed, s.contiguous())
+    codes, sb, g = parts
+    if n_pad != n:
+        codes = torch.cat([codes, torch.zeros(n_pad - n, k, dtype=torch.uint8, device=dev)])
+        sb = torch.cat([sb, torch.zeros(n_pad - n, k // 16, dtype=torch.uint8, device=dev)])
+    e = _frag_order(codes, kge).view(-1, 2)
+    packed = (e[:, 0] | (e[:, 1] << 4)).contiguous()
+    T, KG = n_pad // 16, k // 64
+    sv = sb.reshape(T, 2, 8, KG, 4).permute(0, 3, 2, 4, 1).contiguous().view(-1)
+    return PackedLinear(fmt, n, k, n_pad, packed, sv, g)
+
+
+def rope_pair_perm(n_heads: int, head_dim: int = 128) -> torch.Tensor:
+    """Packed row order for RoPE heads: within each head, (j, j+hd/2) adjacent."""
+    half = head_dim // 2
+    within = torch.stack([torch.arange(half), torch.arange(half) + half], dim=1).reshape(-1)
+    return (torch.arange(n_heads)[:, None] * head_dim + within[None, :]).reshape(-1)
+
+
+def qkv_perm(n_q: int, n_kv: int, head_dim: int = 128) -> torch.Tensor:
+    qk = rope_pair_perm(n_q + n_kv, head_dim)
+    v = torch.arange((n_q + n_kv) * head_dim, (n_q + 2 * n_kv) * head_dim)
+    return torch.cat([qk, v])
+
+
+def gate_up_perm(inter: int) -> torch.Tensor:
+    return torch.stack([torch.arange(inter), torch.arange(inter) + inter], dim=1).reshape(-1)
+
+
+def pack_qkv(wq, wk, wv, n_q, n_kv, fmt, head_dim=128) -> PackedLinear:
+    perm = qkv_perm(n_q, n_kv, head_dim).to(wq.device)
+    w = torch.cat([wq, wk, wv], dim=0)[perm]
+    p = pack_matrix(w, fmt)
+    p.row_perm = perm
+    return p
+
+
+def pack_gate_up(wg, wu, fmt) -> PackedLinear:
+    perm = gate_up_perm(wg.shape[0]).to(wg.device)
+    w = torch.cat([wg, wu], dim=0)[perm]
+    p = pack_matrix(w, fmt)
+    p.row_perm = perm
+    return p
+
+
+def unpack_reference(p: PackedLinear) -> torch.Tensor:
+    """Inverse of the packing for bf16 (pure layout check, CPU or GPU)."""
+    assert p.fmt == "bf16"
+    T, KG, KS = p.n_pad // 16, p.k // 16, 1
+    v = p.w.view(torch.int16).reshape(T, KG, 8, 4, KS, 2, 2, 2)
+    v = v.permute(0, 6, 2, 1, 4, 5, 3, 7).reshape(p.n_pad, p.k)
+    return v[: p.n].view(torch.bfloat16)

@@ -1,0 +1,154 @@
+"""Kernel-level parity on the GPU, through the C ABI, against the CPU oracle.
+
+* dequantisation: bit-exact vs oracle/quant_ref.py for every format;
+* dequant-GEMV: vs ``bf16(x.float() @ W_deq.T)`` (fp32 reference), tolerance
+  stated below;
+* glue ops: vs the reference's torch ops (oracle/granite_ref.py);
+* argmax: torch tie rule (first maximal index).
+"""
+
+import ctypes as C
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import granite_ref as gr
+from oracle import quant_ref as qr
+
+pytestmark = pytest.mark.gpu
+
+if not torch.cuda.is_available():  # collected on CPU hosts too; skip there
+    pytest.skip("needs a CUDA device", allow_module_level=True)
+
+from starling_b200 import _lib, pack  # noqa: E402
+from starling_b200._lib import check, ptr  # noqa: E402
+from starling_b200.rope import rope_tables  # noqa: E402
+
+BF16 = torch.bfloat16
+lib = _lib.load()
+S = lambda: _lib.current_stream()  # noqa: E731
+
+
+def _w(n, k, seed, std=0.02):
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(n, k, generator=g) * std).to(BF16)
+
+
+def _to_dev(p: pack.PackedLinear) -> pack.PackedLinear:
+    p.w = p.w.cuda()
+    p.scale = None if p.scale is None else p.scale.cuda()
+    return p
+
+
+def _oracle_dense(w, fmt):
+    if fmt == "bf16":
+        return w.float()
+    return torch.from_numpy(qr.dequantize(fmt, qr.quantize(fmt, w.float().numpy())))
+
+
+@pytest.mark.parametrize("fmt", ["bf16", "fp8", "int8", "nvfp4"])
+def test_dequant_bit_exact(fmt):
+    w = _w(100, 320 if fmt != "nvfp4" else 384, seed=11)
+    p = _to_dev(pack.pack_matrix(w, fmt))
+    out = torch.empty(p.n, p.k, dtype=torch.float32, device="cuda")
+    check(lib.sb_dequant_f32(C.byref(p.c_struct()), ptr(out), S()))
+    got = out.cpu().numpy()
+    want = _oracle_dense(w, fmt).numpy()
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    outb = torch.empty(p.n, p.k, dtype=BF16, device="cuda")
+    check(lib.sb_dequant_bf16(C.byref(p.c_struct()), ptr(outb), S()))
+    assert torch.equal(outb.cpu(), torch.from_numpy(want).to(BF16))
+
+
+# GEMV tolerance: the kernel accumulates in fp32 in a different order than
+# the fp32 reference, so a bf16 output may differ by one rounding step.
+def _close_bf16(got, ref):
+    g, r = got.float(), ref.float()
+    tol = 2.0 ** -7 * r.abs() + 1e-3 * r.abs().max()  # one bf16 ulp + tiny absolute slack
+    bad = (g - r).abs() > tol
+    assert bad.float().mean() < 1e-4, f"{int(bad.sum())} of {bad.numel()} outside one bf16 ulp"
+    assert (g - r).abs().max() <= 4 * 2.0 ** -7 * r.abs().max()
+
+
+@pytest.mark.parametrize("fmt", ["bf16", "fp8", "int8", "nvfp4"])
+@pytest.mark.parametrize("n,k,m", [(3072, 2048, 1), (2048, 8192, 1), (1000, 2048, 3), (512, 1024, 9),
+                                   (2048, 2048, 48), (4096, 1024, 16)])
+def test_linear(fmt, n, k, m):
+    w = _w(n, k, seed=n + k + m)
+    x = torch.randn(m, k, generator=torch.Generator().manual_seed(5)).to(BF16)
+    p = _to_dev(pack.pack_matrix(w, fmt))
+    y = torch.empty(m, n, dtype=BF16, device="cuda")
+    xd = x.cuda()
+    check(lib.sb_linear(C.byref(p.c_struct()), ptr(xd), ptr(y), m, 0, S()), "sb_linear")
+    ref = (x.float() @ _oracle_dense(w, fmt).T).to(BF16)
+    _close_bf16(y.cpu(), ref)
+
+
+def test_linear_pdl_same_as_plain():
+    w = _w(2048, 2048, seed=3)
+    p = _to_dev(pack.pack_matrix(w, "nvfp4"))
+    x = torch.randn(1, 2048, device="cuda").to(BF16)
+    y0 = torch.empty(1, 2048, dtype=BF16, device="cuda")
+    y1 = torch.empty_like(y0)
+    check(lib.sb_linear(C.byref(p.c_struct()), ptr(x), ptr(y0), 1, 0, S()))
+    check(lib.sb_linear(C.byref(p.c_struct()), ptr(x), ptr(y1), 1, 1, S()))
+    assert torch.equal(y0, y1)
+
+
+def test_glue_rmsnorm_silu_residual():
+    g = torch.Generator().manual_seed(9)
+    x = (torch.randn(4, 2048, generator=g) * 3).to(BF16)
+    w = (1 + 0.1 * torch.randn(2048, generator=g)).to(BF16)
+    y = torch.empty_like(x, device="cuda")
+    check(lib.sb_rmsnorm(ptr(x.cuda()), ptr(w.cuda()), ptr(y), 4, 2048, C.c_float(1e-5), S()))
+    ref = gr.rmsnorm(x, w, 1e-5)
+    diff = (y.cpu().float() != ref.float())
+    assert diff.float().mean() < 1e-3  # rare 1-ulp flips from the sum order of mean(x^2)
+    assert torch.allclose(y.cpu().float(), ref.float(), rtol=2 ** -7, atol=0)
+
+    gt = (torch.randn(8192, generator=g) * 4).to(BF16)
+    up = torch.randn(8192, generator=g).to(BF16)
+    o = torch.empty(8192, dtype=BF16, device="cuda")
+    check(lib.sb_silu_mul(ptr(gt.cuda()), ptr(up.cuda()), ptr(o), 8192, S()))
+    ref = gr.silu_mul(gt, up)
+    assert (o.cpu().float() != ref.float()).float().mean() < 1e-3
+    assert torch.allclose(o.cpu().float(), ref.float(), rtol=2 ** -7, atol=1e-30)
+
+    a = torch.randn(2048, generator=g).to(BF16)
+    b = torch.randn(2048, generator=g).to(BF16)
+    z = torch.empty(2048, dtype=BF16, device="cuda")
+    check(lib.sb_residual_scale(ptr(a.cuda()), ptr(b.cuda()), ptr(z), 2048, C.c_float(0.22), S()))
+    assert torch.equal(z.cpu(), gr.residual_scale(a, b, 0.22))  # bf16 products: exact
+
+
+def test_glue_rope_bit_exact():
+    d = gr.BASELINE_DIMS
+    cs, sn = rope_tables(128, d.theta, 1024)
+    pos = torch.tensor([0, 7, 300, 1023], dtype=torch.int32)
+    q = (torch.randn(4, 16, 128, generator=torch.Generator().manual_seed(2)) * 20).to(BF16)
+    qd = q.cuda().contiguous()
+    check(lib.sb_rope(ptr(qd), 64, 16, ptr(pos.cuda()), ptr(cs.cuda()), ptr(sn.cuda()), S()))
+    c4, s4 = gr.rope_cos_sin(d, pos.long().view(4, 1))  # (4, 1, 128)
+    ref = q * c4 + gr.rotate_half(q) * s4  # llm_mega.py:542 with per-position cos/sin
+    assert torch.equal(qd.cpu(), ref)
+
+
+def test_rope_table_matches_hf_formula():
+    d = gr.BASELINE_DIMS
+    cs, sn = rope_tables(128, d.theta, 700)
+    c, s = gr.rope_cos_sin(d, torch.arange(700).view(1, -1))
+    assert torch.equal(cs, c[0, :, :64]) and torch.equal(sn, s[0, :, :64])
+    assert torch.equal(c[0, :, :64], c[0, :, 64:])
+
+
+def test_argmax_first_max():
+    x = torch.zeros(3, 100353, dtype=BF16)
+    x[0, 17] = 5.0
+    x[0, 90000] = 5.0
+    x[1, :] = -1.0
+    x[2, 100352] = 1.0
+    out = torch.empty(3, dtype=torch.int64, device="cuda")
+    check(lib.sb_argmax_bf16(ptr(x.cuda()), 3, 100353, ptr(out), S()))
+    assert out.cpu().tolist() == [17, 0, 100352]
+    assert out.cpu().tolist() == x.float().argmax(-1).tolist()
