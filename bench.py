@@ -284,18 +284,27 @@ def dominant_kernel(eng, st, d, B, T, fmt, reset):
             p = eng.layers[0][name]
             nbytes = p.nbytes + B * p.k * 2 + B * (p.n // (2 if name == "gate_up" else 1)) * 2
         reset()
-        for _ in range(3):
+
+        def launch_all():
             for l in range(L):
                 _lib.check(lib.sb_decode_op(C.byref(eng.cmodel), C.byref(st.c), l, op, 0, _lib.current_stream()))
+
+        launch_all()  # eager once (kernel attributes), then one graph of the 40 launches
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            launch_all()
+        for _ in range(2):
+            g.replay()
         torch.cuda.synchronize()
         reps = 5
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for _ in range(reps):
-            for l in range(L):
-                _lib.check(lib.sb_decode_op(C.byref(eng.cmodel), C.byref(st.c), l, op, 0, _lib.current_stream()))
+            g.replay()
         e1.record(stream)
         torch.cuda.synchronize()
+        del g
         us = e0.elapsed_time(e1) * 1000.0 / (reps * L)
         cands[name] = dict(us=us, bytes=nbytes, gbs=nbytes / (us * 1e-6) / 1e9)
     reset()

@@ -117,6 +117,7 @@ typedef struct SbState {
   uint16_t* q;       /* [B*m, n_q*128] */
   uint16_t* attn;    /* [B*m, n_q*128] */
   uint16_t* act;     /* [B*m, inter] */
+  uint16_t* xnorm;   /* [B*m, hidden] normalised rows (used when B*m > 8) */
   uint16_t* logits;  /* [B*m, vocab] or NULL */
   void* workspace;   /* scratch, >= sb_workspace_bytes() bytes, zeroed once */
   size_t workspace_bytes;

@@ -55,7 +55,7 @@ class SbState(C.Structure):
         ("batch", C.c_int32), ("m", C.c_int32), ("mode", C.c_int32), ("use_pdl", C.c_int32),
         ("eos_id", C.c_int64), ("pad_id", C.c_int64),
         ("ids", vp), ("ctrl", vp), ("prompt_len", vp), ("rope_off", vp), ("finished", vp),
-        ("out_ids", vp), ("hidden", vp), ("q", vp), ("attn", vp), ("act", vp), ("logits", vp),
+        ("out_ids", vp), ("hidden", vp), ("q", vp), ("attn", vp), ("act", vp), ("xnorm", vp), ("logits", vp),
         ("workspace", vp), ("workspace_bytes", C.c_size_t),
     ]
 

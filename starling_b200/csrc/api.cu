@@ -116,6 +116,20 @@ static LmWork lm_work(const SbModel* md, int tokens, void* base) {
   return w;
 }
 
+// Token rows above which RMSNorm runs as its own kernel instead of the GEMV
+// prologue (which every CTA of the GEMV would otherwise recompute).
+static const int kFusedNormMaxRows = 8;
+
+static int run_norm(const SbModel* md, const SbState* st, const uint16_t* x, bool embed, const uint16_t* w,
+                    cudaStream_t s) {
+  const int T = st->batch * st->m;
+  if (!st->xnorm) return fail(SB_ERR_ARG, "state->xnorm is required for more than %d token rows", kFusedNormMaxRows);
+  const int rc = norm_rows_launch(embed ? nullptr : x, embed ? st->ids : nullptr, md->embed, md->vocab, md->emb_mult, w,
+                                  st->xnorm, embed ? st->hidden : nullptr, T, md->hidden, md->eps, st->use_pdl != 0, s);
+  if (rc != 0) return fail(rc, "norm launch: %s", rc < 1000 ? cudaGetErrorString((cudaError_t)rc) : "config");
+  return 0;
+}
+
 static int launch_lm_head(const SbModel* md, const SbState* st, int step, cudaStream_t s) {
   const int T = st->batch * st->m;
   LmWork w = lm_work(md, T, st->workspace);
@@ -125,6 +139,11 @@ static int launch_lm_head(const SbModel* md, const SbState* st, int step, cudaSt
   p.x = st->hidden;
   p.norm_w = md->final_norm;
   p.eps = md->eps;
+  if (T > kFusedNormMaxRows) {
+    SB_TRY(run_norm(md, st, st->hidden, false, md->final_norm, s));
+    p.pro = PRO_NONE;
+    p.x = st->xnorm;
+  }
   p.epi = EPI_ARGMAX;
   p.logits = st->logits;
   p.logits_mult = md->logits_mult;
@@ -179,10 +198,16 @@ static int launch_op(const SbModel* md, const SbState* st, int l, int op, int st
   const SbLayer& L = md->layers[l];
   if (!lin_ok(L.qkv) || !lin_ok(L.o) || !lin_ok(L.gate_up) || !lin_ok(L.down))
     return fail(SB_ERR_ARG, "layer %d: bad packed linear", l);
+  const bool sep_norm = T > kFusedNormMaxRows;
   if (op == SB_OP_QKV) {  // RMSNorm (layer 0: embedding x12) -> q/k/v -> RoPE + cache write
     GemvParams p = base_params(L.qkv, T);
     p.pro = l == 0 ? PRO_EMBED : PRO_RMSNORM;
     p.x = st->hidden;
+    if (sep_norm) {
+      SB_TRY(run_norm(md, st, st->hidden, l == 0, L.in_norm, s));
+      p.pro = PRO_NONE;
+      p.x = st->xnorm;
+    }
     p.norm_w = L.in_norm;
     p.eps = md->eps;
     p.ids = st->ids;
@@ -221,6 +246,11 @@ static int launch_op(const SbModel* md, const SbState* st, int l, int op, int st
   p.x = st->hidden;
   p.norm_w = L.post_norm;
   p.eps = md->eps;
+  if (sep_norm) {
+    SB_TRY(run_norm(md, st, st->hidden, false, L.post_norm, s));
+    p.pro = PRO_NONE;
+    p.x = st->xnorm;
+  }
   p.epi = EPI_SWIGLU;
   p.y = st->act;
   return run_gemv(p, L.gate_up.fmt, pdl, s);

@@ -145,13 +145,36 @@ __global__ void __launch_bounds__(512) k_gemv(const __grid_constant__ GemvParams
   uint16_t* const yout = p.y ? p.y + row_off * p.n : nullptr;
   const int ntile = min(p.rt, p.n_tiles - tile0);
   const int rt16 = p.rt * 16;
+  // Each warp owns one row tile; the wpt warps of a tile split its K range
+  // (kgroups my_sub, my_sub + wpt, ...).
+  const int wpt = W / p.rt;
+  const int my_tile = warp / wpt, my_sub = warp % wpt;
+  const bool tile_live = my_tile < ntile;
+  const size_t tt = static_cast<size_t>(tile0 + (tile_live ? my_tile : 0));
+  const uint4* wt = reinterpret_cast<const uint4*>(p.w) + (tt * p.kg_total + kg0) * 32 + lane;
+  const uint2* st = reinterpret_cast<const uint2*>(p.scale) + (tt * p.kg_total + kg0) * 8 + g;
 
-  // ---- 1. prefetch this CTA's weights into L2, then wait for the producer ----
-  if (tid == 0) {
+  // ---- 1. weights do not depend on the previous kernel: start streaming them
+  //         before waiting for it (first PRE kgroups per warp into registers,
+  //         the rest of the CTA's range into L2) ---------------------------------
+  constexpr int PRE = 8;
+  uint4 a[PRE];
+  uint2 s[PRE];
+#pragma unroll
+  for (int u = 0; u < PRE; ++u) {
+    const int kg = my_sub + u * wpt;
+    if (tile_live && kg < kg_cta) {
+      a[u] = ldg_stream(wt + static_cast<size_t>(kg) * 32);
+      if constexpr (FMT == SB_FMT_NVFP4) s[u] = ldg_stream2(st + static_cast<size_t>(kg) * 8);
+    }
+  }
+  if (tid == 0 && kg_cta > PRE * wpt) {
+    const int kg_rest = PRE * wpt;
     for (int r = 0; r < ntile; ++r) {
       const size_t t = static_cast<size_t>(tile0 + r);
-      prefetch_l2(p.w + (t * p.kg_total + kg0) * 512, static_cast<uint32_t>(kg_cta) * 512u);
-      if (FMT == SB_FMT_NVFP4) prefetch_l2(p.scale + (t * p.kg_total + kg0) * 64, static_cast<uint32_t>(kg_cta) * 64u);
+      prefetch_l2(p.w + (t * p.kg_total + kg0 + kg_rest) * 512, static_cast<uint32_t>(kg_cta - kg_rest) * 512u);
+      if (FMT == SB_FMT_NVFP4)
+        prefetch_l2(p.scale + (t * p.kg_total + kg0 + kg_rest) * 64, static_cast<uint32_t>(kg_cta - kg_rest) * 64u);
     }
   }
   pdl_wait();
@@ -161,110 +184,140 @@ __global__ void __launch_bounds__(512) k_gemv(const __grid_constant__ GemvParams
   const int xs_stride = k_cta + 8;
   uint16_t* xs = reinterpret_cast<uint16_t*>(smem);
   size_t off = (static_cast<size_t>(M) * xs_stride * 2 + 15) & ~size_t(15);
-  float* red = reinterpret_cast<float*>(smem + off);  // [W][rt16][M]
-  float* tot = red + static_cast<size_t>(W) * rt16 * M;  // [rt16][M]
-  int* xshift = reinterpret_cast<int*>(tot + rt16 * M);  // [M]
-  int* s_best = xshift + 64;                             // [M]
-  float* s_bval = reinterpret_cast<float*>(s_best + 64);  // [M]
-  int* s_flag = reinterpret_cast<int*>(s_bval + 64);
+  float* red = reinterpret_cast<float*>(smem + off);        // [W][16][M]
+  float* tot = red + static_cast<size_t>(W) * 16 * M;       // [rt16][M]
+  int* xshift = reinterpret_cast<int*>(tot + rt16 * M);     // [64]
+  int* s_best = xshift + 64;                                // [64]
+  float* s_bval = reinterpret_cast<float*>(s_best + 64);     // [64]
+  int* s_flag = reinterpret_cast<int*>(s_bval + 64);        // [4]
+  float* s_red = reinterpret_cast<float*>(s_flag + 4);      // [16] per-warp partial sums
+  float* s_amx = s_red + 16;                                // [16] per-warp partial maxima
 
   // ---- 3. stage the activation rows (prologue) -----------------------------------
-  for (int m = warp; m < M; m += W) {
-    const uint16_t* src;
-    if (p.pro == PRO_EMBED) {
-      int64_t id = p.ids[m];
-      id = id < 0 ? 0 : (id >= p.embed_rows ? p.embed_rows - 1 : id);  // never read outside the table
-      src = p.embed + static_cast<size_t>(id) * p.k;
-    } else {
-      src = xin + static_cast<size_t>(m) * p.k;
-    }
-    float rstd = 1.f;
-    if (p.pro != PRO_NONE) {
-      float ss = 0.f;
-      const bool write_h = p.pro == PRO_EMBED && blockIdx.x == 0 && p.hidden_out != nullptr;
-      for (int k = lane * 8; k < p.k; k += 256) {
-        float f[8];
-        unpack8(*reinterpret_cast<const uint4*>(src + k), f);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          if (p.pro == PRO_EMBED) f[j] = bf(f[j] * p.emb_mult);  // embed_tokens(ids) * 12 (llm_mega.py:514)
-          ss += f[j] * f[j];
-        }
-        if (write_h) *reinterpret_cast<uint4*>(p.hidden_out + static_cast<size_t>(m) * p.k + k) = pack8(f);
-      }
-      ss = warp_sum(ss);
-      rstd = 1.f / sqrtf(ss / static_cast<float>(p.k) + p.eps);
-    }
-    float amax = 0.f;
-    for (int k = lane * 8; k < k_cta; k += 256) {
-      float f[8];
-      unpack8(*reinterpret_cast<const uint4*>(src + k0 + k), f);
-      if (p.pro != PRO_NONE) {
-        float w8[8];
-        unpack8(*reinterpret_cast<const uint4*>(p.norm_w + k0 + k), w8);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          float h = p.pro == PRO_EMBED ? bf(f[j] * p.emb_mult) : f[j];
-          f[j] = bf(w8[j] * bf(h * rstd));  // weight * bf16(x * rstd)  (modeling_granite.py:192-197)
+  // A row is handled by wpr = W / M warps (one pass when M <= W) whose loads
+  // are all independent; per-row sums and maxima are combined through shared
+  // memory in a fixed order.
+  {
+    const int wpr = W / M >= 1 ? W / M : 1;
+    const int nslot = W / wpr;
+    const int slot = warp / wpr, sub = warp % wpr;
+    const int gt = sub * 32 + lane, gn = wpr * 32;
+    const bool norm = p.pro != PRO_NONE;
+    for (int m0 = 0; m0 < M; m0 += nslot) {
+      const int m = m0 + slot;
+      const bool live = slot < nslot && m < M;
+      const uint16_t* src = xin;
+      if (live) {
+        if (p.pro == PRO_EMBED) {
+          int64_t id = p.ids[m];
+          id = id < 0 ? 0 : (id >= p.embed_rows ? p.embed_rows - 1 : id);  // never read outside the table
+          src = p.embed + static_cast<size_t>(id) * p.k;
+        } else {
+          src = xin + static_cast<size_t>(m) * p.k;
         }
       }
+      float rstd = 1.f;
+      if (norm) {
+        float ss = 0.f;
+        if (live) {
+          const bool write_h = p.pro == PRO_EMBED && blockIdx.x == 0 && p.hidden_out != nullptr;
+#pragma unroll 4
+          for (int k = gt * 8; k < p.k; k += gn * 8) {
+            float f[8];
+            unpack8(*reinterpret_cast<const uint4*>(src + k), f);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(f[j]));
-      *reinterpret_cast<uint4*>(xs + m * xs_stride + k) = pack8(f);
-    }
-    if (FMT != SB_FMT_BF16) {
-      amax = warp_max(amax);
-      int e = 0;
-      if (amax > 0.f) frexpf(amax, &e);
-      const int shift = 15 - e;  // amax * 2^shift in [2^14, 2^15): exact bf16 -> f16
-      for (int k = lane * 8; k < k_cta; k += 256) {
-        float f[8];
-        uint4 v = *reinterpret_cast<const uint4*>(xs + m * xs_stride + k);
-        unpack8(v, f);
-        uint32_t h[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          __half2 hh = __floats2half2_rn(ldexpf(f[2 * j], shift), ldexpf(f[2 * j + 1], shift));
-          h[j] = *reinterpret_cast<uint32_t*>(&hh);
+            for (int j = 0; j < 8; ++j) {
+              if (p.pro == PRO_EMBED) f[j] = bf(f[j] * p.emb_mult);  // embed_tokens(ids) * 12 (llm_mega.py:514)
+              ss += f[j] * f[j];
+            }
+            if (write_h) *reinterpret_cast<uint4*>(p.hidden_out + static_cast<size_t>(m) * p.k + k) = pack8(f);
+          }
         }
-        *reinterpret_cast<uint4*>(xs + m * xs_stride + k) = make_uint4(h[0], h[1], h[2], h[3]);
+        ss = warp_sum(ss);
+        if (lane == 0) s_red[warp] = ss;
+        __syncthreads();
+        if (live) {
+          float tsum = 0.f;
+          for (int q = 0; q < wpr; ++q) tsum += s_red[slot * wpr + q];
+          rstd = 1.f / sqrtf(tsum / static_cast<float>(p.k) + p.eps);
+        }
       }
-      if (lane == 0) xshift[m] = shift;
-    } else if (lane == 0) {
-      xshift[m] = 0;
+      float amax = 0.f;
+      if (live) {
+#pragma unroll 4
+        for (int k = gt * 8; k < k_cta; k += gn * 8) {
+          float f[8];
+          unpack8(*reinterpret_cast<const uint4*>(src + k0 + k), f);
+          if (norm) {
+            float w8[8];
+            unpack8(*reinterpret_cast<const uint4*>(p.norm_w + k0 + k), w8);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float h = p.pro == PRO_EMBED ? bf(f[j] * p.emb_mult) : f[j];
+              f[j] = bf(w8[j] * bf(h * rstd));  // weight * bf16(x * rstd)  (modeling_granite.py:192-197)
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(f[j]));
+          *reinterpret_cast<uint4*>(xs + m * xs_stride + k) = pack8(f);
+        }
+      }
+      if (FMT != SB_FMT_BF16) {
+        amax = warp_max(amax);
+        if (lane == 0) s_amx[warp] = amax;
+        __syncthreads();
+        if (live) {
+          float am = 0.f;
+          for (int q = 0; q < wpr; ++q) am = fmaxf(am, s_amx[slot * wpr + q]);
+          int e = 0;
+          if (am > 0.f) frexpf(am, &e);
+          const int shift = 15 - e;  // row max * 2^shift in [2^14, 2^15): exact bf16 -> f16
+          for (int k = gt * 8; k < k_cta; k += gn * 8) {  // same thread wrote these elements
+            float f[8];
+            unpack8(*reinterpret_cast<const uint4*>(xs + m * xs_stride + k), f);
+            uint32_t h[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              __half2 hh = __floats2half2_rn(ldexpf(f[2 * j], shift), ldexpf(f[2 * j + 1], shift));
+              h[j] = *reinterpret_cast<uint32_t*>(&hh);
+            }
+            *reinterpret_cast<uint4*>(xs + m * xs_stride + k) = make_uint4(h[0], h[1], h[2], h[3]);
+          }
+          if (sub == 0 && lane == 0) xshift[m] = shift;
+        }
+      } else if (live && sub == 0 && lane == 0) {
+        xshift[m] = 0;
+      }
+      __syncthreads();  // xs rows complete; s_red / s_amx free for the next pass
     }
   }
-  __syncthreads();
 
-  // ---- 4. stream the weight tiles through the tensor cores -------------------------
-  const uint4* wbase = reinterpret_cast<const uint4*>(p.w);
-  const uint2* sbase = reinterpret_cast<const uint2*>(p.scale);
-  for (int r = 0; r < ntile; ++r) {
-    const size_t t = static_cast<size_t>(tile0 + r);
-    float acc[NT][4];
+  // ---- 4. the weight tile through the tensor cores ---------------------------------
+  float acc[NT][4];
 #pragma unroll
-    for (int i = 0; i < NT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
-    const uint4* wt = wbase + (t * p.kg_total + kg0) * 32 + lane;
-    const uint2* st = sbase + (t * p.kg_total + kg0) * 8 + g;
-    constexpr int U = 4;
-    for (int kb = warp; kb < kg_cta; kb += W * U) {
-      uint4 a[U];
-      uint2 s[U];
+  for (int i = 0; i < NT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int kg = kb + u * W;
-        if (kg < kg_cta) {
-          a[u] = ldg_stream(wt + static_cast<size_t>(kg) * 32);
-          if constexpr (FMT == SB_FMT_NVFP4) s[u] = ldg_stream2(st + static_cast<size_t>(kg) * 8);
-        }
-      }
+  for (int u = 0; u < PRE; ++u) {
+    const int kg = my_sub + u * wpt;
+    if (tile_live && kg < kg_cta) process_kgroup<FMT, NT>(a[u], s[u], kg * KGE, xs, xs_stride, M, g, c, acc);
+  }
+  for (int base = PRE; my_sub + base * wpt < kg_cta; base += PRE) {  // ranges longer than the preload
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int kg = kb + u * W;
-        if (kg < kg_cta) process_kgroup<FMT, NT>(a[u], s[u], kg * KGE, xs, xs_stride, M, g, c, acc);
+    for (int u = 0; u < PRE; ++u) {
+      const int kg = my_sub + (base + u) * wpt;
+      if (tile_live && kg < kg_cta) {
+        a[u] = ldg_stream(wt + static_cast<size_t>(kg) * 32);
+        if constexpr (FMT == SB_FMT_NVFP4) s[u] = ldg_stream2(st + static_cast<size_t>(kg) * 8);
       }
     }
-    float* rw = red + (static_cast<size_t>(warp) * rt16 + r * 16) * M;
+#pragma unroll
+    for (int u = 0; u < PRE; ++u) {
+      const int kg = my_sub + (base + u) * wpt;
+      if (tile_live && kg < kg_cta) process_kgroup<FMT, NT>(a[u], s[u], kg * KGE, xs, xs_stride, M, g, c, acc);
+    }
+  }
+  {
+    float* rw = red + static_cast<size_t>(warp) * 16 * M;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       const int col = nt * 8 + 2 * c;
@@ -280,12 +333,17 @@ __global__ void __launch_bounds__(512) k_gemv(const __grid_constant__ GemvParams
   }
   __syncthreads();
 
-  // ---- 5. reduce: warps (fixed order), then cluster ranks (fixed order) ------------
+  // ---- 5. reduce: the tile's warps (fixed order), then cluster ranks (fixed order)
   const int nrow = ntile * 16;
   for (int i = tid; i < nrow * M; i += blockDim.x) {
-    float s = 0.f;
-    for (int w = 0; w < W; ++w) s += red[static_cast<size_t>(w) * rt16 * M + i];
-    tot[i] = s;
+    const int lrow = i / M, m = i % M;
+    const int r = lrow >> 4, rr = lrow & 15;
+    float sum = 0.f;
+    for (int q = 0; q < wpt; ++q) sum += red[(static_cast<size_t>(r * wpt + q) * 16 + rr) * M + m];
+    // undo this CTA's power-of-two activation scale before ranks are summed:
+    // each rank chose it from the max of its own K slice
+    if (FMT != SB_FMT_BF16) sum = ldexpf(sum, -xshift[m]);
+    tot[i] = sum;
   }
   if (ck > 1) {
     cg::cluster_group cl = cg::this_cluster();
@@ -309,7 +367,6 @@ __global__ void __launch_bounds__(512) k_gemv(const __grid_constant__ GemvParams
     float v = tot[lrow * M + m];
     if (FMT == SB_FMT_NVFP4) v *= p.gscale;
     if (FMT == SB_FMT_FP8 || FMT == SB_FMT_INT8) v *= reinterpret_cast<const float*>(p.scale)[row0 + lrow];
-    if (FMT != SB_FMT_BF16) v = ldexpf(v, -xshift[m]);
     return v;
   };
 
@@ -484,11 +541,17 @@ GemvCfg gemv_pick(int fmt, int n_pad, int k, int m) {
   int ck = 1;
   while (ck < 8 && static_cast<long>(m) * (k / ck + 8) * 2 > 96 * 1024 && (k / (2 * ck)) % kge == 0) ck *= 2;
   while (ck < 4 && n_tiles * ck < 2 * kSMs && (k / (2 * ck)) % kge == 0 && k / (2 * ck) >= 256) ck *= 2;
+  c.warps = (k / ck / kge) >= 64 ? 16 : 8;
+  const int kg_cta = k / ck / kge;
+  // more row tiles per CTA while: the grid stays >= 2 waves, every warp's
+  // weight range still fits the register preload (<= 8 kgroups), and the
+  // reduction buffers stay small
   int rt = 1;
-  while (rt < 8 && (n_tiles / (rt * 2)) * ck >= 2 * kSMs) rt *= 2;
+  while (rt < 8 && rt * 2 <= c.warps && (n_tiles / (rt * 2)) * ck >= 2 * kSMs &&
+         (rt * 2) * kg_cta <= 8 * c.warps && static_cast<long>(c.warps + rt * 2) * 16 * m * 4 <= 64 * 1024)
+    rt *= 2;
   c.ck = ck;
   c.rt = rt;
-  c.warps = (k / ck / kge) >= 64 ? 16 : 8;
   return c;
 }
 
@@ -496,7 +559,7 @@ size_t gemv_smem_bytes(const GemvCfg& c, int k, int m) {
   const int k_cta = k / c.ck;
   size_t off = (static_cast<size_t>(m) * (k_cta + 8) * 2 + 15) & ~size_t(15);
   const size_t rt16 = static_cast<size_t>(c.rt) * 16;
-  return off + (static_cast<size_t>(c.warps) + 1) * rt16 * m * 4 + 64 * 4 * 3 + 16;
+  return off + (static_cast<size_t>(c.warps) * 16 + rt16) * m * 4 + (64 * 3 + 4 + 32) * 4 + 16;
 }
 
 int gemv_grid(const GemvCfg& c, int n_tiles) { return ((n_tiles + c.rt - 1) / c.rt) * c.ck; }

@@ -33,6 +33,55 @@ __global__ void k_rmsnorm(const uint16_t* x, const uint16_t* w, uint16_t* y, int
     yr[i] = f_to_bf16_bits(u16_to_f(w[i]) * bf(u16_to_f(xr[i]) * rstd));
 }
 
+// RMSNorm of whole rows for the decode step when it has more than 8 token
+// rows (the GEMV prologue would otherwise recompute it in every CTA).  With
+// ids != nullptr the row is first the embedding row times mult (rounded to
+// bf16, llm_mega.py:514) and is also written to h_out (the residual stream).
+__global__ void __launch_bounds__(256) k_norm_rows(const uint16_t* x, const int64_t* ids, const uint16_t* embed,
+                                                   int embed_rows, float mult, const uint16_t* w, uint16_t* y,
+                                                   uint16_t* h_out, int n, float eps) {
+  pdl_wait();
+  pdl_launch();
+  const uint16_t* xr;
+  if (ids) {
+    int64_t id = ids[blockIdx.x];
+    id = id < 0 ? 0 : (id >= embed_rows ? embed_rows - 1 : id);
+    xr = embed + static_cast<size_t>(id) * n;
+  } else {
+    xr = x + static_cast<size_t>(blockIdx.x) * n;
+  }
+  uint16_t* yr = y + static_cast<size_t>(blockIdx.x) * n;
+  __shared__ float red[8];
+  float v[32];  // n <= 256 threads * 32
+  int cnt = 0;
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const int k = threadIdx.x + i * 256;
+    if (k < n) {
+      float f = u16_to_f(xr[k]);
+      if (ids) f = bf(f * mult);
+      v[i] = f;
+      ss += f * f;
+      cnt = i + 1;
+    }
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tsum = 0.f;
+  for (int q = 0; q < 8; ++q) tsum += red[q];
+  const float rstd = 1.f / sqrtf(tsum / static_cast<float>(n) + eps);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const int k = threadIdx.x + i * 256;
+    if (i < cnt) {
+      yr[k] = f_to_bf16_bits(u16_to_f(w[k]) * bf(v[i] * rstd));
+      if (ids && h_out) h_out[static_cast<size_t>(blockIdx.x) * n + k] = f_to_bf16_bits(v[i]);
+    }
+  }
+}
+
 // fused_silu_mul (llm_kernels.py:241-285): bf16(silu(g)) * up
 __global__ void k_silu_mul(const uint16_t* g, const uint16_t* u, uint16_t* o, int64_t count) {
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < count;
@@ -192,6 +241,22 @@ int dequant_launch(const SbLinear& lin, void* out, bool f32, cudaStream_t s) {
   else
     k_dequant<uint16_t><<<grid, bs, 0, s>>>(lin, static_cast<uint16_t*>(out));
   return cudaGetLastError();
+}
+
+int norm_rows_launch(const uint16_t* x, const int64_t* ids, const uint16_t* embed, int embed_rows, float mult,
+                     const uint16_t* w, uint16_t* y, uint16_t* h_out, int rows, int n, float eps, bool pdl,
+                     cudaStream_t s) {
+  if (n > 256 * 32) return SB_ERR_CONFIG;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(rows);
+  cfg.blockDim = dim3(256);
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k_norm_rows, x, ids, embed, embed_rows, mult, w, y, h_out, n, eps);
 }
 
 int rmsnorm_launch(const uint16_t* x, const uint16_t* w, uint16_t* y, int rows, int n, float eps, cudaStream_t s) {

@@ -91,6 +91,7 @@ class EngineState:
         self.q = torch.zeros(T, d.n_q * d.head_dim, dtype=BF16, device=dev)
         self.attn = torch.zeros(T, d.n_q * d.head_dim, dtype=BF16, device=dev)
         self.act = torch.zeros(T, d.inter, dtype=BF16, device=dev)
+        self.xnorm = torch.zeros(T, d.hidden, dtype=BF16, device=dev)
         self.logits = torch.zeros(T, d.vocab, dtype=BF16, device=dev) if keep_logits else None
         nbytes = eng.lib.sb_workspace_bytes(C.byref(eng.cmodel), T)
         self.workspace = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=dev)
@@ -102,6 +103,7 @@ class EngineState:
         s.out_ids, s.hidden, s.q, s.attn, s.act = (ptr(self.out_ids), ptr(self.hidden), ptr(self.q),
                                                    ptr(self.attn), ptr(self.act))
         s.logits = ptr(self.logits)
+        s.xnorm = ptr(self.xnorm)
         s.workspace, s.workspace_bytes = ptr(self.workspace), self.workspace.numel()
         self.c = s
 

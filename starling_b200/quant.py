@@ -21,6 +21,13 @@ E4M3_MAX = 448.0
 E2M1_MAX = 6.0
 
 
+def _div(a: torch.Tensor, b: float) -> torch.Tensor:
+    """a / b with IEEE division on every device.  (On CUDA, torch evaluates
+    ``tensor / python_scalar`` as a multiply by the rounded reciprocal, which
+    is not the correctly rounded quotient; dividing by a tensor is.)"""
+    return a / torch.full_like(a, b)
+
+
 def _e4m3_bits(v: torch.Tensor) -> torch.Tensor:
     """fp32 (already within +-448) -> e4m3fn bits (RNE), with -0 canonicalised to +0."""
     b = v.to(torch.float8_e4m3fn).view(torch.uint8)
@@ -34,7 +41,7 @@ def e4m3_to_f32(bits: torch.Tensor) -> torch.Tensor:
 def quant_fp8(w: torch.Tensor):
     """-> (q uint8 [N,K] e4m3 bits, s fp32 [N])."""
     w = w.float()
-    s = w.abs().amax(dim=1) / E4M3_MAX
+    s = _div(w.abs().amax(dim=1), E4M3_MAX)
     s = torch.where(s == 0, torch.ones_like(s), s)
     v = (w / s[:, None]).clamp(-E4M3_MAX, E4M3_MAX)
     return _e4m3_bits(v), s
@@ -43,7 +50,7 @@ def quant_fp8(w: torch.Tensor):
 def quant_int8(w: torch.Tensor):
     """-> (q int8 [N,K], s fp32 [N])."""
     w = w.float()
-    s = w.abs().amax(dim=1) / 127.0
+    s = _div(w.abs().amax(dim=1), 127.0)
     s = torch.where(s == 0, torch.ones_like(s), s)
     q = torch.round(w / s[:, None]).clamp(-127, 127).to(torch.int8)
     return q, s
@@ -78,11 +85,11 @@ def quant_nvfp4(w: torch.Tensor):
     n, k = w.shape
     if k % 16:
         raise ValueError("nvfp4 needs K % 16 == 0")
-    g = (w.abs().amax() / (E2M1_MAX * E4M3_MAX)).reshape(1)
+    g = _div(w.abs().amax().reshape(1), E2M1_MAX * E4M3_MAX)
     g = torch.where(g == 0, torch.ones_like(g), g)
     wb = w.view(n, k // 16, 16)
     amax_b = wb.abs().amax(dim=2)
-    sb_bits = _e4m3_bits(((amax_b / E2M1_MAX) / g).clamp(max=E4M3_MAX))
+    sb_bits = _e4m3_bits((_div(amax_b, E2M1_MAX) / g).clamp(max=E4M3_MAX))
     sf = e4m3_to_f32(sb_bits) * g
     safe = torch.where(sf == 0, torch.ones_like(sf), sf)
     v = wb / safe[:, :, None]

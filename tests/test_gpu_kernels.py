@@ -47,6 +47,21 @@ def _oracle_dense(w, fmt):
     return torch.from_numpy(qr.dequantize(fmt, qr.quantize(fmt, w.float().numpy())))
 
 
+@pytest.mark.parametrize("fmt", ["fp8", "int8", "nvfp4"])
+@pytest.mark.parametrize("shape,std", [((96, 512), 0.05), ((2064, 512), 0.2), ((100, 1024), 1e-3)])
+def test_quantizer_on_gpu_matches_oracle(fmt, shape, std):
+    """Packing runs on the GPU at load time; its arithmetic must be the oracle's
+    (IEEE division, RNE conversions) bit-for-bit."""
+    from starling_b200 import quant
+
+    w = _w(*shape, seed=shape[0], std=std)
+    ours = quant.quantize(fmt, w.cuda())
+    ref = qr.quantize(fmt, w.float().numpy())
+    a = qr.dequantize(fmt, ref)
+    b = quant.dequantize(fmt, ours).cpu().numpy()
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
 @pytest.mark.parametrize("fmt", ["bf16", "fp8", "int8", "nvfp4"])
 def test_dequant_bit_exact(fmt):
     w = _w(100, 320 if fmt != "nvfp4" else 384, seed=11)
@@ -101,7 +116,8 @@ def test_glue_rmsnorm_silu_residual():
     x = (torch.randn(4, 2048, generator=g) * 3).to(BF16)
     w = (1 + 0.1 * torch.randn(2048, generator=g)).to(BF16)
     y = torch.empty_like(x, device="cuda")
-    check(lib.sb_rmsnorm(ptr(x.cuda()), ptr(w.cuda()), ptr(y), 4, 2048, C.c_float(1e-5), S()))
+    xd, wd = x.cuda(), w.cuda()  # keep device copies alive until the kernel has run
+    check(lib.sb_rmsnorm(ptr(xd), ptr(wd), ptr(y), 4, 2048, C.c_float(1e-5), S()))
     ref = gr.rmsnorm(x, w, 1e-5)
     diff = (y.cpu().float() != ref.float())
     assert diff.float().mean() < 1e-3  # rare 1-ulp flips from the sum order of mean(x^2)
@@ -110,7 +126,8 @@ def test_glue_rmsnorm_silu_residual():
     gt = (torch.randn(8192, generator=g) * 4).to(BF16)
     up = torch.randn(8192, generator=g).to(BF16)
     o = torch.empty(8192, dtype=BF16, device="cuda")
-    check(lib.sb_silu_mul(ptr(gt.cuda()), ptr(up.cuda()), ptr(o), 8192, S()))
+    gd, ud = gt.cuda(), up.cuda()
+    check(lib.sb_silu_mul(ptr(gd), ptr(ud), ptr(o), 8192, S()))
     ref = gr.silu_mul(gt, up)
     assert (o.cpu().float() != ref.float()).float().mean() < 1e-3
     assert torch.allclose(o.cpu().float(), ref.float(), rtol=2 ** -7, atol=1e-30)
@@ -118,7 +135,8 @@ def test_glue_rmsnorm_silu_residual():
     a = torch.randn(2048, generator=g).to(BF16)
     b = torch.randn(2048, generator=g).to(BF16)
     z = torch.empty(2048, dtype=BF16, device="cuda")
-    check(lib.sb_residual_scale(ptr(a.cuda()), ptr(b.cuda()), ptr(z), 2048, C.c_float(0.22), S()))
+    ad, bd = a.cuda(), b.cuda()
+    check(lib.sb_residual_scale(ptr(ad), ptr(bd), ptr(z), 2048, C.c_float(0.22), S()))
     assert torch.equal(z.cpu(), gr.residual_scale(a, b, 0.22))  # bf16 products: exact
 
 
@@ -128,7 +146,8 @@ def test_glue_rope_bit_exact():
     pos = torch.tensor([0, 7, 300, 1023], dtype=torch.int32)
     q = (torch.randn(4, 16, 128, generator=torch.Generator().manual_seed(2)) * 20).to(BF16)
     qd = q.cuda().contiguous()
-    check(lib.sb_rope(ptr(qd), 64, 16, ptr(pos.cuda()), ptr(cs.cuda()), ptr(sn.cuda()), S()))
+    pd, csd, snd = pos.cuda(), cs.cuda(), sn.cuda()
+    check(lib.sb_rope(ptr(qd), 64, 16, ptr(pd), ptr(csd), ptr(snd), S()))
     c4, s4 = gr.rope_cos_sin(d, pos.long().view(4, 1))  # (4, 1, 128)
     ref = q * c4 + gr.rotate_half(q) * s4  # llm_mega.py:542 with per-position cos/sin
     assert torch.equal(qd.cpu(), ref)
@@ -149,6 +168,7 @@ def test_argmax_first_max():
     x[1, :] = -1.0
     x[2, 100352] = 1.0
     out = torch.empty(3, dtype=torch.int64, device="cuda")
-    check(lib.sb_argmax_bf16(ptr(x.cuda()), 3, 100353, ptr(out), S()))
+    xd = x.cuda()
+    check(lib.sb_argmax_bf16(ptr(xd), 3, 100353, ptr(out), S()))
     assert out.cpu().tolist() == [17, 0, 100352]
     assert out.cpu().tolist() == x.float().argmax(-1).tolist()
