@@ -158,6 +158,17 @@ int sb_decode_op(const SbModel* model, const SbState* state, int32_t layer, int3
  * `.argmax(-1)` (llm_mega.py:200-202, batched.py:275-276). */
 int sb_lm_head_argmax(const SbModel* model, const SbState* state, int32_t step, sb_stream_t stream);
 
+/* sb_lm_head_argmax for callers that cannot allocate device memory (no
+ * device allocator of their own, or cudaMalloc forbidden because it
+ * synchronises the device).  No counterpart in the reference.  Same inputs
+ * and outputs as sb_lm_head_argmax; state->workspace is ignored: the scratch
+ * is a fixed 256 KiB device array inside the library (held on every GPU that
+ * loads it until exit).  Calls whose scratch would exceed it return
+ * SB_ERR_CONFIG.  The first call on a device looks up the array's device
+ * address; make that first call before any stream capture.  Calls share the
+ * array: calls that overlap on the GPU race. */
+int sb_lm_head_argmax_static(const SbModel* model, const SbState* state, int32_t step, sb_stream_t stream);
+
 /* ---- single ops (each one replaces one reference call site) ------------- */
 /* y[m, :] = x[m, :] W^T, bf16 out: nn.Linear (llm_mega.py:534-536,560,572-573,579,588).
  * Any m >= 1 (processed in blocks of 64 rows); y columns in packed row order. */

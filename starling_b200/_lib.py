@@ -64,6 +64,7 @@ EXPORTS = [
     "sb_last_error", "sb_version", "sb_workspace_bytes", "sb_decode_step", "sb_lm_head_argmax",
     "sb_linear", "sb_dequant_f32", "sb_dequant_bf16", "sb_rmsnorm", "sb_silu_mul",
     "sb_residual_scale", "sb_rope", "sb_argmax_bf16", "sb_attention", "sb_decode_op",
+    "sb_lm_head_argmax_static",
 ]
 
 
@@ -90,6 +91,7 @@ def load() -> C.CDLL:
     lib.sb_workspace_bytes.argtypes = [C.POINTER(SbModel), C.c_int32]
     lib.sb_decode_step.argtypes = [C.POINTER(SbModel), C.POINTER(SbState), C.c_int32, vp]
     lib.sb_lm_head_argmax.argtypes = [C.POINTER(SbModel), C.POINTER(SbState), C.c_int32, vp]
+    lib.sb_lm_head_argmax_static.argtypes = [C.POINTER(SbModel), C.POINTER(SbState), C.c_int32, vp]
     lib.sb_attention.argtypes = [C.POINTER(SbModel), C.POINTER(SbState), C.c_int32, vp]
     lib.sb_decode_op.argtypes = [C.POINTER(SbModel), C.POINTER(SbState), C.c_int32, C.c_int32, C.c_int32, vp]
     lib.sb_linear.argtypes = [C.POINTER(SbLinear), vp, vp, C.c_int32, C.c_int32, vp]

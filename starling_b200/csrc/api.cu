@@ -350,3 +350,55 @@ int sb_attention(const SbModel* md, const SbState* st, int32_t layer, sb_stream_
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// lm_head + argmax without a caller-provided workspace.
+//
+// Some callers cannot allocate device memory: an embedding runtime that binds
+// only this C ABI and owns no device allocator, or a latency-critical serving
+// loop that forbids cudaMalloc because it synchronises the whole device and
+// may fail once another framework has reserved the HBM pool.  This variant of
+// sb_lm_head_argmax keeps its argmax partials and completion counter in a
+// fixed file-scope device array instead of state->workspace.  The array is
+// kStaticLmScratchBytes (256 KiB) and lives on every GPU that loads this
+// library until the process exits.  Calls whose partials would not fit are
+// rejected.  All calls share the array, so two calls that overlap on the GPU
+// (different streams, or two processes' kernels interleaved through one
+// context) race: serialise them.
+// ---------------------------------------------------------------------------
+namespace {
+constexpr size_t kStaticLmScratchBytes = 256 * 1024;
+__device__ __align__(256) unsigned char g_lm_scratch[kStaticLmScratchBytes];
+constexpr int kMaxDevices = 64;
+void* g_lm_scratch_addr[kMaxDevices] = {};  // device address of g_lm_scratch per device
+}  // namespace
+
+extern "C" int sb_lm_head_argmax_static(const SbModel* md, const SbState* st, int32_t step, sb_stream_t stream) {
+  SB_TRY(check_state(md, st));
+  if (!lin_ok(md->lm_head)) return fail(SB_ERR_ARG, "bad lm_head");
+  int dev = 0;
+  SB_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return fail(SB_ERR_ARG, "device index %d out of range", dev);
+  // one-time set-up per device (this device is current): host code must use
+  // the symbol's device address, never &g_lm_scratch, which is a host stand-in
+  if (!g_lm_scratch_addr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_lm_scratch);
+    if (e != cudaSuccess) return fail(e, "cudaGetSymbolAddress(g_lm_scratch): %s", cudaGetErrorString(e));
+    g_lm_scratch_addr[dev] = p;
+  }
+  const int T = st->batch * st->m;
+  const size_t need = lm_work(md, T, nullptr).bytes;
+  if (need > kStaticLmScratchBytes)
+    return fail(SB_ERR_CONFIG,
+                "sb_lm_head_argmax_static: %d token rows need %zu scratch bytes, more than the fixed %zu; "
+                "use sb_lm_head_argmax with a caller workspace",
+                T, need, kStaticLmScratchBytes);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // the completion counter (first 256 bytes) must start at zero on every call
+  SB_TRY(cudaMemsetAsync(g_lm_scratch_addr[dev], 0, 256, s));
+  SbState local = *st;
+  local.workspace = g_lm_scratch_addr[dev];
+  local.workspace_bytes = kStaticLmScratchBytes;
+  return launch_op(md, &local, 0, SB_OP_LM_HEAD, step, s);
+}

@@ -1,0 +1,71 @@
+"""sb_lm_head_argmax_static: the lm_head + argmax entry point for callers that
+cannot allocate device memory (its scratch is a fixed array inside the
+library).  Called through the C ABI, it must give the same logits and token
+ids as sb_lm_head_argmax with a caller workspace, on two calls in a row, and
+reject shapes whose scratch would not fit.
+
+This file is named so that pytest collects it last.
+"""
+
+import ctypes as C
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+if not torch.cuda.is_available():
+    pytest.skip("needs a CUDA device", allow_module_level=True)
+
+from starling_b200 import _lib  # noqa: E402
+from starling_b200.engine import GraniteDims, GraniteEngine  # noqa: E402
+
+torch.set_grad_enabled(False)
+
+
+def _engine(vocab, fmt):
+    d = GraniteDims(hidden=512, n_q=4, n_kv=2, inter=1024, vocab=vocab, layers=1)
+    g = torch.Generator(device="cuda").manual_seed(7)
+    w = {}
+    for name, shape in [("embed_tokens.weight", (vocab, 512)), ("norm.weight", (512,)),
+                        ("layers.0.input_layernorm.weight", (512,)), ("layers.0.post_attention_layernorm.weight", (512,)),
+                        ("layers.0.self_attn.q_proj.weight", (512, 512)), ("layers.0.self_attn.k_proj.weight", (256, 512)),
+                        ("layers.0.self_attn.v_proj.weight", (256, 512)), ("layers.0.self_attn.o_proj.weight", (512, 512)),
+                        ("layers.0.mlp.gate_proj.weight", (1024, 512)), ("layers.0.mlp.up_proj.weight", (1024, 512)),
+                        ("layers.0.mlp.down_proj.weight", (512, 1024))]:
+        w[name] = (torch.randn(shape, generator=g, device="cuda") * (0.05 if len(shape) == 2 else 1.0)).to(torch.bfloat16)
+    return GraniteEngine(d, w, fmt, max_cache_len=64, max_batch=8)
+
+
+@pytest.mark.parametrize("vocab,fmt,batch", [(100352, "nvfp4", 1), (2051, "bf16", 1), (100352, "fp8", 2)])
+def test_static_scratch_matches_workspace_version(vocab, fmt, batch):
+    eng = _engine(vocab, fmt)
+    lib = eng.lib
+    ref = eng.new_state(batch, 1, _lib.SB_MODE_FIRST, out_steps=1)
+    new = eng.new_state(batch, 1, _lib.SB_MODE_FIRST, out_steps=1)
+    h = torch.randn(batch, 512, generator=torch.Generator(device="cuda").manual_seed(1), device="cuda").to(torch.bfloat16)
+    ref.hidden.copy_(h)
+    new.hidden.copy_(h)
+    s = _lib.current_stream()
+    _lib.check(lib.sb_lm_head_argmax(C.byref(eng.cmodel), C.byref(ref.c), 0, s), "sb_lm_head_argmax")
+    for call in range(2):  # two calls in a row share (and must re-clear) the fixed scratch
+        new.out_ids.zero_()
+        new.logits.zero_()
+        _lib.check(lib.sb_lm_head_argmax_static(C.byref(eng.cmodel), C.byref(new.c), 0, s),
+                   "sb_lm_head_argmax_static")
+        torch.cuda.synchronize()
+        # same kernel and configuration: results are identical (the tests'
+        # tolerance for a bf16 logit is one rounding step; here it is zero)
+        assert torch.equal(new.logits, ref.logits), f"call {call}: logits differ"
+        assert torch.equal(new.out_ids[:batch], ref.out_ids[:batch]), f"call {call}: token ids differ"
+        assert torch.equal(new.out_ids[:batch], ref.logits.float().argmax(-1))
+
+
+def test_static_scratch_rejects_too_many_rows():
+    eng = _engine(100352, "fp8")
+    rows = 32
+    assert eng.lib.sb_workspace_bytes(C.byref(eng.cmodel), rows) > 256 * 1024  # does not fit the fixed array
+    st = eng.new_state(1, rows, _lib.SB_MODE_VERIFY, out_steps=1)
+    rc = eng.lib.sb_lm_head_argmax_static(C.byref(eng.cmodel), C.byref(st.c), 0, _lib.current_stream())
+    assert rc == 1002  # SB_ERR_CONFIG
+    assert b"scratch" in eng.lib.sb_last_error()
