@@ -423,11 +423,15 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
+    # stdout carries exactly one JSON line: anything libraries print (NCCL's
+    # banner, warnings) goes to stderr instead
+    json_out = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     rank, world, local_rank = _env_int("RANK", 0), _env_int("WORLD_SIZE", 1), _env_int("LOCAL_RANK", 0)
     if args.impl == "reference":
         out = run_reference(args, rank, world)
         if out is not None:
-            print(json.dumps(out), flush=True)
+            print(json.dumps(out), file=json_out, flush=True)
         return
     if world > 1:
         import datetime
@@ -440,7 +444,7 @@ def main():
     try:
         out = run_native(args, rank, world, local_rank)
         if rank == 0:
-            print(json.dumps(out), flush=True)
+            print(json.dumps(out), file=json_out, flush=True)
     finally:
         if world > 1:
             import torch.distributed as dist

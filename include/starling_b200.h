@@ -94,6 +94,7 @@ typedef struct SbModel {
 #define SB_CTRL_SLOT 0    /* cache slot of token 0 of the next forward */
 #define SB_CTRL_PADLEN 1  /* padded prompt length T (right-padded batches) */
 #define SB_CTRL_ACCEPT 2  /* verify: accepted prefix length (output) */
+#define SB_CTRL_ERR 3     /* set to 1 by a kernel whose bounded wait expired (results invalid) */
 #define SB_CTRL_WORDS 8
 
 #define SB_MODE_DECODE 0  /* argmax -> out_ids[step], feed back to ids, slot += M */

@@ -14,6 +14,7 @@
 // captured once into a CUDA graph and replayed.
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 
 #include "attention.cuh"
@@ -63,7 +64,28 @@ static GemvParams base_params(const SbLinear& l, int m) {
   return p;
 }
 
+// STARLING_B200_GEMV=v1 forces the general kernel for every shape (A/B runs).
+static bool use_dec_kernel() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("STARLING_B200_GEMV");
+    v = (e && strcmp(e, "v1") == 0) ? 0 : 1;
+  }
+  return v == 1;
+}
+
+static bool dec_plan_for(int fmt, int n_tiles, int k, int m, DecPlan& pl) {
+  return use_dec_kernel() && gemv_dec_plan(fmt, n_tiles, k, m, pl);
+}
+
 static int run_gemv(GemvParams& p, int fmt, bool pdl, cudaStream_t s) {
+  DecPlan pl;
+  if (p.m <= 8 && dec_plan_for(fmt, p.n_tiles, p.k, p.m, pl)) {
+    const int rc = gemv_dec_launch(p, pl, fmt, pdl, s);
+    if (rc != 0) return fail(rc, "decode gemv launch (n=%d k=%d m=%d): %s", p.n, p.k, p.m,
+                             rc < 1000 ? cudaGetErrorString((cudaError_t)rc) : "config");
+    return 0;
+  }
   const GemvCfg c = gemv_pick(fmt, p.n_tiles * 16, p.k, p.m < 64 ? p.m : 64);
   p.rt = c.rt;
   p.ck = c.ck;
@@ -104,9 +126,14 @@ struct LmWork {
 
 static LmWork lm_work(const SbModel* md, int tokens, void* base) {
   const SbLinear& l = md->lm_head;
-  const GemvCfg c = gemv_pick(l.fmt, l.n_pad, l.k, tokens);
   LmWork w;
-  w.n_ctas = gemv_grid(c, l.n_pad / 16) / c.ck;
+  DecPlan pl;
+  if (tokens <= 8 && dec_plan_for(l.fmt, l.n_pad / 16, l.k, tokens, pl)) {
+    w.n_ctas = pl.n_ctas;
+  } else {
+    const GemvCfg c = gemv_pick(l.fmt, l.n_pad, l.k, tokens);
+    w.n_ctas = gemv_grid(c, l.n_pad / 16) / c.ck;
+  }
   const size_t pv = static_cast<size_t>(w.n_ctas) * tokens * 4;
   char* b = static_cast<char*>(base);
   w.counter = reinterpret_cast<int*>(b);

@@ -37,12 +37,6 @@ namespace sb {
 
 int kgroup_elems(int fmt) { return fmt == SB_FMT_NVFP4 ? 64 : (fmt == SB_FMT_BF16 ? 16 : 32); }
 
-template <int FMT>
-struct KG {
-  static constexpr int E = FMT == SB_FMT_NVFP4 ? 64 : (FMT == SB_FMT_BF16 ? 16 : 32);
-  static constexpr int KS = E / 16;  // mma k-steps per kgroup
-};
-
 template <int FMT, int NT>
 __device__ __forceinline__ void mma_rows(float (&acc)[NT][4], const uint32_t* A, const uint16_t* xs,
                                          int xs_stride, int kk, int M, int g, int c) {

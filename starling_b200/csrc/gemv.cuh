@@ -62,6 +62,20 @@ struct GemvParams {
   int64_t pad_id;
 };
 
+template <int FMT>
+struct KG {
+  static constexpr int E = FMT == SB_FMT_NVFP4 ? 64 : (FMT == SB_FMT_BF16 ? 16 : 32);  // K elements per kgroup
+  static constexpr int KS = E / 16;                                                  // mma k-steps per kgroup
+};
+
+// launch plan of the persistent decode GEMV (gemv_dec.cu)
+struct DecPlan {
+  int ksw, warps, slots, batch, n_ctas;
+  size_t smem;
+};
+bool gemv_dec_plan(int fmt, int n_tiles, int k, int m, DecPlan& pl);
+int gemv_dec_launch(const GemvParams& p, const DecPlan& pl, int fmt, bool pdl, cudaStream_t stream);
+
 struct GemvCfg {
   int rt, ck, warps, nt;
 };

@@ -1,0 +1,386 @@
+// Persistent decode GEMV for up to 8 token rows, sm_100a.
+//
+// Same operation and epilogues as k_gemv (gemv.cu), organised for the B=1
+// decode regime where every kernel is small and latency decides:
+//  * one wave: at most one CTA per SM, each owning a contiguous range of
+//    16-row tiles of the (packed) weight;
+//  * the CTA's weight tiles are streamed by bulk copies
+//    (cp.async.bulk ... mbarrier::complete_tx) into a ring of shared-memory
+//    slots; the first ring-full is issued BEFORE griddepcontrol.wait, so it
+//    overlaps the previous kernel;
+//  * the activation rows are read once per CTA, straight into registers in
+//    mma B-fragment order: warp w owns K slice w for every tile, so its
+//    fragments are reused across all of the CTA's tiles (no shared-memory
+//    staging).  RMSNorm statistics are combined across warps in a fixed
+//    order; each warp scales its slice by its own power of two (exact
+//    bf16 -> f16) and undoes it on its partial sums;
+//  * weight fragments are decoded from shared memory (e2m1 / e4m3 / int8 ->
+//    f16 with PTX cvt, NVFP4 block scale applied as an exact f16 product) into
+//    mma.m16n8k16 with fp32 accumulation; per-tile partials of all warps are
+//    reduced through shared memory in a fixed order, a batch of tiles at a
+//    time, while the other half of the ring is in flight.
+// Every wait on the ring is bounded; on expiry the kernel records an error
+// in ctrl[SB_CTRL_ERR] and carries on (results are then invalid) instead of
+// hanging.
+#include "gemv.cuh"
+#include "gemv_epi.cuh"
+
+namespace sb {
+
+namespace {
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t n) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(n) : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+// e2m1x2 bytes of one 32-bit word -> four f16x2 registers (PTX cvt, sm_100a)
+__device__ __forceinline__ void e2m1x8_to_h2x4(uint32_t w, uint32_t& a0, uint32_t& a1, uint32_t& a2, uint32_t& a3) {
+  asm("{\n .reg .b8 b0, b1, b2, b3;\n mov.b32 {b0, b1, b2, b3}, %4;\n"
+      " cvt.rn.f16x2.e2m1x2 %0, b0;\n cvt.rn.f16x2.e2m1x2 %1, b1;\n"
+      " cvt.rn.f16x2.e2m1x2 %2, b2;\n cvt.rn.f16x2.e2m1x2 %3, b3;\n}\n"
+      : "=r"(a0), "=r"(a1), "=r"(a2), "=r"(a3)
+      : "r"(w));
+}
+__device__ __forceinline__ void e4m3x4_to_h2x2(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  asm("{\n .reg .b16 l, h;\n mov.b32 {l, h}, %2;\n cvt.rn.f16x2.e4m3x2 %0, l;\n cvt.rn.f16x2.e4m3x2 %1, h;\n}\n"
+      : "=r"(lo), "=r"(hi)
+      : "r"(w));
+}
+
+constexpr long kSpinLimit = 1L << 26;  // bounded waits (~seconds), then flag an error
+
+__device__ __forceinline__ void ring_wait(uint64_t* bar, uint32_t parity, int32_t* err) {
+  long it = 0;
+  while (!mbar_try_wait(bar, parity)) {
+    if (++it > kSpinLimit) {
+      if (err) atomicExch(err, 1);
+      return;
+    }
+  }
+}
+
+}  // namespace
+
+template <int FMT, int KSW>
+__global__ void __launch_bounds__(512, 1) k_gemv_dec(const __grid_constant__ GemvParams p, int slots, int batch) {
+  constexpr int KGE = KG<FMT>::E;
+  constexpr int KS = KGE / 16;
+  constexpr int KPW = KSW / KS;  // kgroups per warp
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, W = blockDim.x >> 5;
+  const int g = lane >> 2, c = lane & 3;
+  const int M = p.m;  // 1..8
+  const int nct = gridDim.x;
+  const int base = p.n_tiles / nct, extra = p.n_tiles % nct;
+  const int ntile = base + (static_cast<int>(blockIdx.x) < extra ? 1 : 0);
+  const int t0 = static_cast<int>(blockIdx.x) * base + min(static_cast<int>(blockIdx.x), extra);
+
+  const uint32_t wbytes = static_cast<uint32_t>(p.kg_total) * 512u;
+  const uint32_t sbytes = FMT == SB_FMT_NVFP4 ? static_cast<uint32_t>(p.kg_total) * 64u : 0u;
+  const uint32_t slot_bytes = (wbytes + sbytes + 127u) & ~127u;
+  uint8_t* ring = smem;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(slots) * slot_bytes);
+  float* red = reinterpret_cast<float*>(bars + slots);   // [batch][W][16][M]
+  float* tot = red + static_cast<size_t>(batch) * W * 16 * M;  // [batch*16][M]
+  float* s_ss = tot + static_cast<size_t>(batch) * 16 * M;     // [16 warps][8 rows]
+  int* s_best = reinterpret_cast<int*>(s_ss + 128);           // [8]
+  float* s_bval = reinterpret_cast<float*>(s_best + 8);       // [8]
+  int* s_flag = reinterpret_cast<int*>(s_bval + 8);
+  int32_t* err = p.ctrl ? p.ctrl + SB_CTRL_ERR : nullptr;
+
+  auto issue_tile = [&](int j) {  // tile j of this CTA -> slot j % slots
+    uint8_t* dst = ring + static_cast<size_t>(j % slots) * slot_bytes;
+    uint64_t* bar = bars + (j % slots);
+    const size_t t = static_cast<size_t>(t0 + j);
+    mbar_expect_tx(bar, wbytes + sbytes);
+    const uint8_t* src = p.w + t * wbytes;
+    for (uint32_t o = 0; o < wbytes; o += 32768u) bulk_g2s(dst + o, src + o, min(32768u, wbytes - o), bar);
+    if (sbytes) bulk_g2s(dst + wbytes, p.scale + t * sbytes, sbytes, bar);
+  };
+
+  // ---- 1. start streaming this CTA's weights, then wait for the producer ----
+  if (tid == 0) {
+    for (int s = 0; s < slots; ++s) mbar_init(bars + s, 1);
+    mbar_fence_init();
+    for (int j = 0; j < min(slots, ntile); ++j) issue_tile(j);
+  }
+  __syncthreads();
+  pdl_wait();
+  pdl_launch();
+
+  // ---- 2. activation rows -> B fragments in registers ---------------------------
+  // lane (g, c) holds, for token n = min(g, M-1) and every k-step ks of this
+  // warp's slice, x[n][k0 + 16ks + 2c .. +1] and x[n][k0 + 16ks + 8 + 2c .. +1].
+  const int Kw = KSW * 16;  // K elements per warp
+  const int k0 = warp * Kw;
+  const int n = g < M ? g : M - 1;
+  const uint16_t* src;
+  if (p.pro == PRO_EMBED) {
+    int64_t id = p.ids[n];
+    id = id < 0 ? 0 : (id >= p.embed_rows ? p.embed_rows - 1 : id);
+    src = p.embed + static_cast<size_t>(id) * p.k;
+  } else {
+    src = p.x + static_cast<size_t>(n) * p.k;
+  }
+  auto load4 = [&](const uint16_t* base, int ks, float* f) {
+    const uint32_t u0 = *reinterpret_cast<const uint32_t*>(base + k0 + ks * 16 + 2 * c);
+    const uint32_t u1 = *reinterpret_cast<const uint32_t*>(base + k0 + ks * 16 + 8 + 2 * c);
+    f[0] = __uint_as_float(u0 << 16);
+    f[1] = __uint_as_float(u0 & 0xffff0000u);
+    f[2] = __uint_as_float(u1 << 16);
+    f[3] = __uint_as_float(u1 & 0xffff0000u);
+  };
+  const bool embed = p.pro == PRO_EMBED;
+  if (embed && blockIdx.x == 0 && p.hidden_out) {  // the residual stream of layer 0
+    for (int i = tid; i < M * p.k; i += blockDim.x) {
+      const int r = i / p.k, k = i % p.k;
+      int64_t id = p.ids[r];
+      id = id < 0 ? 0 : (id >= p.embed_rows ? p.embed_rows - 1 : id);
+      p.hidden_out[static_cast<size_t>(r) * p.k + k] =
+          f_to_bf16_bits(bf(u16_to_f(p.embed[static_cast<size_t>(id) * p.k + k]) * p.emb_mult));
+    }
+  }
+  float rstd = 1.f;
+  if (p.pro != PRO_NONE) {  // RMSNorm: full-row mean of squares, warps combined in a fixed order
+    float ss = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < KSW; ++ks) {
+      float f[4];
+      load4(src, ks, f);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float h = embed ? bf(f[e] * p.emb_mult) : f[e];  // embed_tokens(ids) * 12 (llm_mega.py:514)
+        ss += h * h;
+      }
+    }
+    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+    if (c == 0) s_ss[warp * 8 + g] = ss;
+    __syncthreads();
+    float tsum = 0.f;
+    for (int q = 0; q < W; ++q) tsum += s_ss[q * 8 + g];
+    rstd = 1.f / sqrtf(tsum / static_cast<float>(p.k) + p.eps);
+  }
+  // normalised bf16 activations, packed as bf16x2 in B-fragment order
+  uint32_t bfr[KSW][2];
+  float am = 0.f;
+#pragma unroll
+  for (int ks = 0; ks < KSW; ++ks) {
+    float f[4];
+    load4(src, ks, f);
+    if (p.pro != PRO_NONE) {
+      float wn[4];
+      load4(p.norm_w, ks, wn);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float h = embed ? bf(f[e] * p.emb_mult) : f[e];
+        f[e] = bf(wn[e] * bf(h * rstd));  // weight * bf16(x * rstd)  (modeling_granite.py:192-197)
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) am = fmaxf(am, fabsf(f[e]));
+    bfr[ks][0] = static_cast<uint32_t>(f_to_bf16_bits(f[0])) | (static_cast<uint32_t>(f_to_bf16_bits(f[1])) << 16);
+    bfr[ks][1] = static_cast<uint32_t>(f_to_bf16_bits(f[2])) | (static_cast<uint32_t>(f_to_bf16_bits(f[3])) << 16);
+  }
+  int shift = 0;
+  if (FMT != SB_FMT_BF16) {  // -> f16 scaled by this warp's power of two (exact)
+    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
+    int e2 = 0;
+    if (am > 0.f) frexpf(am, &e2);
+    shift = 15 - e2;  // slice max * 2^shift in [2^14, 2^15)
+#pragma unroll
+    for (int ks = 0; ks < KSW; ++ks)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t u = bfr[ks][h];
+        __half2 hh = __floats2half2_rn(ldexpf(__uint_as_float(u << 16), shift),
+                                       ldexpf(__uint_as_float(u & 0xffff0000u), shift));
+        bfr[ks][h] = *reinterpret_cast<uint32_t*>(&hh);
+      }
+  }
+  // output column j of the D fragment is token j: the lanes that own columns
+  // 2c and 2c+1 need those tokens' shifts (owned by lanes 4*(2c) and 4*(2c+1))
+  const int sh0 = __shfl_sync(0xffffffffu, shift, min(2 * c, M - 1) * 4);
+  const int sh1 = __shfl_sync(0xffffffffu, shift, min(2 * c + 1, M - 1) * 4);
+
+  // ---- 3. tiles: decode from the ring, tensor cores, batched reduction ----------
+  for (int jb = 0; jb < ntile; jb += batch) {
+    const int nb = min(batch, ntile - jb);
+    for (int jj = 0; jj < nb; ++jj) {
+      const int j = jb + jj;
+      uint8_t* slot = ring + static_cast<size_t>(j % slots) * slot_bytes;
+      ring_wait(bars + (j % slots), static_cast<uint32_t>((j / slots) & 1), err);
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int q = 0; q < KPW; ++q) {
+        const int kg = warp * KPW + q;
+        const uint4 a = *reinterpret_cast<const uint4*>(slot + static_cast<size_t>(kg) * 512 + lane * 16);
+        if constexpr (FMT == SB_FMT_NVFP4) {
+          const uint2 s = *reinterpret_cast<const uint2*>(slot + wbytes + static_cast<size_t>(kg) * 64 + g * 8);
+          const uint32_t wv[4] = {a.x, a.y, a.z, a.w};
+          uint32_t sc[4];  // f16x2 {scale(g), scale(g+8)} for k-steps 0..3
+          e4m3x4_to_h2x2(s.x, sc[0], sc[1]);
+          e4m3x4_to_h2x2(s.y, sc[2], sc[3]);
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            uint32_t A[4];
+            e2m1x8_to_h2x4(wv[t], A[0], A[1], A[2], A[3]);
+            const uint32_t slo = __byte_perm(sc[t], 0, 0x1010), shi = __byte_perm(sc[t], 0, 0x3232);
+            A[0] = hmul2_u32(A[0], slo);
+            A[2] = hmul2_u32(A[2], slo);
+            A[1] = hmul2_u32(A[1], shi);
+            A[3] = hmul2_u32(A[3], shi);
+            mma_f16(acc, A, bfr[q * 4 + t][0], bfr[q * 4 + t][1]);
+          }
+        } else if constexpr (FMT == SB_FMT_FP8) {
+          uint32_t A[4];
+          e4m3x4_to_h2x2(a.x, A[0], A[1]);
+          e4m3x4_to_h2x2(a.y, A[2], A[3]);
+          mma_f16(acc, A, bfr[q * 2][0], bfr[q * 2][1]);
+          e4m3x4_to_h2x2(a.z, A[0], A[1]);
+          e4m3x4_to_h2x2(a.w, A[2], A[3]);
+          mma_f16(acc, A, bfr[q * 2 + 1][0], bfr[q * 2 + 1][1]);
+        } else if constexpr (FMT == SB_FMT_INT8) {
+          uint32_t A[4];
+          i8x4_to_h2x2(a.x, A[0], A[1]);
+          i8x4_to_h2x2(a.y, A[2], A[3]);
+          mma_f16(acc, A, bfr[q * 2][0], bfr[q * 2][1]);
+          i8x4_to_h2x2(a.z, A[0], A[1]);
+          i8x4_to_h2x2(a.w, A[2], A[3]);
+          mma_f16(acc, A, bfr[q * 2 + 1][0], bfr[q * 2 + 1][1]);
+        } else {
+          const uint32_t A[4] = {a.x, a.y, a.z, a.w};
+          mma_bf16(acc, A, bfr[q][0], bfr[q][1]);
+        }
+      }
+      // undo this warp's activation scale, store the partial of tile jj
+      float* rw = red + (static_cast<size_t>(jj) * W + warp) * 16 * M;
+      const int col = 2 * c;
+      if (col < M) {
+        rw[g * M + col] = FMT == SB_FMT_BF16 ? acc[0] : ldexpf(acc[0], -sh0);
+        rw[(g + 8) * M + col] = FMT == SB_FMT_BF16 ? acc[2] : ldexpf(acc[2], -sh0);
+      }
+      if (col + 1 < M) {
+        rw[g * M + col + 1] = FMT == SB_FMT_BF16 ? acc[1] : ldexpf(acc[1], -sh1);
+        rw[(g + 8) * M + col + 1] = FMT == SB_FMT_BF16 ? acc[3] : ldexpf(acc[3], -sh1);
+      }
+    }
+    __syncthreads();  // all warps done with this batch's slots and partials
+    // refill the slots of this batch with the tiles one ring further on
+    if (tid == 0)
+      for (int jj = 0; jj < nb; ++jj)
+        if (jb + jj + slots < ntile) issue_tile(jb + jj + slots);
+    // reduce over warps in a fixed order
+    for (int i = tid; i < nb * 16 * M; i += blockDim.x) {
+      const int jj = i / (16 * M), rm = i % (16 * M);
+      float sum = 0.f;
+      for (int q = 0; q < W; ++q) sum += red[(static_cast<size_t>(jj) * W + q) * 16 * M + rm];
+      tot[i] = sum;
+    }
+    __syncthreads();
+    gemv_epilogue<FMT>(p, tot, (t0 + jb) * 16, nb * 16, M, s_best, s_bval, jb == 0, jb + nb >= ntile);
+    __syncthreads();
+  }
+  gemv_argmax_finish(p, s_best, s_bval, M, ntile > 0, s_flag);
+}
+
+// ---- host side ------------------------------------------------------------------
+static const int kSMs = 148;
+static const size_t kDecSmem = 220 * 1024;
+
+bool gemv_dec_plan(int fmt, int n_tiles, int k, int m, DecPlan& pl) {
+  if (m < 1 || m > 8) return false;
+  const int kge = kgroup_elems(fmt);
+  const int ksteps = k / 16;
+  int ksw = 16;
+  if (ksteps % ksw) return false;
+  if (ksteps / ksw > 16) ksw = 32;
+  if (ksteps % ksw) return false;
+  const int W = ksteps / ksw;
+  if (W < 1 || W > 16 || (ksw * 16) % kge) return false;
+  const size_t wbytes = static_cast<size_t>(k / kge) * 512;
+  const size_t sbytes = fmt == SB_FMT_NVFP4 ? static_cast<size_t>(k / 64) * 64 : 0;
+  const size_t slot = (wbytes + sbytes + 127) & ~size_t(127);
+  const int n_ctas = n_tiles < kSMs ? n_tiles : kSMs;
+  const int per = (n_tiles + n_ctas - 1) / n_ctas;
+  int slots = static_cast<int>(160 * 1024 / slot);
+  if (slots > 2 * per) slots = 2 * per;
+  if (slots > 16) slots = 16;
+  if (slots < 2) return false;
+  int batch = slots / 2;
+  // reduction buffers: batch * (W + 1) * 16 * m floats
+  while (batch > 1 && static_cast<size_t>(batch) * (W + 1) * 16 * m * 4 > 48 * 1024) --batch;
+  const size_t smem = slot * slots + 8 * slots + static_cast<size_t>(batch) * (W + 1) * 16 * m * 4 + 128 * 4 + 64;
+  if (smem > kDecSmem) return false;
+  pl.ksw = ksw;
+  pl.warps = W;
+  pl.slots = slots;
+  pl.batch = batch;
+  pl.n_ctas = n_ctas;
+  pl.smem = smem;
+  return true;
+}
+
+template <int FMT, int KSW>
+static int dec_launch_t(const GemvParams& p, const DecPlan& pl, bool pdl, cudaStream_t stream) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static unsigned configured = 0;
+  if (!(configured & (1u << dev))) {
+    cudaError_t e = cudaFuncSetAttribute(k_gemv_dec<FMT, KSW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kDecSmem));
+    if (e != cudaSuccess) return e;
+    configured |= 1u << dev;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(pl.n_ctas);
+  cfg.blockDim = dim3(pl.warps * 32);
+  cfg.dynamicSmemBytes = pl.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k_gemv_dec<FMT, KSW>, p, pl.slots, pl.batch);
+}
+
+template <int FMT>
+static int dec_launch_f(const GemvParams& p, const DecPlan& pl, bool pdl, cudaStream_t s) {
+  return pl.ksw == 16 ? dec_launch_t<FMT, 16>(p, pl, pdl, s) : dec_launch_t<FMT, 32>(p, pl, pdl, s);
+}
+
+int gemv_dec_launch(const GemvParams& p, const DecPlan& pl, int fmt, bool pdl, cudaStream_t s) {
+  switch (fmt) {
+    case SB_FMT_BF16: return dec_launch_f<SB_FMT_BF16>(p, pl, pdl, s);
+    case SB_FMT_FP8: return dec_launch_f<SB_FMT_FP8>(p, pl, pdl, s);
+    case SB_FMT_INT8: return dec_launch_f<SB_FMT_INT8>(p, pl, pdl, s);
+    case SB_FMT_NVFP4: return dec_launch_f<SB_FMT_NVFP4>(p, pl, pdl, s);
+  }
+  return SB_ERR_ARG;
+}
+
+}  // namespace sb
