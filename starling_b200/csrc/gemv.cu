@@ -102,22 +102,6 @@ __device__ __forceinline__ void process_kgroup(const uint4 a, const uint2 s, int
   }
 }
 
-__device__ __forceinline__ void unpack8(const uint4 v, float* f) {
-  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    f[2 * i] = __uint_as_float(w[i] << 16);
-    f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
-  }
-}
-__device__ __forceinline__ uint4 pack8(const float* f) {
-  uint32_t w[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i)
-    w[i] = static_cast<uint32_t>(f_to_bf16_bits(f[2 * i])) | (static_cast<uint32_t>(f_to_bf16_bits(f[2 * i + 1])) << 16);
-  return make_uint4(w[0], w[1], w[2], w[3]);
-}
-
 template <int FMT, int NT>
 __global__ void __launch_bounds__(512) k_gemv(const __grid_constant__ GemvParams p) {
   extern __shared__ __align__(16) uint8_t smem[];

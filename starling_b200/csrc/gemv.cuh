@@ -73,6 +73,27 @@ struct DecPlan {
   int ksw, warps, slots, batch, n_ctas;
   size_t smem;
 };
+// Shared-memory layout of the decode GEMV, computed identically on the host
+// (allocation size) and in the kernel (offsets).  All offsets 16-aligned.
+struct DecLayout {
+  size_t slot_bytes, bars, red, tot, ss, shift, best, bval, flag, xs, total;
+};
+__host__ __device__ inline DecLayout dec_layout(size_t tile_bytes, int slots, int batch, int warps, int m, int kw) {
+  auto up16 = [](size_t x) { return (x + 15) & ~size_t(15); };
+  DecLayout L;
+  L.slot_bytes = (tile_bytes + 127) & ~size_t(127);
+  L.bars = L.slot_bytes * slots;
+  L.red = up16(L.bars + 8 * static_cast<size_t>(slots));
+  L.tot = up16(L.red + static_cast<size_t>(batch) * warps * 16 * m * 4);
+  L.ss = up16(L.tot + static_cast<size_t>(batch) * 16 * m * 4);
+  L.shift = up16(L.ss + 128 * 4);
+  L.best = up16(L.shift + 128 * 4);
+  L.bval = up16(L.best + 8 * 4);
+  L.flag = up16(L.bval + 8 * 4);
+  L.xs = up16(L.flag + 16);  // [warps][m][kw + 8] activation slices
+  L.total = up16(L.xs + static_cast<size_t>(warps) * m * (kw + 8) * 2);
+  return L;
+}
 bool gemv_dec_plan(int fmt, int n_tiles, int k, int m, DecPlan& pl);
 int gemv_dec_launch(const GemvParams& p, const DecPlan& pl, int fmt, bool pdl, cudaStream_t stream);
 

@@ -99,15 +99,16 @@ __global__ void __launch_bounds__(512, 1) k_gemv_dec(const __grid_constant__ Gem
 
   const uint32_t wbytes = static_cast<uint32_t>(p.kg_total) * 512u;
   const uint32_t sbytes = FMT == SB_FMT_NVFP4 ? static_cast<uint32_t>(p.kg_total) * 64u : 0u;
-  const uint32_t slot_bytes = (wbytes + sbytes + 127u) & ~127u;
+  const DecLayout L = dec_layout(wbytes + sbytes, slots, batch, W, M, KSW * 16);
+  const uint32_t slot_bytes = static_cast<uint32_t>(L.slot_bytes);
   uint8_t* ring = smem;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(slots) * slot_bytes);
-  float* red = reinterpret_cast<float*>(bars + slots);   // [batch][W][16][M]
-  float* tot = red + static_cast<size_t>(batch) * W * 16 * M;  // [batch*16][M]
-  float* s_ss = tot + static_cast<size_t>(batch) * 16 * M;     // [16 warps][8 rows]
-  int* s_best = reinterpret_cast<int*>(s_ss + 128);           // [8]
-  float* s_bval = reinterpret_cast<float*>(s_best + 8);       // [8]
-  int* s_flag = reinterpret_cast<int*>(s_bval + 8);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
+  float* red = reinterpret_cast<float*>(smem + L.red);     // [batch][W][16][M]
+  float* tot = reinterpret_cast<float*>(smem + L.tot);     // [batch*16][M]
+  float* s_ss = reinterpret_cast<float*>(smem + L.ss);     // [16 warps][8 rows]
+  int* s_best = reinterpret_cast<int*>(smem + L.best);     // [8]
+  float* s_bval = reinterpret_cast<float*>(smem + L.bval); // [8]
+  int* s_flag = reinterpret_cast<int*>(smem + L.flag);
   int32_t* err = p.ctrl ? p.ctrl + SB_CTRL_ERR : nullptr;
 
   auto issue_tile = [&](int j) {  // tile j of this CTA -> slot j % slots
@@ -130,120 +131,117 @@ __global__ void __launch_bounds__(512, 1) k_gemv_dec(const __grid_constant__ Gem
   pdl_wait();
   pdl_launch();
 
-  // ---- 2. activation rows -> B fragments in registers ---------------------------
-  // lane (g, c) holds, for token n = min(g, M-1) and every k-step ks of this
-  // warp's slice, x[n][k0 + 16ks + 2c .. +1] and x[n][k0 + 16ks + 8 + 2c .. +1].
+  // ---- 2. activation rows -> this warp's K slice, f16 (or bf16), in shared memory
+  // Warp w owns K slice w for every tile of the CTA.  Compact, rolled loops:
+  // this code runs once per launch, so instruction fetch (not ALU) decides.
   const int Kw = KSW * 16;  // K elements per warp
   const int k0 = warp * Kw;
-  const int n = g < M ? g : M - 1;
-  const uint16_t* src;
-  if (p.pro == PRO_EMBED) {
-    int64_t id = p.ids[n];
-    id = id < 0 ? 0 : (id >= p.embed_rows ? p.embed_rows - 1 : id);
-    src = p.embed + static_cast<size_t>(id) * p.k;
-  } else {
-    src = p.x + static_cast<size_t>(n) * p.k;
-  }
-  auto load4 = [&](const uint16_t* base, int ks, float* f) {
-    const uint32_t u0 = *reinterpret_cast<const uint32_t*>(base + k0 + ks * 16 + 2 * c);
-    const uint32_t u1 = *reinterpret_cast<const uint32_t*>(base + k0 + ks * 16 + 8 + 2 * c);
-    f[0] = __uint_as_float(u0 << 16);
-    f[1] = __uint_as_float(u0 & 0xffff0000u);
-    f[2] = __uint_as_float(u1 << 16);
-    f[3] = __uint_as_float(u1 & 0xffff0000u);
-  };
+  const int xstride = Kw + 8;
+  uint16_t* xw = reinterpret_cast<uint16_t*>(smem + L.xs) + static_cast<size_t>(warp) * M * xstride;
+  int* s_shift = reinterpret_cast<int*>(smem + L.shift);  // [16 warps][8 rows]
   const bool embed = p.pro == PRO_EMBED;
+  auto row_src = [&](int m) -> const uint16_t* {
+    if (embed) {
+      int64_t id = p.ids[m];
+      id = id < 0 ? 0 : (id >= p.embed_rows ? p.embed_rows - 1 : id);  // never read outside the table
+      return p.embed + static_cast<size_t>(id) * p.k;
+    }
+    return p.x + static_cast<size_t>(m) * p.k;
+  };
   if (embed && blockIdx.x == 0 && p.hidden_out) {  // the residual stream of layer 0
     for (int i = tid; i < M * p.k; i += blockDim.x) {
       const int r = i / p.k, k = i % p.k;
-      int64_t id = p.ids[r];
-      id = id < 0 ? 0 : (id >= p.embed_rows ? p.embed_rows - 1 : id);
-      p.hidden_out[static_cast<size_t>(r) * p.k + k] =
-          f_to_bf16_bits(bf(u16_to_f(p.embed[static_cast<size_t>(id) * p.k + k]) * p.emb_mult));
+      p.hidden_out[static_cast<size_t>(r) * p.k + k] = f_to_bf16_bits(bf(u16_to_f(row_src(r)[k]) * p.emb_mult));
     }
   }
-  float rstd = 1.f;
-  if (p.pro != PRO_NONE) {  // RMSNorm: full-row mean of squares, warps combined in a fixed order
-    float ss = 0.f;
+  if (p.pro != PRO_NONE) {  // RMSNorm statistics: full-row sum of squares, warps combined in a fixed order
+    for (int m = 0; m < M; ++m) {
+      const uint16_t* src = row_src(m);
+      float ss = 0.f;
+      for (int k = lane * 8; k < Kw; k += 256) {
+        float f[8];
+        unpack8(*reinterpret_cast<const uint4*>(src + k0 + k), f);
 #pragma unroll
-    for (int ks = 0; ks < KSW; ++ks) {
-      float f[4];
-      load4(src, ks, f);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float h = embed ? bf(f[e] * p.emb_mult) : f[e];  // embed_tokens(ids) * 12 (llm_mega.py:514)
-        ss += h * h;
+        for (int e = 0; e < 8; ++e) {
+          const float h = embed ? bf(f[e] * p.emb_mult) : f[e];  // embed_tokens(ids) * 12 (llm_mega.py:514)
+          ss += h * h;
+        }
       }
+      ss = warp_sum(ss);
+      if (lane == 0) s_ss[warp * 8 + m] = ss;
     }
-    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-    ss += __shfl_xor_sync(0xffffffffu, ss, 2);
-    if (c == 0) s_ss[warp * 8 + g] = ss;
     __syncthreads();
-    float tsum = 0.f;
-    for (int q = 0; q < W; ++q) tsum += s_ss[q * 8 + g];
-    rstd = 1.f / sqrtf(tsum / static_cast<float>(p.k) + p.eps);
   }
-  // normalised bf16 activations, packed as bf16x2 in B-fragment order
-  uint32_t bfr[KSW][2];
-  float am = 0.f;
-#pragma unroll
-  for (int ks = 0; ks < KSW; ++ks) {
-    float f[4];
-    load4(src, ks, f);
+  for (int m = 0; m < M; ++m) {
+    const uint16_t* src = row_src(m);
+    float rstd = 1.f;
     if (p.pro != PRO_NONE) {
-      float wn[4];
-      load4(p.norm_w, ks, wn);
+      float tsum = 0.f;
+      for (int q = 0; q < W; ++q) tsum += s_ss[q * 8 + m];
+      rstd = 1.f / sqrtf(tsum / static_cast<float>(p.k) + p.eps);
+    }
+    float am = 0.f;
+    for (int k = lane * 8; k < Kw; k += 256) {
+      float f[8];
+      unpack8(*reinterpret_cast<const uint4*>(src + k0 + k), f);
+      if (p.pro != PRO_NONE) {
+        float wn[8];
+        unpack8(*reinterpret_cast<const uint4*>(p.norm_w + k0 + k), wn);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float h = embed ? bf(f[e] * p.emb_mult) : f[e];
-        f[e] = bf(wn[e] * bf(h * rstd));  // weight * bf16(x * rstd)  (modeling_granite.py:192-197)
+        for (int e = 0; e < 8; ++e) {
+          const float h = embed ? bf(f[e] * p.emb_mult) : f[e];
+          f[e] = bf(wn[e] * bf(h * rstd));  // weight * bf16(x * rstd)  (modeling_granite.py:192-197)
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) am = fmaxf(am, fabsf(f[e]));
+      *reinterpret_cast<uint4*>(xw + m * xstride + k) = pack8(f);
+    }
+    int shift = 0;
+    if (FMT != SB_FMT_BF16) {  // -> f16 scaled by a power of two per (warp, row): exact
+      am = warp_max(am);
+      int e2 = 0;
+      if (am > 0.f) frexpf(am, &e2);
+      shift = 15 - e2;  // slice max * 2^shift in [2^14, 2^15)
+      for (int k = lane * 8; k < Kw; k += 256) {  // same lane wrote these elements
+        float f[8];
+        unpack8(*reinterpret_cast<const uint4*>(xw + m * xstride + k), f);
+        uint32_t h[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          __half2 hh = __floats2half2_rn(ldexpf(f[2 * e], shift), ldexpf(f[2 * e + 1], shift));
+          h[e] = *reinterpret_cast<uint32_t*>(&hh);
+        }
+        *reinterpret_cast<uint4*>(xw + m * xstride + k) = make_uint4(h[0], h[1], h[2], h[3]);
       }
     }
-#pragma unroll
-    for (int e = 0; e < 4; ++e) am = fmaxf(am, fabsf(f[e]));
-    bfr[ks][0] = static_cast<uint32_t>(f_to_bf16_bits(f[0])) | (static_cast<uint32_t>(f_to_bf16_bits(f[1])) << 16);
-    bfr[ks][1] = static_cast<uint32_t>(f_to_bf16_bits(f[2])) | (static_cast<uint32_t>(f_to_bf16_bits(f[3])) << 16);
+    if (lane == 0) s_shift[warp * 8 + m] = shift;
   }
-  int shift = 0;
-  if (FMT != SB_FMT_BF16) {  // -> f16 scaled by this warp's power of two (exact)
-    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
-    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
-    int e2 = 0;
-    if (am > 0.f) frexpf(am, &e2);
-    shift = 15 - e2;  // slice max * 2^shift in [2^14, 2^15)
-#pragma unroll
-    for (int ks = 0; ks < KSW; ++ks)
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const uint32_t u = bfr[ks][h];
-        __half2 hh = __floats2half2_rn(ldexpf(__uint_as_float(u << 16), shift),
-                                       ldexpf(__uint_as_float(u & 0xffff0000u), shift));
-        bfr[ks][h] = *reinterpret_cast<uint32_t*>(&hh);
-      }
-  }
-  // output column j of the D fragment is token j: the lanes that own columns
-  // 2c and 2c+1 need those tokens' shifts (owned by lanes 4*(2c) and 4*(2c+1))
-  const int sh0 = __shfl_sync(0xffffffffu, shift, min(2 * c, M - 1) * 4);
-  const int sh1 = __shfl_sync(0xffffffffu, shift, min(2 * c + 1, M - 1) * 4);
+  __syncwarp();
+  // D-fragment column j is token j: this lane's columns 2c and 2c+1
+  const int sh0 = s_shift[warp * 8 + min(2 * c, M - 1)];
+  const int sh1 = s_shift[warp * 8 + min(2 * c + 1, M - 1)];
+  const uint16_t* xb = xw + (g < M ? g : M - 1) * xstride + 2 * c;  // B fragment base of this lane
 
   // ---- 3. tiles: decode from the ring, tensor cores, batched reduction ----------
   for (int jb = 0; jb < ntile; jb += batch) {
     const int nb = min(batch, ntile - jb);
     for (int jj = 0; jj < nb; ++jj) {
       const int j = jb + jj;
-      uint8_t* slot = ring + static_cast<size_t>(j % slots) * slot_bytes;
+      const uint8_t* slot = ring + static_cast<size_t>(j % slots) * slot_bytes;
       ring_wait(bars + (j % slots), static_cast<uint32_t>((j / slots) & 1), err);
       float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
+#pragma unroll 1
       for (int q = 0; q < KPW; ++q) {
         const int kg = warp * KPW + q;
         const uint4 a = *reinterpret_cast<const uint4*>(slot + static_cast<size_t>(kg) * 512 + lane * 16);
+        const uint16_t* xq = xb + q * KGE;
         if constexpr (FMT == SB_FMT_NVFP4) {
-          const uint2 s = *reinterpret_cast<const uint2*>(slot + wbytes + static_cast<size_t>(kg) * 64 + g * 8);
+          const uint2 s2 = *reinterpret_cast<const uint2*>(slot + wbytes + static_cast<size_t>(kg) * 64 + g * 8);
           const uint32_t wv[4] = {a.x, a.y, a.z, a.w};
-          uint32_t sc[4];  // f16x2 {scale(g), scale(g+8)} for k-steps 0..3
-          e4m3x4_to_h2x2(s.x, sc[0], sc[1]);
-          e4m3x4_to_h2x2(s.y, sc[2], sc[3]);
+          uint32_t sc[4];  // f16x2 {scale(row g), scale(row g+8)} for k-steps 0..3
+          e4m3x4_to_h2x2(s2.x, sc[0], sc[1]);
+          e4m3x4_to_h2x2(s2.y, sc[2], sc[3]);
 #pragma unroll
           for (int t = 0; t < 4; ++t) {
             uint32_t A[4];
@@ -253,39 +251,39 @@ __global__ void __launch_bounds__(512, 1) k_gemv_dec(const __grid_constant__ Gem
             A[2] = hmul2_u32(A[2], slo);
             A[1] = hmul2_u32(A[1], shi);
             A[3] = hmul2_u32(A[3], shi);
-            mma_f16(acc, A, bfr[q * 4 + t][0], bfr[q * 4 + t][1]);
+            mma_f16(acc, A, *reinterpret_cast<const uint32_t*>(xq + t * 16),
+                    *reinterpret_cast<const uint32_t*>(xq + t * 16 + 8));
           }
-        } else if constexpr (FMT == SB_FMT_FP8) {
-          uint32_t A[4];
-          e4m3x4_to_h2x2(a.x, A[0], A[1]);
-          e4m3x4_to_h2x2(a.y, A[2], A[3]);
-          mma_f16(acc, A, bfr[q * 2][0], bfr[q * 2][1]);
-          e4m3x4_to_h2x2(a.z, A[0], A[1]);
-          e4m3x4_to_h2x2(a.w, A[2], A[3]);
-          mma_f16(acc, A, bfr[q * 2 + 1][0], bfr[q * 2 + 1][1]);
-        } else if constexpr (FMT == SB_FMT_INT8) {
-          uint32_t A[4];
-          i8x4_to_h2x2(a.x, A[0], A[1]);
-          i8x4_to_h2x2(a.y, A[2], A[3]);
-          mma_f16(acc, A, bfr[q * 2][0], bfr[q * 2][1]);
-          i8x4_to_h2x2(a.z, A[0], A[1]);
-          i8x4_to_h2x2(a.w, A[2], A[3]);
-          mma_f16(acc, A, bfr[q * 2 + 1][0], bfr[q * 2 + 1][1]);
+        } else if constexpr (FMT == SB_FMT_FP8 || FMT == SB_FMT_INT8) {
+          const uint32_t wv[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            uint32_t A[4];
+            if constexpr (FMT == SB_FMT_FP8) {
+              e4m3x4_to_h2x2(wv[2 * t], A[0], A[1]);
+              e4m3x4_to_h2x2(wv[2 * t + 1], A[2], A[3]);
+            } else {
+              i8x4_to_h2x2(wv[2 * t], A[0], A[1]);
+              i8x4_to_h2x2(wv[2 * t + 1], A[2], A[3]);
+            }
+            mma_f16(acc, A, *reinterpret_cast<const uint32_t*>(xq + t * 16),
+                    *reinterpret_cast<const uint32_t*>(xq + t * 16 + 8));
+          }
         } else {
           const uint32_t A[4] = {a.x, a.y, a.z, a.w};
-          mma_bf16(acc, A, bfr[q][0], bfr[q][1]);
+          mma_bf16(acc, A, *reinterpret_cast<const uint32_t*>(xq), *reinterpret_cast<const uint32_t*>(xq + 8));
         }
       }
       // undo this warp's activation scale, store the partial of tile jj
       float* rw = red + (static_cast<size_t>(jj) * W + warp) * 16 * M;
       const int col = 2 * c;
       if (col < M) {
-        rw[g * M + col] = FMT == SB_FMT_BF16 ? acc[0] : ldexpf(acc[0], -sh0);
-        rw[(g + 8) * M + col] = FMT == SB_FMT_BF16 ? acc[2] : ldexpf(acc[2], -sh0);
+        rw[g * M + col] = ldexpf(acc[0], -sh0);
+        rw[(g + 8) * M + col] = ldexpf(acc[2], -sh0);
       }
       if (col + 1 < M) {
-        rw[g * M + col + 1] = FMT == SB_FMT_BF16 ? acc[1] : ldexpf(acc[1], -sh1);
-        rw[(g + 8) * M + col + 1] = FMT == SB_FMT_BF16 ? acc[3] : ldexpf(acc[3], -sh1);
+        rw[g * M + col + 1] = ldexpf(acc[1], -sh1);
+        rw[(g + 8) * M + col + 1] = ldexpf(acc[3], -sh1);
       }
     }
     __syncthreads();  // all warps done with this batch's slots and partials
@@ -323,7 +321,7 @@ bool gemv_dec_plan(int fmt, int n_tiles, int k, int m, DecPlan& pl) {
   if (W < 1 || W > 16 || (ksw * 16) % kge) return false;
   const size_t wbytes = static_cast<size_t>(k / kge) * 512;
   const size_t sbytes = fmt == SB_FMT_NVFP4 ? static_cast<size_t>(k / 64) * 64 : 0;
-  const size_t slot = (wbytes + sbytes + 127) & ~size_t(127);
+  const size_t slot = (wbytes + sbytes + 127) & ~size_t(127);  // = dec_layout().slot_bytes
   const int n_ctas = n_tiles < kSMs ? n_tiles : kSMs;
   const int per = (n_tiles + n_ctas - 1) / n_ctas;
   int slots = static_cast<int>(160 * 1024 / slot);
@@ -333,7 +331,7 @@ bool gemv_dec_plan(int fmt, int n_tiles, int k, int m, DecPlan& pl) {
   int batch = slots / 2;
   // reduction buffers: batch * (W + 1) * 16 * m floats
   while (batch > 1 && static_cast<size_t>(batch) * (W + 1) * 16 * m * 4 > 48 * 1024) --batch;
-  const size_t smem = slot * slots + 8 * slots + static_cast<size_t>(batch) * (W + 1) * 16 * m * 4 + 128 * 4 + 64;
+  const size_t smem = dec_layout(wbytes + sbytes, slots, batch, W, m, ksw * 16).total;
   if (smem > kDecSmem) return false;
   pl.ksw = ksw;
   pl.warps = W;
