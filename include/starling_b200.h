@@ -47,6 +47,13 @@ typedef void* sb_stream_t; /* a cudaStream_t */
  * 16 bytes are its mma.m16n8k16 A-fragments for those K elements.
  * scale: fp8/int8 -> float[n_pad]; nvfp4 -> e4m3 bytes
  * [n_pad/16][k/64][8 row pairs][8] ; bf16 -> NULL.
+ *
+ * w_tc (optional, fp8 and bf16): a second copy of the same rows (same packed
+ * row order, same scale) for the tcgen05 GEMM that serves 9..128 token rows:
+ * [ceil(n/128) tiles][k*eb/128 K blocks][16 row groups][8 K chunks][8 rows]
+ * [16 bytes] (eb = bytes per element), i.e. every 128-row x 128-byte block is
+ * contiguous in the no-swizzle K-major canonical layout of tcgen05.mma;
+ * rows >= n are zero.  NULL: those token counts use the mma.sync GEMV.
  */
 typedef struct SbLinear {
   int32_t fmt;
@@ -57,6 +64,7 @@ typedef struct SbLinear {
   const void* scale;
   float global_scale; /* nvfp4 per-tensor scale, else 1 */
   int32_t _pad;
+  const void* w_tc;
 } SbLinear;
 
 /* One decoder layer.  qkv rows are [q heads | k heads | v heads] with the
@@ -94,7 +102,8 @@ typedef struct SbModel {
 #define SB_CTRL_SLOT 0    /* cache slot of token 0 of the next forward */
 #define SB_CTRL_PADLEN 1  /* padded prompt length T (right-padded batches) */
 #define SB_CTRL_ACCEPT 2  /* verify: accepted prefix length (output) */
-#define SB_CTRL_ERR 3     /* set to 1 by a kernel whose bounded wait expired (results invalid) */
+#define SB_CTRL_ERR 3     /* set non-zero by a kernel whose bounded wait expired (results invalid):
+                             1 = decode GEMV, 2 = tensor-core GEMM */
 #define SB_CTRL_WORDS 8
 
 #define SB_MODE_DECODE 0  /* argmax -> out_ids[step], feed back to ids, slot += M */
@@ -172,9 +181,17 @@ int sb_lm_head_argmax_static(const SbModel* model, const SbState* state, int32_t
 
 /* ---- single ops (each one replaces one reference call site) ------------- */
 /* y[m, :] = x[m, :] W^T, bf16 out: nn.Linear (llm_mega.py:534-536,560,572-573,579,588).
- * Any m >= 1 (processed in blocks of 64 rows); y columns in packed row order. */
+ * Any m >= 1 (processed in blocks of 64 rows); y columns in packed row order.
+ * GEMV kernels only (no workspace). */
 int sb_linear(const SbLinear* lin, const uint16_t* x, uint16_t* y, int32_t m, int32_t use_pdl,
               sb_stream_t stream);
+/* bytes of workspace sb_linear_ex needs to run (lin, m) on the tensor-core
+ * GEMM (0: that path does not serve it) */
+size_t sb_linear_workspace_bytes(const SbLinear* lin, int32_t m);
+/* sb_linear with operand scratch: with lin->w_tc set and m > 8 the rows go
+ * through the tcgen05 GEMM in blocks of 128 (prefill projections) */
+int sb_linear_ex(const SbLinear* lin, const uint16_t* x, uint16_t* y, int32_t m, void* workspace,
+                 size_t workspace_bytes, int32_t use_pdl, sb_stream_t stream);
 /* exact dequantisation of a packed layer to fp32 [n, k] (rows in packed order,
  * padding rows dropped); the quantised formats have no reference counterpart */
 int sb_dequant_f32(const SbLinear* lin, float* out, sb_stream_t stream);

@@ -27,6 +27,7 @@ class SbLinear(C.Structure):
     _fields_ = [
         ("fmt", C.c_int32), ("n", C.c_int32), ("k", C.c_int32), ("n_pad", C.c_int32),
         ("w", vp), ("scale", vp), ("global_scale", C.c_float), ("_pad", C.c_int32),
+        ("w_tc", vp),
     ]
 
 
@@ -64,7 +65,7 @@ EXPORTS = [
     "sb_last_error", "sb_version", "sb_workspace_bytes", "sb_decode_step", "sb_lm_head_argmax",
     "sb_linear", "sb_dequant_f32", "sb_dequant_bf16", "sb_rmsnorm", "sb_silu_mul",
     "sb_residual_scale", "sb_rope", "sb_argmax_bf16", "sb_attention", "sb_decode_op",
-    "sb_lm_head_argmax_static",
+    "sb_lm_head_argmax_static", "sb_linear_ex", "sb_linear_workspace_bytes",
 ]
 
 
@@ -95,6 +96,9 @@ def load() -> C.CDLL:
     lib.sb_attention.argtypes = [C.POINTER(SbModel), C.POINTER(SbState), C.c_int32, vp]
     lib.sb_decode_op.argtypes = [C.POINTER(SbModel), C.POINTER(SbState), C.c_int32, C.c_int32, C.c_int32, vp]
     lib.sb_linear.argtypes = [C.POINTER(SbLinear), vp, vp, C.c_int32, C.c_int32, vp]
+    lib.sb_linear_ex.argtypes = [C.POINTER(SbLinear), vp, vp, C.c_int32, vp, C.c_size_t, C.c_int32, vp]
+    lib.sb_linear_workspace_bytes.restype = C.c_size_t
+    lib.sb_linear_workspace_bytes.argtypes = [C.POINTER(SbLinear), C.c_int32]
     lib.sb_dequant_f32.argtypes = [C.POINTER(SbLinear), vp, vp]
     lib.sb_dequant_bf16.argtypes = [C.POINTER(SbLinear), vp, vp]
     lib.sb_rmsnorm.argtypes = [vp, vp, vp, C.c_int32, C.c_int32, C.c_float, vp]

@@ -18,6 +18,7 @@
 #include <cstring>
 
 #include "attention.cuh"
+#include "gemm_tc.cuh"
 #include "gemv.cuh"
 #include "glue.cuh"
 
@@ -78,6 +79,22 @@ static bool dec_plan_for(int fmt, int n_tiles, int k, int m, DecPlan& pl) {
   return use_dec_kernel() && gemv_dec_plan(fmt, n_tiles, k, m, pl);
 }
 
+// STARLING_B200_GEMM=mma_sync keeps token counts above 8 on the mma.sync GEMV
+// even when a tensor-core tile copy of the weight exists (A/B runs).
+static bool use_tc_kernel() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("STARLING_B200_GEMM");
+    v = (e && strcmp(e, "mma_sync") == 0) ? 0 : 1;
+  }
+  return v == 1;
+}
+
+// The tcgen05 path serves a linear with a tile copy for 9..128 token rows.
+static bool tc_plan_for(const SbLinear& l, int m, TcPlan& pl) {
+  return m > 8 && l.w_tc && use_tc_kernel() && tc_plan(l.fmt, l.n, l.k, m, pl);
+}
+
 static int run_gemv(GemvParams& p, int fmt, bool pdl, cudaStream_t s) {
   DecPlan pl;
   if (p.m <= 8 && dec_plan_for(fmt, p.n_tiles, p.k, p.m, pl)) {
@@ -95,6 +112,21 @@ static int run_gemv(GemvParams& p, int fmt, bool pdl, cudaStream_t s) {
     return fail(rc, "no gemv configuration for n=%d k=%d m=%d (smem %zu)", p.n, p.k, p.m, gemv_smem_bytes(c, p.k, p.m < 64 ? p.m : 64));
   if (rc != 0) return fail(rc, "gemv launch (n=%d k=%d m=%d): %s", p.n, p.k, p.m, cudaGetErrorString((cudaError_t)rc));
   return 0;
+}
+
+// One linear: the tcgen05 GEMM when it serves (l, p.m) and operand scratch is
+// given, else the GEMV kernels.
+static int run_linear(const SbLinear& l, GemvParams& p, void* tc_scratch, size_t tc_bytes, bool pdl, cudaStream_t s) {
+  TcPlan pl;
+  if (tc_scratch && tc_plan_for(l, p.m, pl)) {
+    const size_t need = tc_operand_bytes(l.fmt, l.k, p.m);
+    if (need > tc_bytes) return fail(SB_ERR_ARG, "tensor-core operand scratch too small (%zu < %zu)", tc_bytes, need);
+    const int rc = tc_launch(p, l.w_tc, tc_scratch, pl, l.fmt, pdl, s);
+    if (rc != 0) return fail(rc, "tensor-core gemm launch (n=%d k=%d m=%d): %s", p.n, p.k, p.m,
+                             rc < 1000 ? cudaGetErrorString((cudaError_t)rc) : "config");
+    return 0;
+  }
+  return run_gemv(p, l.fmt, pdl, s);
 }
 
 static int attn_split(int max_len) {
@@ -128,8 +160,11 @@ static LmWork lm_work(const SbModel* md, int tokens, void* base) {
   const SbLinear& l = md->lm_head;
   LmWork w;
   DecPlan pl;
+  TcPlan tp;
   if (tokens <= 8 && dec_plan_for(l.fmt, l.n_pad / 16, l.k, tokens, pl)) {
     w.n_ctas = pl.n_ctas;
+  } else if (tc_plan_for(l, tokens, tp)) {
+    w.n_ctas = tp.n_ctas;
   } else {
     const GemvCfg c = gemv_pick(l.fmt, l.n_pad, l.k, tokens);
     w.n_ctas = gemv_grid(c, l.n_pad / 16) / c.ck;
@@ -141,6 +176,41 @@ static LmWork lm_work(const SbModel* md, int tokens, void* base) {
   w.idx = reinterpret_cast<int*>(b + 256 + ((pv + 255) & ~size_t(255)));
   w.bytes = 256 + 2 * ((pv + 255) & ~size_t(255));
   return w;
+}
+
+// Workspace = [lm_head argmax partials | tensor-core operand scratch].
+struct WsLayout {
+  size_t lm_bytes, tc_off, tc_bytes, total;
+};
+static size_t tc_scratch_need(const SbLinear& l, int tokens) {
+  TcPlan pl;
+  return tc_plan_for(l, tokens, pl) ? tc_operand_bytes(l.fmt, l.k, tokens) : 0;
+}
+static WsLayout ws_layout(const SbModel* md, int tokens) {
+  WsLayout w;
+  w.lm_bytes = lm_work(md, tokens, nullptr).bytes;
+  w.tc_off = (w.lm_bytes + 255) & ~size_t(255);
+  size_t need = tc_scratch_need(md->lm_head, tokens);
+  for (int l = 0; md->layers && l < md->n_layers; ++l) {
+    const SbLayer& L = md->layers[l];
+    const SbLinear* lins[4] = {&L.qkv, &L.o, &L.gate_up, &L.down};
+    for (const SbLinear* x : lins) {
+      const size_t b = tc_scratch_need(*x, tokens);
+      if (b > need) need = b;
+    }
+  }
+  w.tc_bytes = need;
+  w.total = need ? w.tc_off + need : w.lm_bytes;
+  return w;
+}
+// The state's workspace must hold ws_layout().total bytes; tc scratch is
+// null when no linear of the model takes the tensor-core path at this size.
+static int tc_scratch_of(const SbModel* md, const SbState* st, void*& ptr, size_t& bytes) {
+  const WsLayout w = ws_layout(md, st->batch * st->m);
+  if (st->workspace_bytes < w.total) return fail(SB_ERR_ARG, "workspace too small (%zu < %zu)", st->workspace_bytes, w.total);
+  ptr = w.tc_bytes ? static_cast<char*>(st->workspace) + w.tc_off : nullptr;
+  bytes = w.tc_bytes ? st->workspace_bytes - w.tc_off : 0;
+  return 0;
 }
 
 // Token rows above which RMSNorm runs as its own kernel instead of the GEMV
@@ -166,7 +236,12 @@ static int launch_lm_head(const SbModel* md, const SbState* st, int step, cudaSt
   p.x = st->hidden;
   p.norm_w = md->final_norm;
   p.eps = md->eps;
-  if (T > kFusedNormMaxRows) {
+  size_t tcb = 0;
+  void* tcs = nullptr;
+  SB_TRY(tc_scratch_of(md, st, tcs, tcb));
+  TcPlan tp;
+  const bool tc = tcs && tc_plan_for(md->lm_head, T, tp);
+  if (T > kFusedNormMaxRows && !tc) {
     SB_TRY(run_norm(md, st, st->hidden, false, md->final_norm, s));
     p.pro = PRO_NONE;
     p.x = st->xnorm;
@@ -187,7 +262,7 @@ static int launch_lm_head(const SbModel* md, const SbState* st, int step, cudaSt
   p.eos_id = st->eos_id;
   p.pad_id = st->pad_id;
   p.ctrl = st->ctrl;
-  return run_gemv(p, md->lm_head.fmt, st->use_pdl != 0, s);
+  return run_linear(md->lm_head, p, tcs, tcb, st->use_pdl != 0, s);
 }
 
 static int launch_attention(const SbModel* md, const SbState* st, int l, cudaStream_t s) {
@@ -225,12 +300,19 @@ static int launch_op(const SbModel* md, const SbState* st, int l, int op, int st
   const SbLayer& L = md->layers[l];
   if (!lin_ok(L.qkv) || !lin_ok(L.o) || !lin_ok(L.gate_up) || !lin_ok(L.down))
     return fail(SB_ERR_ARG, "layer %d: bad packed linear", l);
-  const bool sep_norm = T > kFusedNormMaxRows;
+  size_t tcb = 0;
+  void* tcs = nullptr;
+  SB_TRY(tc_scratch_of(md, st, tcs, tcb));
+  // the tensor-core path computes the RMSNorm prologue in its operand preparation
+  auto sep_norm_for = [&](const SbLinear& lin) {
+    TcPlan tp;
+    return T > kFusedNormMaxRows && !(tcs && tc_plan_for(lin, T, tp));
+  };
   if (op == SB_OP_QKV) {  // RMSNorm (layer 0: embedding x12) -> q/k/v -> RoPE + cache write
     GemvParams p = base_params(L.qkv, T);
     p.pro = l == 0 ? PRO_EMBED : PRO_RMSNORM;
     p.x = st->hidden;
-    if (sep_norm) {
+    if (sep_norm_for(L.qkv)) {
       SB_TRY(run_norm(md, st, st->hidden, l == 0, L.in_norm, s));
       p.pro = PRO_NONE;
       p.x = st->xnorm;
@@ -255,7 +337,7 @@ static int launch_op(const SbModel* md, const SbState* st, int l, int op, int st
     p.rope_max = md->rope_max_pos;
     p.rope_off = st->rope_off;
     p.ctrl = st->ctrl;
-    return run_gemv(p, L.qkv.fmt, pdl, s);
+    return run_linear(L.qkv, p, tcs, tcb, pdl, s);
   }
   if (op == SB_OP_O || op == SB_OP_DOWN) {  // o / down -> residual scale-add into hidden
     const SbLinear& lin = op == SB_OP_O ? L.o : L.down;
@@ -265,7 +347,7 @@ static int launch_op(const SbModel* md, const SbState* st, int l, int op, int st
     p.epi = EPI_RESID;
     p.y = st->hidden;
     p.res_mult = md->res_mult;
-    return run_gemv(p, lin.fmt, pdl, s);
+    return run_linear(lin, p, tcs, tcb, pdl, s);
   }
   // gate/up: RMSNorm -> interleaved gate|up -> SiLU(gate)*up
   GemvParams p = base_params(L.gate_up, T);
@@ -273,14 +355,14 @@ static int launch_op(const SbModel* md, const SbState* st, int l, int op, int st
   p.x = st->hidden;
   p.norm_w = L.post_norm;
   p.eps = md->eps;
-  if (sep_norm) {
+  if (sep_norm_for(L.gate_up)) {
     SB_TRY(run_norm(md, st, st->hidden, false, L.post_norm, s));
     p.pro = PRO_NONE;
     p.x = st->xnorm;
   }
   p.epi = EPI_SWIGLU;
   p.y = st->act;
-  return run_gemv(p, L.gate_up.fmt, pdl, s);
+  return run_linear(L.gate_up, p, tcs, tcb, pdl, s);
 }
 
 extern "C" {
@@ -290,7 +372,7 @@ int sb_version(void) { return 1; }
 
 size_t sb_workspace_bytes(const SbModel* md, int32_t tokens) {
   if (!md || tokens < 1) return 0;
-  return lm_work(md, tokens, nullptr).bytes;
+  return ws_layout(md, tokens).total;
 }
 
 int sb_decode_step(const SbModel* md, const SbState* st, int32_t step, sb_stream_t stream) {
@@ -315,14 +397,39 @@ int sb_lm_head_argmax(const SbModel* md, const SbState* st, int32_t step, sb_str
 }
 
 int sb_linear(const SbLinear* lin, const uint16_t* x, uint16_t* y, int32_t m, int32_t use_pdl, sb_stream_t stream) {
+  return sb_linear_ex(lin, x, y, m, nullptr, 0, use_pdl, stream);
+}
+
+size_t sb_linear_workspace_bytes(const SbLinear* lin, int32_t m) {
+  if (!lin || m < 1) return 0;
+  return tc_scratch_need(*lin, m > 128 ? 128 : m);
+}
+
+int sb_linear_ex(const SbLinear* lin, const uint16_t* x, uint16_t* y, int32_t m, void* workspace,
+                 size_t workspace_bytes, int32_t use_pdl, sb_stream_t stream) {
   if (!lin || !lin_ok(*lin) || !x || !y) return fail(SB_ERR_ARG, "sb_linear: bad arguments");
   if (m < 1) return fail(SB_ERR_ARG, "sb_linear: m must be >= 1");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  TcPlan pl;
+  if (workspace && tc_plan_for(*lin, m > 128 ? 128 : m, pl)) {
+    // tensor-core path in blocks of at most 128 token rows
+    for (int r0 = 0; r0 < m; r0 += 128) {
+      const int mr = m - r0 < 128 ? m - r0 : 128;
+      GemvParams p = base_params(*lin, mr);
+      p.pro = PRO_NONE;
+      p.x = x + static_cast<size_t>(r0) * lin->k;
+      p.epi = EPI_STORE;
+      p.y = y + static_cast<size_t>(r0) * lin->n;
+      SB_TRY(run_linear(*lin, p, mr > 8 ? workspace : nullptr, workspace_bytes, use_pdl != 0, s));
+    }
+    return 0;
+  }
   GemvParams p = base_params(*lin, m);
   p.pro = PRO_NONE;
   p.x = x;
   p.epi = EPI_STORE;
   p.y = y;
-  return run_gemv(p, lin->fmt, use_pdl != 0, static_cast<cudaStream_t>(stream));
+  return run_gemv(p, lin->fmt, use_pdl != 0, s);
 }
 
 int sb_dequant_f32(const SbLinear* lin, float* out, sb_stream_t stream) {
@@ -415,7 +522,7 @@ extern "C" int sb_lm_head_argmax_static(const SbModel* md, const SbState* st, in
     g_lm_scratch_addr[dev] = p;
   }
   const int T = st->batch * st->m;
-  const size_t need = lm_work(md, T, nullptr).bytes;
+  const size_t need = ws_layout(md, T).total;
   if (need > kStaticLmScratchBytes)
     return fail(SB_ERR_CONFIG,
                 "sb_lm_head_argmax_static: %d token rows need %zu scratch bytes, more than the fixed %zu; "

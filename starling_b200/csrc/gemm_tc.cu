@@ -1,0 +1,567 @@
+// Tensor-core skinny GEMM for 9..128 token rows (batched decode, speculative
+// verify, prefill chunks), sm_100a: tcgen05.mma with the accumulator in TMEM.
+//
+// y[m][row] = sum_k x[m][k] * W[row][k] with the same fused prologues
+// (RMSNorm, embedding) and epilogues (RoPE + KV-cache write, residual,
+// SwiGLU, argmax + token feedback) as the dequant-GEMV.  The weight rows are
+// the MMA's M side (128 rows per tile), the tokens its N side.
+//
+// Operands.  The weight is read from its tensor-core tile copy (SbLinear.w_tc):
+// for every (128-row tile, 128-byte K block) one contiguous 16 KiB block in
+// the canonical no-swizzle K-major layout of tcgen05 (8-row x 16-byte core
+// matrices; K chunks 128 B apart, 8-row groups 1024 B apart), so one bulk
+// copy (cp.async.bulk, no tensor map) stages it.  The activations are
+// prepared once per launch by k_tc_prep into the same layout:
+//  * bf16 weights (kind::f16): the bf16 rows themselves (after the prologue);
+//  * fp8 weights (kind::f8f6f4, e4m3 x e4m3): each row is scaled by a power
+//    of two 2^s (max |x| 2^s in [128, 256)) and split into two e4m3 terms,
+//    x 2^s = t0 + t1/16 with t0 = e4m3(x 2^s), t1 = e4m3(16 (x 2^s - t0)).
+//    Both subtractions are exact, and the pair represents every bf16 value
+//    within 2^13 of the row maximum exactly (smaller ones to 2^-14 absolute
+//    in the scaled units).  The two terms are the two halves of the MMA's N
+//    (columns m and mp + m); the epilogue forms (D0 + D1/16) 2^-s.  Products
+//    of e4m3 values are exact, so the result differs from the dequantised
+//    fp32 reference only by fp32 accumulation order.
+//
+// Kernel (192 threads, one CTA per SM):
+//  * warp 4 (one thread) streams (A block, B block) pairs into a ring of
+//    shared-memory stages with bulk copies completing on mbarriers; the weight
+//    blocks of the first ring are issued BEFORE griddepcontrol.wait, so they
+//    overlap the previous kernel;
+//  * warp 5 (one thread) issues four tcgen05.mma (K = 32 bytes each) per
+//    stage and frees the stage with tcgen05.commit;
+//  * warps 0-3 read the 128 x N fp32 accumulator (warp w owns TMEM lanes
+//    32w..32w+31 = tile rows), undo the activation scaling and run the fused
+//    epilogue.
+// With many tiles (lm_head, gate/up) each CTA is persistent over tiles and the
+// epilogue of one tile overlaps the weight stream of the next.  With few tiles
+// a cluster of `split` CTAs shares a tile, each taking a contiguous K range;
+// the partial tiles are reduced over distributed shared memory in rank order
+// (deterministic), each CTA finishing 128/split rows.
+// Every wait is bounded (2 s of %globaltimer); on expiry the kernel records
+// SB_CTRL_ERR = 2 and carries on with invalid results instead of hanging.
+#include <cooperative_groups.h>
+
+#include "gemm_tc.cuh"
+#include "gemv_epi.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace sb {
+
+namespace {
+
+__device__ __forceinline__ uint32_t su32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t n) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(n) : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(su32(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   su32(dst)),
+               "l"(src), "r"(bytes), "r"(su32(bar))
+               : "memory");
+}
+__device__ __forceinline__ uint64_t gtimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+constexpr uint64_t kWaitNs = 2000000000ull;
+
+// Wait for the phase of parity `parity` to complete; bounded.
+__device__ __noinline__ void wait_bounded(uint64_t* bar, uint32_t parity, int32_t* err) {
+  if (mbar_try_wait(bar, parity)) return;
+  const uint64_t t0 = gtimer();
+  for (;;) {
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait(bar, parity)) return;
+    if (gtimer() - t0 > kWaitNs) {
+      if (err) atomicExch(err, 2);
+      return;
+    }
+  }
+}
+
+// ---- tcgen05 ------------------------------------------------------------------
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(dst)), "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// Shared-memory matrix descriptor: no swizzle, K-major canonical layout.
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = static_cast<uint64_t>((saddr >> 4) & 0x3FFF);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFF) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFF) << 32;
+  d |= static_cast<uint64_t>(1) << 46;  // descriptor version (sm_100)
+  return d;                             // base offset 0, layout type 0 = no swizzle
+}
+template <int FMT>
+__device__ __forceinline__ void tc_mma(uint32_t tmem, uint64_t ad, uint64_t bd, uint32_t idesc, uint32_t acc) {
+  if constexpr (FMT == SB_FMT_BF16) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
+        "l"(ad), "l"(bd), "r"(idesc), "r"(acc)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
+        "l"(ad), "l"(bd), "r"(idesc), "r"(acc)
+        : "memory");
+  }
+}
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t* r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// fixed-order block reductions over 256 threads
+__device__ __forceinline__ float block_sum256(float v, float* s_red) {
+  v = warp_sum(v);
+  if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) t += s_red[i];
+  __syncthreads();
+  return t;
+}
+__device__ __forceinline__ float block_max256(float v, float* s_red) {
+  v = warp_max(v);
+  if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) t = fmaxf(t, s_red[i]);
+  __syncthreads();
+  return t;
+}
+
+__device__ __forceinline__ float e4m3_round(float v, uint8_t& q) {
+  q = __nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3);
+  return __half2float(__half(__nv_cvt_fp8_to_halfraw(q, __NV_E4M3)));
+}
+
+}  // namespace
+
+struct TcArgs {
+  const uint8_t* wt;      // weight tiles [tiles][kb][16 KiB]
+  const uint8_t* xq;      // B operand [kb][np/8][8 chunks][8 rows][16 B]
+  const int32_t* xshift;  // fp8: per-row power-of-two scale of the activations
+  uint32_t idesc;
+  int mp, np, tiles, kb, split, stages, ncols;
+};
+
+// ---- B operand: prologue + layout ------------------------------------------------
+// One CTA per (padded) token row.  Rows >= m are written as zeros.
+template <int FMT>
+__global__ void __launch_bounds__(256) k_tc_prep(const __grid_constant__ GemvParams p, uint8_t* xq, int32_t* xshift,
+                                                  int mp, int np) {
+  constexpr int CE = FMT == SB_FMT_BF16 ? 8 : 16;  // elements per 16-byte chunk
+  __shared__ float s_red[8];
+  const int m = blockIdx.x, tid = threadIdx.x, K = p.k;
+  const int nch = K / CE;
+  const size_t kb_bytes = static_cast<size_t>(np) * 128;
+  auto off = [&](int n, int c) -> size_t {
+    return static_cast<size_t>(c >> 3) * kb_bytes + static_cast<size_t>(n >> 3) * 1024 + (c & 7) * 128 + (n & 7) * 16;
+  };
+  pdl_wait();
+  pdl_launch();
+  if (m >= p.m) {
+    for (int c = tid; c < nch; c += blockDim.x) {
+      *reinterpret_cast<uint4*>(xq + off(m, c)) = make_uint4(0, 0, 0, 0);
+      if (FMT == SB_FMT_FP8) *reinterpret_cast<uint4*>(xq + off(mp + m, c)) = make_uint4(0, 0, 0, 0);
+    }
+    if (FMT == SB_FMT_FP8 && tid == 0) xshift[m] = 0;
+    return;
+  }
+  const bool embed = p.pro == PRO_EMBED;
+  const uint16_t* src;
+  if (embed) {
+    int64_t id = p.ids[m];
+    id = id < 0 ? 0 : (id >= p.embed_rows ? p.embed_rows - 1 : id);  // never read outside the table
+    src = p.embed + static_cast<size_t>(id) * K;
+  } else {
+    src = p.x + static_cast<size_t>(m) * K;
+  }
+  auto load_h = [&](int k, float* h) {  // the residual-stream value (embedding x 12 for layer 0)
+    unpack8(*reinterpret_cast<const uint4*>(src + k), h);
+    if (embed) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) h[e] = bf(h[e] * p.emb_mult);  // llm_mega.py:514
+    }
+  };
+  float rstd = 1.f;
+  if (p.pro != PRO_NONE) {
+    float ss = 0.f;
+    for (int k = tid * 8; k < K; k += blockDim.x * 8) {
+      float h[8];
+      load_h(k, h);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss += h[e] * h[e];
+    }
+    ss = block_sum256(ss, s_red);
+    rstd = 1.f / sqrtf(ss / static_cast<float>(K) + p.eps);
+  }
+  auto norm8 = [&](int k, float* f) {  // weight * bf16(x * rstd)  (modeling_granite.py:192-197)
+    load_h(k, f);
+    if (p.pro != PRO_NONE) {
+      float wn[8];
+      unpack8(*reinterpret_cast<const uint4*>(p.norm_w + k), wn);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) f[e] = bf(wn[e] * bf(f[e] * rstd));
+    }
+  };
+  if (embed && p.hidden_out) {
+    for (int k = tid * 8; k < K; k += blockDim.x * 8) {
+      float h[8];
+      load_h(k, h);
+      *reinterpret_cast<uint4*>(p.hidden_out + static_cast<size_t>(m) * K + k) = pack8(h);
+    }
+  }
+  int shift = 0;
+  if (FMT == SB_FMT_FP8) {
+    float am = 0.f;
+    for (int k = tid * 8; k < K; k += blockDim.x * 8) {
+      float f[8];
+      norm8(k, f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) am = fmaxf(am, fabsf(f[e]));
+    }
+    am = block_max256(am, s_red);
+    int e2 = 0;
+    if (am > 0.f) frexpf(am, &e2);
+    shift = 8 - e2;  // max |x| 2^shift in [128, 256)
+    if (tid == 0) xshift[m] = shift;
+  }
+  for (int c = tid; c < nch; c += blockDim.x) {
+    const int k = c * CE;
+    if constexpr (FMT == SB_FMT_BF16) {
+      float f[8];
+      norm8(k, f);
+      *reinterpret_cast<uint4*>(xq + off(m, c)) = pack8(f);
+    } else {
+      uint8_t q0[16], q1[16];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float f[8];
+        norm8(k + 8 * h, f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float v = ldexpf(f[e], shift);  // exact
+          const float t0 = e4m3_round(v, q0[8 * h + e]);
+          e4m3_round((v - t0) * 16.f, q1[8 * h + e]);  // exact residual
+        }
+      }
+      *reinterpret_cast<uint4*>(xq + off(m, c)) = *reinterpret_cast<const uint4*>(q0);
+      *reinterpret_cast<uint4*>(xq + off(mp + m, c)) = *reinterpret_cast<const uint4*>(q1);
+    }
+  }
+}
+
+// ---- the GEMM ----------------------------------------------------------------------
+template <int FMT>
+__global__ void __launch_bounds__(192, 1) k_tc_gemm(const __grid_constant__ GemvParams p, const __grid_constant__ TcArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int M = p.m;
+  const TcLayout L = tc_layout(a.np, a.stages, M, a.split);
+  uint8_t* ring = smem;
+  float* part = reinterpret_cast<float*>(smem + L.part);  // [128][M] this CTA's tile (partial if split)
+  float* outb = reinterpret_cast<float*>(smem + L.out);   // [128/split][M] reduced rows (split > 1)
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
+  uint64_t* empty = full + a.stages;
+  uint64_t* acc_full = empty + a.stages;
+  uint64_t* acc_empty = acc_full + 1;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + L.tmem);
+  int* s_flag = reinterpret_cast<int*>(smem + L.flag);
+  int* s_best = reinterpret_cast<int*>(smem + L.best);
+  float* s_bval = reinterpret_cast<float*>(smem + L.bval);
+  int* s_shift = reinterpret_cast<int*>(smem + L.shift);
+  int32_t* err = p.ctrl ? p.ctrl + SB_CTRL_ERR : nullptr;
+
+  const int S = a.split;
+  const int q = S > 1 ? static_cast<int>(cg::this_cluster().block_rank()) : 0;
+  const int cid = blockIdx.x / S, ncl = gridDim.x / S;
+  const int kb0 = q * a.kb / S, kb1 = (q + 1) * a.kb / S, nk = kb1 - kb0;
+  const int my_tiles = cid < a.tiles ? (a.tiles - cid + ncl - 1) / ncl : 0;
+  const uint32_t a_bytes = 16384u, b_bytes = static_cast<uint32_t>(a.np) * 128u;
+
+  if (warp == 4 && lane == 0) {
+    for (int s = 0; s < a.stages; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, 128);
+    mbar_fence_init();
+  }
+  if (warp == 5) tmem_alloc(s_tmem, static_cast<uint32_t>(a.ncols));
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+
+  if (warp == 4) {
+    // ---- producer ----
+    if (lane == 0) {
+      const int total = my_tiles * nk;
+      auto a_src = [&](int it) {
+        const int t = cid + (it / nk) * ncl, kbi = kb0 + it % nk;
+        return a.wt + (static_cast<size_t>(t) * a.kb + kbi) * 16384;
+      };
+      auto b_src = [&](int it) { return a.xq + static_cast<size_t>(kb0 + it % nk) * b_bytes; };
+      const int pre = total < a.stages ? total : a.stages;
+      for (int it = 0; it < pre; ++it) {  // weights do not depend on the previous kernel
+        mbar_expect_tx(full + it, a_bytes + b_bytes);
+        bulk_g2s(ring + it * L.stage_bytes, a_src(it), a_bytes, full + it);
+      }
+      pdl_wait();
+      for (int it = 0; it < pre; ++it) bulk_g2s(ring + it * L.stage_bytes + 16384, b_src(it), b_bytes, full + it);
+      for (int it = pre; it < total; ++it) {
+        const int s = it % a.stages;
+        wait_bounded(empty + s, static_cast<uint32_t>((it / a.stages - 1) & 1), err);
+        mbar_expect_tx(full + s, a_bytes + b_bytes);
+        bulk_g2s(ring + s * L.stage_bytes, a_src(it), a_bytes, full + s);
+        bulk_g2s(ring + s * L.stage_bytes + 16384, b_src(it), b_bytes, full + s);
+      }
+    }
+    __syncwarp();
+    pdl_wait();
+    pdl_launch();
+  } else if (warp == 5) {
+    // ---- MMA issuer ----
+    pdl_wait();
+    pdl_launch();
+    if (lane == 0) {
+      int it = 0;
+      for (int tc = 0; tc < my_tiles; ++tc) {
+        if (tc > 0) wait_bounded(acc_empty, static_cast<uint32_t>((tc - 1) & 1), err);
+        tc_fence_after();
+        for (int j = 0; j < nk; ++j, ++it) {
+          const int s = it % a.stages;
+          wait_bounded(full + s, static_cast<uint32_t>((it / a.stages) & 1), err);
+          tc_fence_after();
+          const uint32_t sa = su32(ring + s * L.stage_bytes), sbb = sa + 16384u;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            tc_mma<FMT>(tmem, sdesc(sa + kk * 256u, 128u, 1024u), sdesc(sbb + kk * 256u, 128u, 1024u), a.idesc,
+                        (j > 0 || kk > 0) ? 1u : 0u);
+          tc_commit(empty + s);  // the stage is free once these MMAs have read it
+        }
+        tc_commit(acc_full);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---- epilogue warps 0-3: TMEM lanes 32w.. = tile rows ----
+    pdl_wait();
+    pdl_launch();
+    if (FMT == SB_FMT_FP8)
+      for (int i = tid; i < M; i += 128) s_shift[i] = a.xshift[i];
+    epi_sync();
+    const int row = warp * 32 + lane;
+    const uint32_t taddr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    for (int tc = 0; tc < my_tiles; ++tc) {
+      const int t = cid + tc * ncl;
+      wait_bounded(acc_full, static_cast<uint32_t>(tc & 1), err);
+      tc_fence_after();
+      for (int m0 = 0; m0 < a.mp; m0 += 8) {
+        uint32_t d0[8], d1[8];
+        tmem_ld8(taddr + m0, d0);
+        if (FMT == SB_FMT_FP8) tmem_ld8(taddr + a.mp + m0, d1);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int m = m0 + i;
+          if (m < M) {
+            float v = __uint_as_float(d0[i]);
+            if (FMT == SB_FMT_FP8) v = ldexpf(v + __uint_as_float(d1[i]) * 0.0625f, -s_shift[m]);
+            part[row * M + m] = v;
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(acc_empty);  // the MMA warp may overwrite the accumulator
+      if (S == 1) {
+        epi_sync();
+        gemv_epilogue<FMT>(p, part, t * 128, 128, M, s_best, s_bval, tc == 0, tc == my_tiles - 1, tid, 128);
+        epi_sync();
+      }
+    }
+  }
+
+  if (S > 1) {  // one tile per cluster: reduce the K partials in rank order
+    cg::cluster_group cl = cg::this_cluster();
+    cl.sync();
+    const int rp = (128 + S - 1) / S, r0 = q * rp;
+    const int nr = r0 >= 128 ? 0 : (r0 + rp > 128 ? 128 - r0 : rp);
+    for (int i = tid; i < nr * M; i += blockDim.x) {
+      const int r = r0 + i / M, m = i % M;
+      float s = 0.f;
+      for (int c = 0; c < S; ++c) s += cl.map_shared_rank(part, c)[r * M + m];
+      outb[i] = s;
+    }
+    __syncthreads();
+    if (my_tiles > 0 && nr > 0)
+      gemv_epilogue<FMT>(p, outb, cid * 128 + r0, nr, M, s_best, s_bval, true, true, tid, blockDim.x);
+    cl.sync();  // the peers have finished reading this CTA's partials
+  }
+  __syncthreads();
+  gemv_argmax_finish(p, s_best, s_bval, M, my_tiles > 0, s_flag);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, static_cast<uint32_t>(a.ncols));
+  }
+}
+
+// ---- host side ------------------------------------------------------------------
+static const int kSMs = 148;
+static const size_t kTcSmem = 220 * 1024;
+
+static int elem_bytes(int fmt) { return fmt == SB_FMT_BF16 ? 2 : 1; }
+static int pad_rows(int fmt, int m) { return fmt == SB_FMT_BF16 ? (m + 15) / 16 * 16 : (m + 7) / 8 * 8; }
+
+size_t tc_operand_bytes(int fmt, int k, int m) {
+  if (!tc_format(fmt) || m < 1) return 0;
+  const int mp = pad_rows(fmt, m);
+  const int np = fmt == SB_FMT_FP8 ? 2 * mp : mp;
+  return static_cast<size_t>(np) * k * elem_bytes(fmt) + 128 * 4;
+}
+
+bool tc_plan(int fmt, int n, int k, int m, TcPlan& pl) {
+  if (!tc_format(fmt) || m < 1 || m > 128 || n < 1) return false;
+  const int eb = elem_bytes(fmt);
+  if ((k * eb) % 128 != 0) return false;
+  pl.mp = pad_rows(fmt, m);
+  pl.np = fmt == SB_FMT_FP8 ? 2 * pl.mp : pl.mp;
+  if (pl.np < 16 || pl.np > 256) return false;
+  pl.tiles = (n + 127) / 128;
+  pl.kb = k * eb / 128;
+  if (pl.tiles * 4 >= kSMs * 3) {  // enough tiles: persistent, no K split
+    pl.split = 1;
+    pl.n_ctas = pl.tiles < kSMs ? pl.tiles : kSMs;
+  } else {
+    int s = kSMs / pl.tiles;
+    if (s > 8) s = 8;
+    if (s > pl.kb) s = pl.kb;
+    if (s < 1) s = 1;
+    pl.split = s;
+    pl.n_ctas = pl.tiles * s;
+  }
+  pl.ncols = 32;
+  while (pl.ncols < pl.np) pl.ncols *= 2;
+  pl.stages = 0;
+  for (int st = 8; st >= 2; --st)
+    if (tc_layout(pl.np, st, m, pl.split).total <= kTcSmem) {
+      pl.stages = st;
+      break;
+    }
+  if (!pl.stages) return false;
+  pl.smem = tc_layout(pl.np, pl.stages, m, pl.split).total;
+  return true;
+}
+
+template <int FMT>
+static int tc_launch_t(const GemvParams& p0, const void* w_tc, void* operand, const TcPlan& pl, bool pdl,
+                       cudaStream_t stream) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static unsigned configured = 0;
+  if (!(configured & (1u << dev))) {
+    cudaError_t e = cudaFuncSetAttribute(k_tc_gemm<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kTcSmem));
+    if (e != cudaSuccess) return e;
+    configured |= 1u << dev;
+  }
+  GemvParams p = p0;
+  p.n_ctas = pl.n_ctas;
+  uint8_t* xq = static_cast<uint8_t*>(operand);
+  int32_t* xshift = reinterpret_cast<int32_t*>(xq + static_cast<size_t>(pl.np) * p.k * elem_bytes(FMT));
+
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(pl.mp);
+  cfg.blockDim = dim3(256);
+  cfg.stream = stream;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, k_tc_prep<FMT>, p, xq, xshift, pl.mp, pl.np);
+  if (e != cudaSuccess) return e;
+
+  TcArgs a;
+  a.wt = static_cast<const uint8_t*>(w_tc);
+  a.xq = xq;
+  a.xshift = xshift;
+  // instruction descriptor: D f32, A/B K-major, A/B e4m3 (f8f6f4) or bf16 (f16), N, M = 128
+  const uint32_t ab = FMT == SB_FMT_BF16 ? 1u : 0u;
+  a.idesc = (1u << 4) | (ab << 7) | (ab << 10) | (static_cast<uint32_t>(pl.np >> 3) << 17) | ((128u >> 4) << 24);
+  a.mp = pl.mp;
+  a.np = pl.np;
+  a.tiles = pl.tiles;
+  a.kb = pl.kb;
+  a.split = pl.split;
+  a.stages = pl.stages;
+  a.ncols = pl.ncols;
+  cfg.gridDim = dim3(pl.n_ctas);
+  cfg.blockDim = dim3(192);
+  cfg.dynamicSmemBytes = pl.smem;
+  int na = 0;
+  if (pdl) at[na++] = at[0];
+  if (pl.split > 1) {
+    at[na].id = cudaLaunchAttributeClusterDimension;
+    at[na].val.clusterDim.x = pl.split;
+    at[na].val.clusterDim.y = 1;
+    at[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, k_tc_gemm<FMT>, p, a);
+}
+
+int tc_launch(const GemvParams& p, const void* w_tc, void* operand, const TcPlan& pl, int fmt, bool pdl,
+              cudaStream_t stream) {
+  switch (fmt) {
+    case SB_FMT_BF16: return tc_launch_t<SB_FMT_BF16>(p, w_tc, operand, pl, pdl, stream);
+    case SB_FMT_FP8: return tc_launch_t<SB_FMT_FP8>(p, w_tc, operand, pl, pdl, stream);
+  }
+  return SB_ERR_ARG;
+}
+
+}  // namespace sb

@@ -299,7 +299,8 @@ __global__ void __launch_bounds__(512, 1) k_gemv_dec(const __grid_constant__ Gem
       tot[i] = sum;
     }
     __syncthreads();
-    gemv_epilogue<FMT>(p, tot, (t0 + jb) * 16, nb * 16, M, s_best, s_bval, jb == 0, jb + nb >= ntile);
+    gemv_epilogue<FMT>(p, tot, (t0 + jb) * 16, nb * 16, M, s_best, s_bval, jb == 0, jb + nb >= ntile, tid,
+                       blockDim.x);
     __syncthreads();
   }
   gemv_argmax_finish(p, s_best, s_bval, M, ntile > 0, s_flag);

@@ -7,11 +7,13 @@ namespace sb {
 
 // tot[lrow * M + m] holds the reduced, activation-unscaled dot product of
 // packed row row0 + lrow and token m.  first/last mark the CTA's first and
-// last block (argmax keeps a running best per token across blocks).
+// last block (argmax keeps a running best per token across blocks).  Run by
+// the nthr (a multiple of 32) threads tid = 0..nthr-1 of the block; it has no
+// barrier inside.
 template <int FMT>
 __device__ __forceinline__ void gemv_epilogue(const GemvParams& p, const float* tot, int row0, int nrow, int M,
-                                              int* s_best, float* s_bval, bool first, bool last) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, W = blockDim.x >> 5;
+                                              int* s_best, float* s_bval, bool first, bool last, int tid, int nthr) {
+  const int lane = tid & 31, warp = tid >> 5, W = nthr >> 5;
   auto fin = [&](int lrow, int m) -> float {
     float v = tot[lrow * M + m];
     if (FMT == SB_FMT_NVFP4) v *= p.gscale;
@@ -19,13 +21,13 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams& p, const float* 
     return v;
   };
   if (p.epi == EPI_STORE) {
-    for (int i = tid; i < nrow * M; i += blockDim.x) {
+    for (int i = tid; i < nrow * M; i += nthr) {
       const int m = i / nrow, lrow = i % nrow, row = row0 + lrow;
       if (row < p.n) p.y[static_cast<size_t>(m) * p.n + row] = f_to_bf16_bits(fin(lrow, m));
     }
   } else if (p.epi == EPI_RESID) {
     // hidden = hidden + bf16(res_mult * bf16(y))   (llm_kernels.py:306-313)
-    for (int i = tid; i < nrow * M; i += blockDim.x) {
+    for (int i = tid; i < nrow * M; i += nthr) {
       const int m = i / nrow, lrow = i % nrow, row = row0 + lrow;
       if (row < p.n) {
         uint16_t* hp = p.y + static_cast<size_t>(m) * p.n + row;
@@ -35,7 +37,7 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams& p, const float* 
   } else if (p.epi == EPI_SWIGLU) {
     // act = bf16(bf16(silu(gate)) * up)   (llm_kernels.py:252-260); rows interleave gate/up
     const int inter = p.n / 2, np = nrow / 2;
-    for (int i = tid; i < np * M; i += blockDim.x) {
+    for (int i = tid; i < np * M; i += nthr) {
       const int m = i / np, lp = i % np, lrow = 2 * lp, row = row0 + lrow;
       if (row < p.n) {
         const float gv = bf(fin(lrow, m));
@@ -49,7 +51,7 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams& p, const float* 
     // to cache slot ctrl[SLOT] + token (StaticLayer.update, cache_utils.py:308-335)
     const int qk_rows = (p.n_q + p.n_kv) * 128;
     const int slot_base = p.ctrl[SB_CTRL_SLOT];
-    for (int i = tid; i < nrow * M; i += blockDim.x) {
+    for (int i = tid; i < nrow * M; i += nthr) {
       const int m = i / nrow, lrow = i % nrow, row = row0 + lrow;
       if (row >= p.n) continue;
       const int b = m / p.m_per, mi = m % p.m_per;

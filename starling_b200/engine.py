@@ -118,7 +118,11 @@ class EngineState:
 
 class GraniteEngine:
     def __init__(self, dims, weights: dict, fmt: str = "bf16", max_cache_len: int = 640,
-                 max_batch: int = 1, device="cuda", rope_max_pos: Optional[int] = None):
+                 max_batch: int = 1, device="cuda", rope_max_pos: Optional[int] = None,
+                 tensor_cores: bool = True):
+        """tensor_cores: also keep the tcgen05 tile copy of every fp8 / bf16
+        weight, which serves 9..128 token rows (batched decode, verify,
+        prefill); it doubles the weight memory of those formats."""
         self.lib = _lib.load()
         self.dims = d = GraniteDims.coerce(dims)
         if d.head_dim != 128:
@@ -135,7 +139,8 @@ class GraniteEngine:
         self.embed = W("embed_tokens.weight").contiguous()
         self.final_norm = W("norm.weight").contiguous()
         head_w = weights.get("lm_head.weight", None)
-        self.lm_head = pack_matrix(self.embed if head_w is None else W("lm_head.weight"), fmt)
+        tc = bool(tensor_cores)
+        self.lm_head = pack_matrix(self.embed if head_w is None else W("lm_head.weight"), fmt, tc=tc)
         self.layers = []
         for i in range(d.layers):
             p = f"layers.{i}."
@@ -143,10 +148,10 @@ class GraniteEngine:
                 in_norm=W(p + "input_layernorm.weight").contiguous(),
                 post_norm=W(p + "post_attention_layernorm.weight").contiguous(),
                 qkv=pack_qkv(W(p + "self_attn.q_proj.weight"), W(p + "self_attn.k_proj.weight"),
-                             W(p + "self_attn.v_proj.weight"), d.n_q, d.n_kv, fmt),
-                o=pack_matrix(W(p + "self_attn.o_proj.weight"), fmt),
-                gate_up=pack_gate_up(W(p + "mlp.gate_proj.weight"), W(p + "mlp.up_proj.weight"), fmt),
-                down=pack_matrix(W(p + "mlp.down_proj.weight"), fmt),
+                             W(p + "self_attn.v_proj.weight"), d.n_q, d.n_kv, fmt, tc=tc),
+                o=pack_matrix(W(p + "self_attn.o_proj.weight"), fmt, tc=tc),
+                gate_up=pack_gate_up(W(p + "mlp.gate_proj.weight"), W(p + "mlp.up_proj.weight"), fmt, tc=tc),
+                down=pack_matrix(W(p + "mlp.down_proj.weight"), fmt, tc=tc),
             )
             self.layers.append(L)
         # static KV cache: [layer][k|v][batch][n_kv][max_len][128] (StaticLayer layout per layer)
@@ -224,7 +229,12 @@ class GraniteEngine:
         x2 = x.reshape(-1, shp[-1]).to(BF16).contiguous()
         y = torch.empty(x2.shape[0], p.n, dtype=BF16, device=self.device)
         c = p.c_struct()
-        check(self.lib.sb_linear(C.byref(c), ptr(x2), ptr(y), x2.shape[0], 0, _lib.current_stream()), "sb_linear")
+        need = int(self.lib.sb_linear_workspace_bytes(C.byref(c), x2.shape[0]))
+        ws = getattr(self, "_lin_ws", None)
+        if need and (ws is None or ws.numel() < need):
+            self._lin_ws = ws = torch.empty(need, dtype=torch.uint8, device=self.device)
+        check(self.lib.sb_linear_ex(C.byref(c), ptr(x2), ptr(y), x2.shape[0], ptr(ws) if need else None,
+                                    ws.numel() if need else 0, 0, _lib.current_stream()), "sb_linear_ex")
         if p.row_perm is not None:
             y = y[:, self._inverse_perm(p)]
         return y.view(*shp[:-1], p.n)

@@ -19,6 +19,13 @@ head the RoPE halves are interleaved (packed row ``2j`` = dim ``j``, ``2j+1`` =
 dim ``j+64``) so that the GEMV epilogue holds both operands of each RoPE pair;
 ``gate_up`` interleaves gate row ``i`` (``2i``) and up row ``i`` (``2i+1``) for the
 SwiGLU epilogue.  Quantised fused matrices are quantised as one tensor.
+
+Tensor-core tile copy (``w_tc``, fp8 and bf16): the same packed rows as raw
+bytes (e4m3 codes / bf16), rows padded to a multiple of 128, cut into
+128-row x 128-byte blocks, each block in the no-swizzle K-major canonical
+layout of ``tcgen05.mma``: byte ``(row, kbyte)`` of block ``(tile, kb)`` sits at
+``rg*1024 + kc*128 + r*16 + b`` with ``row = 128*tile + 8*rg + r`` and
+``kbyte = 128*kb + 16*kc + b``.
 """
 
 from __future__ import annotations
@@ -42,6 +49,7 @@ class PackedLinear:
     scale: Optional[torch.Tensor]  # fp32 [n_pad] (fp8/int8) or uint8 (nvfp4) or None
     global_scale: float = 1.0
     row_perm: Optional[torch.Tensor] = None  # packed row r holds logical row row_perm[r]
+    w_tc: Optional[torch.Tensor] = None  # uint8 tensor-core tile copy (fp8 / bf16)
 
     def c_struct(self) -> SbLinear:
         s = SbLinear()
@@ -50,6 +58,7 @@ class PackedLinear:
         s.w = self.w.data_ptr()
         s.scale = self.scale.data_ptr() if self.scale is not None else None
         s.global_scale = float(self.global_scale)
+        s.w_tc = self.w_tc.data_ptr() if self.w_tc is not None else None
         return s
 
     @property
@@ -70,29 +79,58 @@ def _frag_order(q: torch.Tensor, kge: int) -> torch.Tensor:
     return v.reshape(-1)
 
 
-def pack_matrix(w: torch.Tensor, fmt: str) -> PackedLinear:
-    """Quantise (if needed) and pack a logical weight [N, K] (bf16 or fp32)."""
+TC_FORMATS = ("fp8", "bf16")
+
+
+def tc_tiles(rows: torch.Tensor) -> torch.Tensor:
+    """Row-major bytes ``[n, kbytes]`` (uint8) -> the tensor-core tile copy."""
+    n, kbytes = rows.shape
+    if kbytes % 128:
+        raise ValueError(f"row bytes {kbytes} must be a multiple of 128")
+    n_pad = (n + 127) // 128 * 128
+    if n_pad != n:
+        rows = torch.cat([rows, torch.zeros(n_pad - n, kbytes, dtype=torch.uint8, device=rows.device)])
+    T, KB = n_pad // 128, kbytes // 128
+    v = rows.reshape(T, 16, 8, KB, 8, 16)  # (tile, rg, r, kb, kc, b)
+    return v.permute(0, 3, 1, 4, 2, 5).contiguous().view(-1)
+
+
+def tc_untile(t: torch.Tensor, n: int, kbytes: int) -> torch.Tensor:
+    """Inverse of :func:`tc_tiles` (layout check)."""
+    n_pad = (n + 127) // 128 * 128
+    T, KB = n_pad // 128, kbytes // 128
+    v = t.view(T, KB, 16, 8, 8, 16).permute(0, 2, 4, 1, 3, 5)
+    return v.reshape(n_pad, kbytes)[:n]
+
+
+def pack_matrix(w: torch.Tensor, fmt: str, tc: bool = False) -> PackedLinear:
+    """Quantise (if needed) and pack a logical weight [N, K] (bf16 or fp32).
+
+    tc: also build the tensor-core tile copy (fp8 / bf16 only)."""
     n, k = w.shape
     kge = KGROUP_ELEMS[fmt]
     if k % 64:
         raise ValueError(f"K={k} must be a multiple of 64")
     n_pad = (n + 15) // 16 * 16
     dev = w.device
+    tc = tc and fmt in TC_FORMATS
     if fmt == "bf16":
         q = w.to(torch.bfloat16).view(torch.int16)
+        w_tc = tc_tiles(q.view(torch.uint8).reshape(n, 2 * k)) if tc else None
         if n_pad != n:
             q = torch.cat([q, torch.zeros(n_pad - n, k, dtype=torch.int16, device=dev)])
         packed = _frag_order(q, kge).contiguous().view(torch.uint8)
-        return PackedLinear(fmt, n, k, n_pad, packed, None)
+        return PackedLinear(fmt, n, k, n_pad, packed, None, w_tc=w_tc)
     parts = quant.quantize(fmt, w)
     if fmt in ("fp8", "int8"):
         q, s = parts
         q = q.view(torch.uint8)
+        w_tc = tc_tiles(q) if tc else None
         if n_pad != n:
             q = torch.cat([q, torch.zeros(n_pad - n, k, dtype=torch.uint8, device=dev)])
             s = torch.cat([s, torch.ones(n_pad - n, dtype=torch.float32, device=dev)])
         packed = _frag_order(q, kge).contiguous()
-        return PackedLinear(fmt, n, k, n_pad, packed, s.contiguous())
+        return PackedLinear(fmt, n, k, n_pad, packed, s.contiguous(), w_tc=w_tc)
     codes, sb, g = parts
     if n_pad != n:
         codes = torch.cat([codes, torch.zeros(n_pad - n, k, dtype=torch.uint8, device=dev)])
@@ -121,18 +159,18 @@ def gate_up_perm(inter: int) -> torch.Tensor:
     return torch.stack([torch.arange(inter), torch.arange(inter) + inter], dim=1).reshape(-1)
 
 
-def pack_qkv(wq, wk, wv, n_q, n_kv, fmt, head_dim=128) -> PackedLinear:
+def pack_qkv(wq, wk, wv, n_q, n_kv, fmt, head_dim=128, tc: bool = False) -> PackedLinear:
     perm = qkv_perm(n_q, n_kv, head_dim).to(wq.device)
     w = torch.cat([wq, wk, wv], dim=0)[perm]
-    p = pack_matrix(w, fmt)
+    p = pack_matrix(w, fmt, tc=tc)
     p.row_perm = perm
     return p
 
 
-def pack_gate_up(wg, wu, fmt) -> PackedLinear:
+def pack_gate_up(wg, wu, fmt, tc: bool = False) -> PackedLinear:
     perm = gate_up_perm(wg.shape[0]).to(wg.device)
     w = torch.cat([wg, wu], dim=0)[perm]
-    p = pack_matrix(w, fmt)
+    p = pack_matrix(w, fmt, tc=tc)
     p.row_perm = perm
     return p
 

@@ -252,3 +252,47 @@ def test_one_layer_baseline_dims(golden_dir):
     assert (got.float() - ref.float()).abs().max() <= _logit_tol(ref)
     if _margin(ref) > _logit_tol(ref):
         assert int(st.out_ids[0]) == int(ref.float().argmax())
+
+
+@pytest.mark.parametrize("fmt", ["bf16", "fp8"])
+def test_batched_tensor_cores_teacher_forced(golden, fmt):
+    """B=12 streams (right-padded prompts) step through the tcgen05 GEMM path
+    (every fused epilogue: RoPE + cache write, SwiGLU, residual, argmax
+    feedback); each step starts from the oracle's cache state and every
+    stream's logits are compared with the oracle's."""
+    d, w, _ = golden
+    B, T, L = 12, 24, 96
+    gen = torch.Generator().manual_seed(3)
+    emb = torch.randn(B, T, d.hidden, generator=gen).to(torch.bfloat16)
+    pl = torch.randint(10, T + 1, (B,), generator=gen)
+    pl[0] = T
+    eng = GraniteEngine(d, w, fmt, max_cache_len=L, max_batch=B)
+    assert eng.layers[0]["qkv"].w_tc is not None
+    st = eng.new_state(B, 1, _lib.SB_MODE_DECODE, out_steps=1, prompt_len=pl, rope_off=T - pl)
+    odec = gr.OracleDecoder(gr.OracleModel(d, w, fmt=fmt), L, B=B)
+    odec.prefill(emb, pl)
+    kpos = torch.arange(L)
+    for i in range(6):
+        eng.load_cache_from(odec.cache.k, odec.cache.v)
+        tokens = torch.randint(0, d.vocab, (B,), generator=gen)
+        st.ids[:B] = tokens.to(st.ids.device)
+        st.set_slot(T + i, pad_len=T)
+        eng.decode_step(st, 0)
+        valid = (kpos[None, :] < pl[:, None]) | ((kpos >= T) & (kpos <= T + i))[None, :]
+        ref = odec.step(tokens, T + i - (T - pl), valid)
+        got = st.logits[:B].cpu()
+        for b in range(B):
+            err = (got[b].float() - ref[b].float()).abs().max()
+            assert err <= _logit_tol(ref[b]), f"{fmt} step {i} stream {b}: {err:.4g}"
+            if _margin(ref[b]) > _logit_tol(ref[b]):
+                assert int(st.out_ids[b]) == int(ref[b].argmax())
+        # the new cache rows (k after RoPE, v) equal the oracle's up to one
+        # bf16 rounding step of the head's largest element (RoPE's difference
+        # of two rounded products can cancel, so the bound is per head, not
+        # per element)
+        for li in range(d.layers):
+            for kv in range(2):
+                got_r = eng.kv[li, kv, :B, :, T + i].cpu().float()
+                ref_r = (odec.cache.k if kv == 0 else odec.cache.v)[li][:, :, T + i].float()
+                bound = 2 ** -6 * ref_r.abs().amax(-1, keepdim=True) + 1e-6
+                assert ((got_r - ref_r).abs() <= bound).all(), f"layer {li} {'kv'[kv]} row differs"

@@ -100,6 +100,64 @@ def test_linear(fmt, n, k, m):
     _close_bf16(y.cpu(), ref)
 
 
+def _linear_tc(p, x, pdl=0):
+    m = x.shape[0]
+    c = p.c_struct()
+    need = int(lib.sb_linear_workspace_bytes(C.byref(c), m))
+    assert need > 0, "tensor-core path not selected"
+    ws = torch.empty(need, dtype=torch.uint8, device="cuda")
+    y = torch.empty(m, p.n, dtype=BF16, device="cuda")
+    check(lib.sb_linear_ex(C.byref(c), ptr(x), ptr(y), m, ptr(ws), need, pdl, S()), "sb_linear_ex")
+    return y
+
+
+@pytest.mark.parametrize("fmt", ["bf16", "fp8"])
+@pytest.mark.parametrize("n,k,m", [(3072, 2048, 48), (2048, 8192, 48), (16384, 2048, 48), (2051, 512, 9),
+                                   (4096, 1024, 16), (1000, 2048, 33), (2048, 2048, 64), (640, 1024, 128),
+                                   (384, 512, 300)])
+def test_linear_tensor_cores(fmt, n, k, m):
+    """tcgen05 GEMM (9..128 rows per block, fp8 activations as two e4m3 terms)
+    vs the fp32 reference over the exactly dequantised weight: same bar as the
+    GEMV (one bf16 rounding step)."""
+    w = _w(n, k, seed=n + k + m)
+    x = torch.randn(m, k, generator=torch.Generator().manual_seed(6)).to(BF16)
+    p = pack.pack_matrix(w, fmt, tc=True)
+    p = _to_dev(p)
+    p.w_tc = p.w_tc.cuda()
+    y = _linear_tc(p, x.cuda())
+    ref = (x.float() @ _oracle_dense(w, fmt).T).to(BF16)
+    _close_bf16(y.cpu(), ref)
+
+
+def test_linear_tensor_cores_wide_range_rows():
+    """fp8 activation split: rows spanning many binades (and an all-zero row)
+    still match the fp32 reference."""
+    n, k, m = 512, 1024, 24
+    w = _w(n, k, seed=1)
+    g = torch.Generator().manual_seed(2)
+    x = torch.randn(m, k, generator=g) * torch.exp2(torch.randint(-12, 6, (m, k), generator=g).float())
+    x[3] = 0
+    x[5] *= 1e-20
+    x = x.to(BF16)
+    p = _to_dev(pack.pack_matrix(w, "fp8", tc=True))
+    p.w_tc = p.w_tc.cuda()
+    y = _linear_tc(p, x.cuda()).cpu()
+    ref = (x.float() @ _oracle_dense(w, "fp8").T).to(BF16)
+    assert torch.all(y[3] == 0)
+    _close_bf16(y, ref)
+
+
+def test_linear_tensor_cores_deterministic_and_pdl():
+    w = _w(2048, 8192, seed=4)
+    p = _to_dev(pack.pack_matrix(w, "fp8", tc=True))
+    p.w_tc = p.w_tc.cuda()
+    x = torch.randn(48, 8192, device="cuda").to(BF16)
+    y0 = _linear_tc(p, x, 0)
+    y1 = _linear_tc(p, x, 1)
+    y2 = _linear_tc(p, x, 0)
+    assert torch.equal(y0, y1) and torch.equal(y0, y2)
+
+
 def test_linear_pdl_same_as_plain():
     w = _w(2048, 2048, seed=3)
     p = _to_dev(pack.pack_matrix(w, "nvfp4"))

@@ -106,3 +106,36 @@ def test_row_permutations():
     assert sorted(perm.tolist()) == list(range(512))
     gu = pack.gate_up_perm(4)
     assert gu.tolist() == [0, 4, 1, 5, 2, 6, 3, 7]
+
+
+@pytest.mark.parametrize("fmt", ["bf16", "fp8"])
+def test_tensor_core_tile_layout(fmt):
+    """w_tc: byte (row, kbyte) of block (tile, kb) at rg*1024 + kc*128 + r*16 + b
+    (the no-swizzle K-major canonical layout of tcgen05.mma), padded rows zero,
+    holding the same (quantised) row bytes as the GEMV packing."""
+    n, k = 200, 256
+    w = _w(n, k, seed=9)
+    p = pack.pack_matrix(w, fmt, tc=True)
+    assert p.w_tc is not None
+    if fmt == "bf16":
+        rows = w.view(torch.int16).view(torch.uint8).reshape(n, 2 * k)
+    else:
+        q, _ = qr.quantize("fp8", w.float().numpy())
+        rows = torch.from_numpy(q.view(np.uint8).copy()).reshape(n, k)
+    kbytes = rows.shape[1]
+    t = p.w_tc
+    assert t.numel() == 256 * kbytes  # 200 rows -> 2 tiles of 128
+    KB = kbytes // 128
+    g = torch.Generator().manual_seed(0)
+    for _ in range(500):
+        row = int(torch.randint(0, 256, (1,), generator=g))
+        kb_ = int(torch.randint(0, kbytes, (1,), generator=g))
+        tile, rr = divmod(row, 128)
+        rg, r = divmod(rr, 8)
+        kb, kk = divmod(kb_, 128)
+        kc, b = divmod(kk, 16)
+        off = (tile * KB + kb) * 16384 + rg * 1024 + kc * 128 + r * 16 + b
+        want = int(rows[row, kb_]) if row < n else 0
+        assert int(t[off]) == want
+    assert torch.equal(pack.tc_untile(t, n, kbytes), rows)
+    assert pack.pack_matrix(w, "nvfp4", tc=True).w_tc is None  # no tile copy for nvfp4
