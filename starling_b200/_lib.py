@@ -16,7 +16,7 @@ LIB_PATH = Path(os.environ.get("STARLING_B200_LIB", _PKG / "libstarling_b200.so"
 SB_FMT = {"bf16": 0, "fp8": 1, "int8": 2, "nvfp4": 3}
 KGROUP_ELEMS = {"bf16": 16, "fp8": 32, "int8": 32, "nvfp4": 64}
 
-SB_CTRL_SLOT, SB_CTRL_PADLEN, SB_CTRL_ACCEPT, SB_CTRL_WORDS = 0, 1, 2, 8
+SB_CTRL_SLOT, SB_CTRL_PADLEN, SB_CTRL_ACCEPT, SB_CTRL_ERR, SB_CTRL_WORDS = 0, 1, 2, 3, 8
 SB_MODE_DECODE, SB_MODE_VERIFY, SB_MODE_FIRST = 0, 1, 2
 SB_OP_QKV, SB_OP_ATTN, SB_OP_O, SB_OP_GATE_UP, SB_OP_DOWN, SB_OP_LM_HEAD = range(6)
 

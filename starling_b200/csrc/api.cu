@@ -129,8 +129,13 @@ static int run_linear(const SbLinear& l, GemvParams& p, void* tc_scratch, size_t
   return run_gemv(p, l.fmt, pdl, s);
 }
 
-static int attn_split(int max_len) {
-  int s = (max_len + 63) / 64;
+// CTAs per (stream, KV head): enough (stream, head) groups fill the GPU on
+// their own; few groups split their keys over a cluster of up to 8 CTAs.
+static int attn_split(int groups, int max_len) {
+  if (groups >= 148) return 1;
+  int s = (2 * 148 + groups - 1) / groups;
+  const int by_len = (max_len + 63) / 64;  // at least one 64-key tile per CTA
+  if (s > by_len) s = by_len;
   return s < 1 ? 1 : (s > 8 ? 8 : s);
 }
 
@@ -140,8 +145,8 @@ static int check_state(const SbModel* md, const SbState* st) {
     return fail(SB_ERR_ARG, "batch*m must be in [1, 64] (batch=%d m=%d)", st->batch, st->m);
   if (st->batch > md->max_batch) return fail(SB_ERR_ARG, "batch %d > model max_batch %d", st->batch, md->max_batch);
   if (md->head_dim != 128) return fail(SB_ERR_ARG, "head_dim must be 128");
-  if (md->n_q % md->n_kv != 0 || (md->n_q / md->n_kv) * st->m > 128)
-    return fail(SB_ERR_ARG, "query rows per KV head (n_q/n_kv * m) must be <= 128");
+  if (md->n_q % md->n_kv != 0 || (md->n_q / md->n_kv) * st->m > 64)
+    return fail(SB_ERR_ARG, "query rows per KV head (n_q/n_kv * m) must be <= 64");
   if (!st->ids || !st->ctrl || !st->hidden || !st->q || !st->attn || !st->act || !st->workspace)
     return fail(SB_ERR_ARG, "state buffer missing");
   if (st->mode < SB_MODE_DECODE || st->mode > SB_MODE_FIRST) return fail(SB_ERR_ARG, "bad mode");
@@ -280,8 +285,12 @@ static int launch_attention(const SbModel* md, const SbState* st, int l, cudaStr
   a.attn_mult = md->attn_mult;
   a.ctrl = st->ctrl;
   a.prompt_len = st->prompt_len;
-  a.split = attn_split(md->max_len);
-  a.chunk_cap = (md->max_len + a.split - 1) / a.split;
+  a.split = attn_split(st->batch * md->n_kv, md->max_len);
+  a.chunk_cap = attn_key_capacity(md->max_len, a.split);
+  const int tiles = a.chunk_cap / 64;  // K tiles per CTA at most (as many V tiles)
+  a.slots = 2 * tiles < 4 ? 2 * tiles : 4;
+  if (a.slots < 2) a.slots = 2;
+  a.cache_rows = static_cast<long long>(md->max_batch) * md->n_kv * md->max_len;
   const int rc = attn_launch(a, st->batch, st->use_pdl != 0, s);
   if (rc == SB_ERR_CONFIG) return fail(rc, "no attention configuration (rows=%d)", (md->n_q / md->n_kv) * st->m);
   if (rc != 0) return fail(rc, "attention launch: %s", cudaGetErrorString((cudaError_t)rc));

@@ -5,17 +5,32 @@
 // transformers modeling_granite.py:89-112): repeat_kv copies of K/V, a
 // scores matmul over all max_cache_len slots, an additive -max mask, an fp32
 // softmax cast to bf16 and a probs @ V matmul.  Here:
-//  * no repeat_kv: one cluster serves one (stream, KV head) and all of its
-//    query heads (and, for verify, all query tokens) at once;
-//  * only keys that can be valid are read: [0, slot + m) with right-padding
-//    holes [prompt_len, pad_len) skipped, which is exactly the set the
-//    reference's mask leaves at 0 (masked slots contribute exp(-inf) = 0);
-//  * the `split` CTAs of a cluster each take a slice of the keys; the
-//    softmax max and sum and the P.V partials are combined across the
-//    cluster through distributed shared memory in a fixed order;
+//  * no repeat_kv: one CTA (or a cluster of `split` CTAs) serves one
+//    (stream, KV head) and all of its query heads (and, for verify, all query
+//    tokens) at once;
+//  * only keys that can be valid are read: the prompt part [0, prompt_len)
+//    and the generated part [pad_len, slot + m), skipping the right-padding
+//    hole, which is exactly the set the reference's mask leaves at 0 (masked
+//    slots contribute exp(-inf) = 0).  Each part is cut into tiles of 64
+//    keys; the tiles are shared out over the cluster;
+//  * K tiles and then V tiles stream through a ring of shared-memory slots by
+//    TMA (cp.async.bulk.tensor, 128-byte swizzle, two 64-dim boxes per tile)
+//    completing on mbarriers.  Tiles whose keys are all older than this
+//    step are issued BEFORE griddepcontrol.wait, so those loads overlap the
+//    q/k/v GEMM that precedes the attention;
+//  * both contractions run on the tensor cores (mma.sync m16n8k16, bf16 in,
+//    fp32 accumulate): scores^T = K . Q^T per tile with ldmatrix from the
+//    swizzled tile (conflict-free), then P . V with ldmatrix.trans.  bf16
+//    products are exact, so this is the reference's bf16 matmul up to the
+//    fp32 summation order;
 //  * rounding points follow the reference: score = bf16(bf16(q.k) * scale),
-//    p = bf16(exp(s - max) * (1/sum)) in fp32, out = bf16(sum_j p_j v_j).
+//    p = bf16(exp(s - max) * (1/sum)) in fp32 with the max and sum over ALL
+//    keys (combined across the cluster through distributed shared memory in
+//    rank order), out = bf16(sum_j p_j v_j).
+// Every ring wait is bounded; on expiry the kernel records SB_CTRL_ERR = 3
+// and carries on with invalid results instead of hanging.
 #include <cooperative_groups.h>
+#include <cudaTypedefs.h>
 
 #include "attention.cuh"
 
@@ -23,188 +38,383 @@ namespace cg = cooperative_groups;
 
 namespace sb {
 
-__global__ void __launch_bounds__(256) k_attn(const __grid_constant__ AttnParams p) {
-  extern __shared__ __align__(16) uint8_t smem[];
-  cg::cluster_group cl = cg::this_cluster();
-  const int rank = static_cast<int>(cl.block_rank());
+namespace {
+
+__device__ __forceinline__ uint32_t su32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t n) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(n) : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(su32(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// 2D TMA tile load (no multicast) of box {64 dims, 64 keys} at (x, y).
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          su32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(su32(bar))
+      : "memory");
+}
+__device__ __forceinline__ uint64_t gtimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __noinline__ void ring_wait(uint64_t* bar, uint32_t parity, int32_t* err) {
+  if (mbar_try_wait(bar, parity)) return;
+  const uint64_t t0 = gtimer();
+  for (;;) {
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait(bar, parity)) return;
+    if (gtimer() - t0 > 2000000000ull) {
+      if (err) atomicExch(err, 3);
+      return;
+    }
+  }
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t* r) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t* r) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+// byte offset of (row, 16-byte chunk) in a 128-byte-swizzled box of 128-byte rows
+__device__ __forceinline__ uint32_t swz(int row, int chunk) {
+  return static_cast<uint32_t>(row * 128 + ((chunk ^ (row & 7)) << 4));
+}
+
+constexpr int kTK = 64;                // keys per tile
+constexpr int kTileBytes = kTK * 256;  // two swizzled 64-dim boxes of 8 KiB
+
+}  // namespace
+
+// Shared-memory layout (offsets from a 1024-byte-aligned base), identical on
+// host and device.  cap = keys per CTA at most (a multiple of 64).
+struct AttnLayout {
+  size_t ring, bars, qb, sc, pb, outp, stat, zero, total;
+};
+__host__ __device__ inline AttnLayout attn_layout(int R, int cap, int slots) {
+  auto up = [](size_t x) { return (x + 15) & ~size_t(15); };
+  const int R16 = (R + 15) / 16 * 16;
+  AttnLayout L;
+  L.ring = 0;
+  L.bars = static_cast<size_t>(slots) * kTileBytes;
+  L.qb = up(L.bars + 8 * static_cast<size_t>(slots));
+  L.sc = up(L.qb + static_cast<size_t>(R16) * 136 * 2);            // q bf16 [R16][136]
+  L.pb = up(L.sc + static_cast<size_t>(R) * cap * 4);              // scores f32 [R][cap]
+  L.outp = up(L.pb + static_cast<size_t>(R) * (cap + 8) * 2);      // p bf16 [R][cap + 8]
+  L.stat = up(L.outp + static_cast<size_t>(R) * 128 * 4);          // P.V f32 [R][128]
+  L.zero = up(L.stat + 2 * static_cast<size_t>(R) * 4);            // max, sum [R]
+  L.total = up(L.zero + 16) + 1024;                                // + alignment slack
+  return L;
+}
+
+__global__ void __launch_bounds__(256, 2)
+    k_attn(const __grid_constant__ AttnParams p, const __grid_constant__ CUtensorMap tmk,
+           const __grid_constant__ CUtensorMap tmv) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (su32(smem_raw) & 1023)) & 1023);
   const int split = p.split;
+  const int rank = split > 1 ? static_cast<int>(cg::this_cluster().block_rank()) : 0;
   const int kvh = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, c = lane & 3;
   const int G = p.n_q / p.n_kv;
   const int R = G * p.m_per;
+  const int cap = p.chunk_cap;
+  const int pst = cap + 8;  // p row stride (elements): 16 mod 128 bytes -> conflict-free ldmatrix
+  const AttnLayout L = attn_layout(R, cap, p.slots);
+  uint8_t* ring = smem + L.ring;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
+  uint16_t* qb = reinterpret_cast<uint16_t*>(smem + L.qb);
+  float* sc = reinterpret_cast<float*>(smem + L.sc);
+  uint16_t* pb = reinterpret_cast<uint16_t*>(smem + L.pb);
+  float* outp = reinterpret_cast<float*>(smem + L.outp);
+  float* smax = reinterpret_cast<float*>(smem + L.stat);
+  float* ssum = smax + R;
+  uint16_t* zrow = reinterpret_cast<uint16_t*>(smem + L.zero);  // 16 zero bytes
+  int32_t* err = p.ctrl + SB_CTRL_ERR;
 
+  // ---- this CTA's tiles (device values that are stable before the wait: the
+  // slot and the lengths were written by kernels that precede the q/k/v GEMM)
   const int slot = p.ctrl[SB_CTRL_SLOT];
   const int pad_len = p.ctrl[SB_CTRL_PADLEN];
-  const int plen = p.prompt_len ? p.prompt_len[b] : 0x7fffffff;
   int kv_len = slot + p.m_per;
   kv_len = kv_len > p.max_len ? p.max_len : kv_len;
-  const int chunk = (kv_len + split - 1) / split;
-  const int lo = rank * chunk;
-  const int hi = min(kv_len, lo + chunk);
-  const int nk = hi > lo ? hi - lo : 0;
+  const int plen = p.prompt_len ? p.prompt_len[b] : kv_len;
+  const int n1 = plen < kv_len ? plen : kv_len;     // prompt part [0, n1)
+  const int g0 = plen < pad_len ? pad_len : n1;     // generated part [g0, kv_len)
+  const int n2 = kv_len > g0 ? kv_len - g0 : 0;
+  const int t1 = (n1 + kTK - 1) / kTK, t2 = (n2 + kTK - 1) / kTK;
+  const int per = (t1 + t2 + split - 1) / split;
+  const int i0 = rank * per < t1 + t2 ? rank * per : t1 + t2;
+  const int nT = (i0 + per < t1 + t2 ? i0 + per : t1 + t2) - i0;  // this CTA's tiles
+  auto tstart = [&](int u) { const int i = i0 + u; return i < t1 ? kTK * i : g0 + kTK * (i - t1); };
+  auto trows = [&](int u) {
+    const int i = i0 + u;
+    const int e = i < t1 ? n1 : kv_len, s0 = tstart(u);
+    return e - s0 < kTK ? e - s0 : kTK;
+  };
+  const int head_row0 = (b * p.n_kv + kvh) * p.max_len;
+  auto issue = [&](int it) {  // item it: K tile it (< nT) or V tile it - nT -> slot it % slots
+    const int u = it < nT ? it : it - nT;
+    const CUtensorMap* tm = it < nT ? &tmk : &tmv;
+    uint8_t* dst = ring + static_cast<size_t>(it % p.slots) * kTileBytes;
+    uint64_t* bar = bars + (it % p.slots);
+    tma_load_2d(dst, tm, 0, head_row0 + tstart(u), bar);
+    tma_load_2d(dst + kTileBytes / 2, tm, 64, head_row0 + tstart(u), bar);
+  };
+  auto fresh = [&](int it) {  // the tile holds a key written by the preceding kernel
+    const int u = it < nT ? it : it - nT;
+    return tstart(u) + trows(u) > slot;
+  };
 
-  const size_t head_base = (static_cast<size_t>(b) * p.n_kv + kvh) * p.max_len;
-  const uint16_t* kc = p.k_cache + head_base * 128;
-  const uint16_t* vc = p.v_cache + head_base * 128;
-  if (tid == 0 && nk > 0) {
-    prefetch_l2(kc + static_cast<size_t>(lo) * 128, static_cast<uint32_t>(nk) * 256u);
-    prefetch_l2(vc + static_cast<size_t>(lo) * 128, static_cast<uint32_t>(nk) * 256u);
+  const int total = 2 * nT;
+  const int first = total < p.slots ? total : p.slots;
+  if (tid == 0) {
+    for (int s = 0; s < p.slots; ++s) mbar_init(bars + s, 1);
+    mbar_fence_init();
+    for (int it = 0; it < first; ++it) {
+      mbar_expect_tx(bars + it, kTileBytes);
+      if (!fresh(it)) issue(it);
+    }
   }
+  __syncthreads();
   pdl_wait();
   pdl_launch();
+  if (tid == 0)
+    for (int it = 0; it < first; ++it)
+      if (fresh(it)) issue(it);
 
-  float* qs = reinterpret_cast<float*>(smem);        // [R][128]
-  float* sc = qs + R * 128;                          // [R][chunk_cap]
-  float* part = sc + R * p.chunk_cap;                // [16][4][128]
-  float* outp = part + 16 * 4 * 128;                 // [R][128]
-  float* smax = outp + R * 128;                      // [R]
-  float* ssum = smax + 128;                          // [R]
-
-  // q rows of this KV group: row r = (token mi, head gi)
-  for (int i = tid; i < R * 128; i += blockDim.x) {
-    const int r = i >> 7, d = i & 127;
-    const int mi = r / G, gi = r % G;
-    const size_t t = static_cast<size_t>(b) * p.m_per + mi;
-    qs[i] = u16_to_f(p.q[t * p.n_q * 128 + (kvh * G + gi) * 128 + d]);
+  // q rows of this KV group (row r = (token mi, head gi)) as bf16; rows >= R zero
+  const int R16 = (R + 15) / 16 * 16;
+  for (int i = tid; i < R16 * 64; i += blockDim.x) {
+    const int r = i >> 6, d2 = (i & 63) * 2;
+    uint32_t v = 0;
+    if (r < R) {
+      const int mi = r / G, gi = r % G;
+      const size_t t = static_cast<size_t>(b) * p.m_per + mi;
+      v = *reinterpret_cast<const uint32_t*>(p.q + t * p.n_q * 128 + (kvh * G + gi) * 128 + d2);
+    }
+    *reinterpret_cast<uint32_t*>(qb + r * 136 + d2) = v;
   }
+  if (tid < 4) reinterpret_cast<uint32_t*>(zrow)[tid] = 0u;
   __syncthreads();
 
-  // ---- scores: a half-warp per key, 8 dims per lane --------------------------------
-  const int hw = tid >> 4, l16 = tid & 15;
-  // Both half-warps of a warp run the same trip count (the shuffles below
-  // use the full mask); the odd key of a pair past the end is predicated off.
-  for (int jb = hw & ~1; jb < nk; jb += 16) {
-    const int jj = jb + (hw & 1);
-    const bool live = jj < nk;
-    const int j = lo + (live ? jj : 0);
-    float kf[8];
-    {
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (live) v = *reinterpret_cast<const uint4*>(kc + static_cast<size_t>(j) * 128 + l16 * 8);
-      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  const int NT = (R + 7) / 8;    // q-row n-tiles of the score MMA
+  const int MT = (R + 15) / 16;  // q-row m-tiles of the P.V MMA
+  float acc[4][2][4];            // P.V accumulators [m-tile][n-tile][frag]
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        kf[2 * i] = __uint_as_float(w[i] << 16);
-        kf[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
-      }
-    }
-    const bool hole = j >= plen && j < pad_len;
-    for (int r = 0; r < R; ++r) {
-      const float* qr = qs + r * 128 + l16 * 8;
-      float d = 0.f;
+  for (int a = 0; a < 4; ++a)
 #pragma unroll
-      for (int i = 0; i < 8; ++i) d = fmaf(qr[i], kf[i], d);
-      d += __shfl_xor_sync(0xffffffffu, d, 8);
-      d += __shfl_xor_sync(0xffffffffu, d, 4);
-      d += __shfl_xor_sync(0xffffffffu, d, 2);
-      d += __shfl_xor_sync(0xffffffffu, d, 1);
-      if (l16 == 0 && live) {
-        const int mi = r / G;
-        const bool valid = !hole && j <= slot + mi;
-        sc[r * p.chunk_cap + jj] = valid ? bf(bf(d) * p.attn_mult) : -INFINITY;
-      }
-    }
-  }
-  __syncthreads();
+    for (int n = 0; n < 2; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[a][n][e] = 0.f;
 
-  // ---- softmax statistics across the cluster ------------------------------------------
-  for (int r = warp; r < R; r += 8) {
-    float m = -INFINITY;
-    for (int jj = lane; jj < nk; jj += 32) m = fmaxf(m, sc[r * p.chunk_cap + jj]);
-    m = warp_max(m);
-    if (lane == 0) smax[r] = m;
-  }
-  cl.sync();
-  for (int r = warp; r < R; r += 8) {
-    float gm = -INFINITY;
-    for (int q = 0; q < split; ++q) gm = fmaxf(gm, cl.map_shared_rank(smax, q)[r]);
-    float s = 0.f;
-    for (int jj = lane; jj < nk; jj += 32) {
-      float* e = sc + r * p.chunk_cap + jj;
-      const float ev = gm == -INFINITY ? 0.f : expf(*e - gm);
-      *e = ev;
-      s += ev;
+  auto softmax = [&]() {
+    const int nk = nT * kTK;
+    for (int r = warp; r < R; r += 8) {
+      float m = -INFINITY;
+      for (int jj = lane; jj < nk; jj += 32) m = fmaxf(m, sc[r * cap + jj]);
+      m = warp_max(m);
+      if (lane == 0) smax[r] = m;
     }
-    s = warp_sum(s);
-    if (lane == 0) ssum[r] = s;
-  }
-  cl.sync();
-  for (int r = warp; r < R; r += 8) {
-    float gs = 0.f;
-    for (int q = 0; q < split; ++q) gs += cl.map_shared_rank(ssum, q)[r];
-    const float inv = 1.f / gs;
-    for (int jj = lane; jj < nk; jj += 32) {
-      float* e = sc + r * p.chunk_cap + jj;
-      *e = bf(*e * inv);  // softmax(..., dtype=float32).to(bf16)
-    }
-  }
-  __syncthreads();
-
-  // ---- P.V partial: thread = (key group kg, 8 dims dc), rows in blocks of 4 ---------
-  const int dc = tid & 15, kgp = tid >> 4;
-  for (int r0 = 0; r0 < R; r0 += 4) {
-    const int nr = min(4, R - r0);
-    float acc[4][8];
-#pragma unroll
-    for (int a = 0; a < 4; ++a)
-#pragma unroll
-      for (int i = 0; i < 8; ++i) acc[a][i] = 0.f;
-    for (int jj = kgp; jj < nk; jj += 16) {
-      const uint4 v = *reinterpret_cast<const uint4*>(vc + static_cast<size_t>(lo + jj) * 128 + dc * 8);
-      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-      float vf[8];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        vf[2 * i] = __uint_as_float(w[i] << 16);
-        vf[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    if (split > 1) cg::this_cluster().sync(); else __syncthreads();
+    for (int r = warp; r < R; r += 8) {
+      float gm = -INFINITY;
+      for (int q = 0; q < split; ++q)
+        gm = fmaxf(gm, split > 1 ? cg::this_cluster().map_shared_rank(smax, q)[r] : smax[r]);
+      float s = 0.f;
+      for (int jj = lane; jj < nk; jj += 32) {
+        float* e = sc + r * cap + jj;
+        const float ev = gm == -INFINITY ? 0.f : expf(*e - gm);
+        *e = ev;
+        s += ev;
       }
+      s = warp_sum(s);
+      if (lane == 0) ssum[r] = s;
+    }
+    if (split > 1) cg::this_cluster().sync(); else __syncthreads();
+    for (int r = warp; r < R; r += 8) {
+      float gs = 0.f;
+      for (int q = 0; q < split; ++q) gs += split > 1 ? cg::this_cluster().map_shared_rank(ssum, q)[r] : ssum[r];
+      const float inv = 1.f / gs;
+      for (int jj = lane; jj < nk; jj += 32)
+        pb[r * pst + jj] = f_to_bf16_bits(sc[r * cap + jj] * inv);  // softmax(..., float32).to(bf16)
+    }
+    __syncthreads();
+  };
+
+  for (int it = 0; it < total; ++it) {
+    if (it == nT) softmax();
+    ring_wait(bars + (it % p.slots), static_cast<uint32_t>((it / p.slots) & 1), err);
+    const uint32_t tile = su32(ring + static_cast<size_t>(it % p.slots) * kTileBytes);
+    if (it < nT) {
+      // ---- scores^T[key][row] = K . Q^T: warp w < 4 takes keys 16w..16w+15 of the tile
+      if (warp < 4) {
+        const int u = it;
+        float d[8][4];
 #pragma unroll
-      for (int a = 0; a < 4; ++a) {
-        if (a < nr) {
-          const float pr = sc[(r0 + a) * p.chunk_cap + jj];
+        for (int n = 0; n < 8; ++n)
 #pragma unroll
-          for (int i = 0; i < 8; ++i) acc[a][i] = fmaf(pr, vf[i], acc[a][i]);
+          for (int e = 0; e < 4; ++e) d[n][e] = 0.f;
+        const int arow = warp * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          uint32_t a[4];
+          ldsm_x4(tile + (ks >> 2) * (kTileBytes / 2) + swz(arow, (ks & 3) * 2 + (lane >> 4)), a);
+#pragma unroll
+          for (int n = 0; n < 8; ++n) {
+            if (n < NT) {
+              const uint16_t* qr = qb + (n * 8 + g) * 136 + ks * 16 + 2 * c;
+              mma_bf16(d[n], a, *reinterpret_cast<const uint32_t*>(qr), *reinterpret_cast<const uint32_t*>(qr + 8));
+            }
+          }
+        }
+        const int rows = trows(u), k0 = tstart(u);
+#pragma unroll
+        for (int n = 0; n < 8; ++n) {
+          if (n < NT) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int key = warp * 16 + g + (e >> 1) * 8;  // key within the tile
+              const int r = n * 8 + 2 * c + (e & 1);         // q row
+              if (r < R) {
+                const int mi = r / G;
+                const bool ok = key < rows && k0 + key <= slot + mi;
+                sc[r * cap + u * kTK + key] = ok ? bf(bf(d[n][e]) * p.attn_mult) : -INFINITY;
+              }
+            }
+          }
+        }
+      }
+    } else {
+      // ---- out[row][dim] += P . V: warp w takes dims 16w..16w+15 (two n-tiles)
+      const int u = it - nT;
+      const int vrow_l = (lane & 7) + 8 * ((lane >> 3) & 1);
+      const int dchunk = warp * 2 + (lane >> 4);  // 8-dim chunk 0..15
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        uint32_t bv[4];
+        ldsm_x4_t(tile + (dchunk >> 3) * (kTileBytes / 2) + swz(ks * 16 + vrow_l, dchunk & 7), bv);
+#pragma unroll
+        for (int mt = 0; mt < 4; ++mt) {
+          if (mt < MT) {
+            const int prow = mt * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
+            const int pkey = u * kTK + ks * 16 + 8 * (lane >> 4);
+            const uint16_t* pa = prow < R ? pb + prow * pst + pkey : zrow;
+            uint32_t a[4];
+            ldsm_x4(su32(pa), a);
+            mma_bf16(acc[mt][0], a, bv[0], bv[1]);
+            mma_bf16(acc[mt][1], a, bv[2], bv[3]);
+          }
         }
       }
     }
-#pragma unroll
-    for (int a = 0; a < 4; ++a)
-#pragma unroll
-      for (int i = 0; i < 8; ++i) part[(kgp * 4 + a) * 128 + dc * 8 + i] = acc[a][i];
-    __syncthreads();
-    for (int i = tid; i < nr * 128; i += blockDim.x) {
-      const int a = i >> 7, d = i & 127;
-      float s = 0.f;
-      for (int q = 0; q < 16; ++q) s += part[(q * 4 + a) * 128 + d];
-      outp[(r0 + a) * 128 + d] = s;
+    __syncthreads();  // slot it % slots is free
+    if (tid == 0 && it + p.slots < total) {
+      const int nx = it + p.slots;
+      mbar_expect_tx(bars + (nx % p.slots), kTileBytes);
+      issue(nx);
+    }
+  }
+  if (nT == 0) {  // no keys here: still take part in the cluster's statistics exchange
+    for (int r = tid; r < R; r += blockDim.x) {
+      smax[r] = -INFINITY;
+      ssum[r] = 0.f;
+    }
+    if (split > 1) {
+      cg::this_cluster().sync();
+      cg::this_cluster().sync();
     }
     __syncthreads();
+  }
+
+  // ---- this CTA's P.V rows -> outp ---------------------------------------------------------
+#pragma unroll
+  for (int mt = 0; mt < 4; ++mt) {
+    if (mt < MT) {
+#pragma unroll
+      for (int n = 0; n < 2; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int r = mt * 16 + g + (e >> 1) * 8;
+          const int dim = warp * 16 + n * 8 + 2 * c + (e & 1);
+          if (r < R) outp[r * 128 + dim] = acc[mt][n][e];
+        }
+    }
   }
 
   // ---- combine the cluster's partial outputs, round, store -----------------------------
-  cl.sync();
+  if (split > 1) cg::this_cluster().sync(); else __syncthreads();
   if (rank == 0) {
     for (int i = tid; i < R * 128; i += blockDim.x) {
       float s = 0.f;
-      for (int q = 0; q < split; ++q) s += cl.map_shared_rank(outp, q)[i];
-      const int r = i >> 7, d = i & 127;
+      for (int q = 0; q < split; ++q) s += split > 1 ? cg::this_cluster().map_shared_rank(outp, q)[i] : outp[i];
+      const int r = i >> 7, dd = i & 127;
       const int mi = r / G, gi = r % G;
       const size_t t = static_cast<size_t>(b) * p.m_per + mi;
-      p.out[t * p.n_q * 128 + (kvh * G + gi) * 128 + d] = f_to_bf16_bits(s);
+      p.out[t * p.n_q * 128 + (kvh * G + gi) * 128 + dd] = f_to_bf16_bits(s);
     }
   }
-  cl.sync();
+  if (split > 1) cg::this_cluster().sync();
 }
 
-size_t attn_smem_bytes(int R, int chunk_cap) {
-  return (static_cast<size_t>(R) * 128 * 2 + static_cast<size_t>(R) * chunk_cap + 16 * 4 * 128 + 128 * 2) * 4 + 16;
+// ---- host side ------------------------------------------------------------------
+size_t attn_smem_bytes(int R, int chunk_cap, int slots) { return attn_layout(R, chunk_cap, slots).total; }
+
+int attn_key_capacity(int max_len, int split) {
+  const int tiles = (max_len + kTK - 1) / kTK + 1;  // the padding hole can cut one tile in two
+  return (tiles + split - 1) / split * kTK;
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  }
+  return fn;
+}
+
+// [rows][128] bf16 cache viewed as a 2D tensor; box {64 dims, 64 keys}, 128B swizzle.
+static int cache_map(CUtensorMap* tm, const uint16_t* base, long long rows) {
+  auto fn = encode_fn();
+  if (!fn) return SB_ERR_CONFIG;
+  cuuint64_t dims[2] = {128, static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {256};
+  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(kTK)};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : SB_ERR_CONFIG;
 }
 
 int attn_launch(const AttnParams& p, int batch, bool pdl, cudaStream_t stream) {
   const int R = (p.n_q / p.n_kv) * p.m_per;
-  if (R > 128 || R < 1 || p.split < 1 || p.split > 8) return SB_ERR_CONFIG;
-  const size_t smem = attn_smem_bytes(R, p.chunk_cap);
+  if (R > 64 || R < 1 || p.split < 1 || p.split > 8 || p.slots < 2 || p.chunk_cap % kTK) return SB_ERR_CONFIG;
+  const size_t smem = attn_smem_bytes(R, p.chunk_cap, p.slots);
   if (smem > 200 * 1024) return SB_ERR_CONFIG;
+  CUtensorMap tmk, tmv;
+  if (cache_map(&tmk, p.k_cache, p.cache_rows) || cache_map(&tmv, p.v_cache, p.cache_rows)) return SB_ERR_CONFIG;
   int dev = 0;
   cudaGetDevice(&dev);
   static unsigned configured = 0;
@@ -219,19 +429,22 @@ int attn_launch(const AttnParams& p, int batch, bool pdl, cudaStream_t stream) {
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attrs[2];
-  attrs[0].id = cudaLaunchAttributeClusterDimension;
-  attrs[0].val.clusterDim.x = p.split;
-  attrs[0].val.clusterDim.y = 1;
-  attrs[0].val.clusterDim.z = 1;
-  int na = 1;
+  int na = 0;
+  if (p.split > 1) {
+    attrs[na].id = cudaLaunchAttributeClusterDimension;
+    attrs[na].val.clusterDim.x = p.split;
+    attrs[na].val.clusterDim.y = 1;
+    attrs[na].val.clusterDim.z = 1;
+    ++na;
+  }
   if (pdl) {
-    attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attrs[1].val.programmaticStreamSerializationAllowed = 1;
-    na = 2;
+    attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
   }
   cfg.attrs = attrs;
   cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, k_attn, p);
+  return cudaLaunchKernelEx(&cfg, k_attn, p, tmk, tmv);
 }
 
 }  // namespace sb

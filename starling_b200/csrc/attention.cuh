@@ -11,13 +11,16 @@ struct AttnParams {
   uint16_t* out;  // [B*m_per][n_q*128]
   int n_q, n_kv, max_len, m_per;
   float attn_mult;
-  const int32_t* ctrl;        // SB_CTRL_SLOT, SB_CTRL_PADLEN
+  int32_t* ctrl;              // SB_CTRL_SLOT, SB_CTRL_PADLEN (read), SB_CTRL_ERR (written on a failed wait)
   const int32_t* prompt_len;  // [B] or nullptr
-  int split;                  // CTAs per cluster splitting the keys
-  int chunk_cap;              // ceil(max_len / split)
+  int split;                  // CTAs per (stream, KV head), one cluster
+  int chunk_cap;              // keys per CTA at most: attn_key_capacity(max_len, split)
+  int slots;                  // ring slots of 64 keys (K or V)
+  long long cache_rows;       // max_batch * n_kv * max_len (rows of 128 of each cache)
 };
 
-size_t attn_smem_bytes(int R, int chunk_cap);
+int attn_key_capacity(int max_len, int split);
+size_t attn_smem_bytes(int R, int chunk_cap, int slots);
 int attn_launch(const AttnParams& p, int batch, bool pdl, cudaStream_t stream);
 
 }  // namespace sb

@@ -230,3 +230,62 @@ def test_argmax_first_max():
     check(lib.sb_argmax_bf16(ptr(xd), 3, 100353, ptr(out), S()))
     assert out.cpu().tolist() == [17, 0, 100352]
     assert out.cpu().tolist() == x.float().argmax(-1).tolist()
+
+
+def _attn_engine(B, max_len, n_q=8, n_kv=4):
+    from starling_b200.engine import GraniteDims, GraniteEngine
+
+    d = GraniteDims(hidden=1024, n_q=n_q, n_kv=n_kv, inter=1024, vocab=256, layers=1)
+    g = torch.Generator(device="cuda").manual_seed(1)
+    shapes = {"embed_tokens.weight": (256, 1024), "norm.weight": (1024,),
+              "layers.0.input_layernorm.weight": (1024,), "layers.0.post_attention_layernorm.weight": (1024,),
+              "layers.0.self_attn.q_proj.weight": (n_q * 128, 1024), "layers.0.self_attn.k_proj.weight": (n_kv * 128, 1024),
+              "layers.0.self_attn.v_proj.weight": (n_kv * 128, 1024), "layers.0.self_attn.o_proj.weight": (1024, n_q * 128),
+              "layers.0.mlp.gate_proj.weight": (1024, 1024), "layers.0.mlp.up_proj.weight": (1024, 1024),
+              "layers.0.mlp.down_proj.weight": (1024, 1024)}
+    w = {k: (torch.randn(s, generator=g, device="cuda") * 0.02).to(BF16) for k, s in shapes.items()}
+    return GraniteEngine(d, w, "bf16", max_cache_len=max_len, max_batch=B, tensor_cores=False)
+
+
+def _attn_reference(q, kc, vc, valid, n_q, n_kv, m, mult):
+    """The reference's eager attention (llm_mega.py:549-556, modeling_granite.py:89-112)
+    on CPU: bf16 matmuls, additive -max mask, fp32 softmax cast to bf16."""
+    B = kc.shape[0]
+    qh = q.view(B, m, n_q, 128).transpose(1, 2)  # (B, n_q, m, 128)
+    kr, vr = gr.repeat_kv(kc, n_q // n_kv), gr.repeat_kv(vc, n_q // n_kv)
+    sc = torch.matmul(qh, kr.transpose(2, 3)) * mult
+    mask = torch.zeros(valid.shape, dtype=BF16).masked_fill_(~valid, gr.NEG)  # (B, m, L)
+    sc = sc + mask[:, None]
+    pr = torch.nn.functional.softmax(sc, dim=-1, dtype=torch.float32).to(BF16)
+    return torch.matmul(pr, vr).transpose(1, 2).reshape(B * m, n_q * 128)
+
+
+@pytest.mark.parametrize("B,m,max_len,slot,holes", [(40, 1, 700, 650, True), (40, 1, 700, 650, False),
+                                                     (3, 1, 700, 400, True), (1, 9, 640, 600, False),
+                                                     (2, 4, 300, 120, True)])
+def test_attention_vs_reference(B, m, max_len, slot, holes):
+    """sb_attention (one CTA per (stream, head) when the groups fill the GPU,
+    else a cluster split; multi-tile key rings; right-padding holes; verify
+    rows with the causal block) vs the reference's eager attention."""
+    eng = _attn_engine(B, max_len)
+    d = eng.dims
+    g = torch.Generator().manual_seed(B * 1000 + slot)
+    pad_len = slot - 5 if holes else slot
+    pl = torch.randint(pad_len // 3, pad_len + 1, (B,), generator=g) if holes else torch.full((B,), pad_len)
+    pl[0] = pad_len
+    st = eng.new_state(B, m, _lib.SB_MODE_DECODE, out_steps=1, prompt_len=pl, rope_off=pad_len - pl)
+    kc = (torch.randn(B, d.n_kv, max_len, 128, generator=g) * 2).to(BF16)
+    vc = torch.randn(B, d.n_kv, max_len, 128, generator=g).to(BF16)
+    q = (torch.randn(B * m, d.n_q * 128, generator=g) * 2).to(BF16)
+    eng.kv[0, 0, :B].copy_(kc)
+    eng.kv[0, 1, :B].copy_(vc)
+    st.q.copy_(q)
+    st.set_slot(slot, pad_len=pad_len)
+    check(lib.sb_attention(C.byref(eng.cmodel), C.byref(st.c), 0, S()), "sb_attention")
+    kpos = torch.arange(max_len)
+    # row token mi sees [0, prompt_len) and [pad_len, slot + mi]
+    valid = ((kpos[None, None, :] < pl[:, None, None]) |
+             ((kpos[None, None, :] >= pad_len) & (kpos[None, None, :] <= slot + torch.arange(m)[None, :, None])))
+    ref = _attn_reference(q, kc, vc, valid, d.n_q, d.n_kv, m, d.attn_mult)
+    _close_bf16(st.attn.cpu(), ref)
+    assert int(st.ctrl[_lib.SB_CTRL_ERR]) == 0
