@@ -123,9 +123,12 @@ __host__ __device__ inline AttnLayout attn_layout(int R, int cap, int slots) {
   return L;
 }
 
+// NT = ceil(R / 8) q-row tiles of the score MMA (R = query rows per KV head).
+template <int NT>
 __global__ void __launch_bounds__(256, 2)
     k_attn(const __grid_constant__ AttnParams p, const __grid_constant__ CUtensorMap tmk,
            const __grid_constant__ CUtensorMap tmv) {
+  constexpr int MT = (NT + 1) / 2;  // q-row m-tiles of the P.V MMA
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (su32(smem_raw) & 1023)) & 1023);
   const int split = p.split;
@@ -215,15 +218,22 @@ __global__ void __launch_bounds__(256, 2)
   if (tid < 4) reinterpret_cast<uint32_t*>(zrow)[tid] = 0u;
   __syncthreads();
 
-  const int NT = (R + 7) / 8;    // q-row n-tiles of the score MMA
-  const int MT = (R + 15) / 16;  // q-row m-tiles of the P.V MMA
-  float acc[4][2][4];            // P.V accumulators [m-tile][n-tile][frag]
+  float acc[MT][2][4];  // P.V accumulators [m-tile][n-tile][frag]
 #pragma unroll
-  for (int a = 0; a < 4; ++a)
+  for (int a = 0; a < MT; ++a)
 #pragma unroll
     for (int n = 0; n < 2; ++n)
 #pragma unroll
       for (int e = 0; e < 4; ++e) acc[a][n][e] = 0.f;
+  // the q rows this lane's score fragments hold: row n*8 + 2c + h; causal limit slot + token
+  int lim[NT][2];
+#pragma unroll
+  for (int n = 0; n < NT; ++n)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int r = n * 8 + 2 * c + h;
+      lim[n][h] = r < R ? slot + r / G : -1;  // -1: padding row, never stored
+    }
 
   auto softmax = [&]() {
     const int nk = nT * kTK;
@@ -267,39 +277,35 @@ __global__ void __launch_bounds__(256, 2)
       // ---- scores^T[key][row] = K . Q^T: warp w < 4 takes keys 16w..16w+15 of the tile
       if (warp < 4) {
         const int u = it;
-        float d[8][4];
+        float d[NT][4];
 #pragma unroll
-        for (int n = 0; n < 8; ++n)
+        for (int n = 0; n < NT; ++n)
 #pragma unroll
           for (int e = 0; e < 4; ++e) d[n][e] = 0.f;
         const int arow = warp * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
+        const uint16_t* qrow = qb + g * 136 + 2 * c;
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {
           uint32_t a[4];
           ldsm_x4(tile + (ks >> 2) * (kTileBytes / 2) + swz(arow, (ks & 3) * 2 + (lane >> 4)), a);
 #pragma unroll
-          for (int n = 0; n < 8; ++n) {
-            if (n < NT) {
-              const uint16_t* qr = qb + (n * 8 + g) * 136 + ks * 16 + 2 * c;
-              mma_bf16(d[n], a, *reinterpret_cast<const uint32_t*>(qr), *reinterpret_cast<const uint32_t*>(qr + 8));
-            }
+          for (int n = 0; n < NT; ++n) {
+            const uint16_t* qr = qrow + n * 8 * 136 + ks * 16;
+            mma_bf16(d[n], a, *reinterpret_cast<const uint32_t*>(qr), *reinterpret_cast<const uint32_t*>(qr + 8));
           }
         }
         const int rows = trows(u), k0 = tstart(u);
 #pragma unroll
-        for (int n = 0; n < 8; ++n) {
-          if (n < NT) {
+        for (int h8 = 0; h8 < 2; ++h8) {
+          const int key = warp * 16 + g + h8 * 8;  // key within the tile
+          const int pk = key < rows ? k0 + key : 0x7fffffff;
+          float* srow = sc + u * kTK + key;
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int key = warp * 16 + g + (e >> 1) * 8;  // key within the tile
-              const int r = n * 8 + 2 * c + (e & 1);         // q row
-              if (r < R) {
-                const int mi = r / G;
-                const bool ok = key < rows && k0 + key <= slot + mi;
-                sc[r * cap + u * kTK + key] = ok ? bf(bf(d[n][e]) * p.attn_mult) : -INFINITY;
-              }
-            }
-          }
+          for (int n = 0; n < NT; ++n)
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+              if (lim[n][h] >= 0)
+                srow[(n * 8 + 2 * c + h) * cap] = pk <= lim[n][h] ? bf(bf(d[n][h8 * 2 + h]) * p.attn_mult) : -INFINITY;
         }
       }
     } else {
@@ -312,16 +318,14 @@ __global__ void __launch_bounds__(256, 2)
         uint32_t bv[4];
         ldsm_x4_t(tile + (dchunk >> 3) * (kTileBytes / 2) + swz(ks * 16 + vrow_l, dchunk & 7), bv);
 #pragma unroll
-        for (int mt = 0; mt < 4; ++mt) {
-          if (mt < MT) {
-            const int prow = mt * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
-            const int pkey = u * kTK + ks * 16 + 8 * (lane >> 4);
-            const uint16_t* pa = prow < R ? pb + prow * pst + pkey : zrow;
-            uint32_t a[4];
-            ldsm_x4(su32(pa), a);
-            mma_bf16(acc[mt][0], a, bv[0], bv[1]);
-            mma_bf16(acc[mt][1], a, bv[2], bv[3]);
-          }
+        for (int mt = 0; mt < MT; ++mt) {
+          const int prow = mt * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
+          const int pkey = u * kTK + ks * 16 + 8 * (lane >> 4);
+          const uint16_t* pa = prow < R ? pb + prow * pst + pkey : zrow;
+          uint32_t a[4];
+          ldsm_x4(su32(pa), a);
+          mma_bf16(acc[mt][0], a, bv[0], bv[1]);
+          mma_bf16(acc[mt][1], a, bv[2], bv[3]);
         }
       }
     }
@@ -346,18 +350,15 @@ __global__ void __launch_bounds__(256, 2)
 
   // ---- this CTA's P.V rows -> outp ---------------------------------------------------------
 #pragma unroll
-  for (int mt = 0; mt < 4; ++mt) {
-    if (mt < MT) {
+  for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-      for (int n = 0; n < 2; ++n)
+    for (int n = 0; n < 2; ++n)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int r = mt * 16 + g + (e >> 1) * 8;
-          const int dim = warp * 16 + n * 8 + 2 * c + (e & 1);
-          if (r < R) outp[r * 128 + dim] = acc[mt][n][e];
-        }
-    }
-  }
+      for (int e = 0; e < 4; ++e) {
+        const int r = mt * 16 + g + (e >> 1) * 8;
+        const int dim = warp * 16 + n * 8 + 2 * c + (e & 1);
+        if (r < R) outp[r * 128 + dim] = acc[mt][n][e];
+      }
 
   // ---- combine the cluster's partial outputs, round, store -----------------------------
   if (split > 1) cg::this_cluster().sync(); else __syncthreads();
@@ -415,13 +416,25 @@ int attn_launch(const AttnParams& p, int batch, bool pdl, cudaStream_t stream) {
   if (smem > 200 * 1024) return SB_ERR_CONFIG;
   CUtensorMap tmk, tmv;
   if (cache_map(&tmk, p.k_cache, p.cache_rows) || cache_map(&tmv, p.v_cache, p.cache_rows)) return SB_ERR_CONFIG;
+  const int NT = (R + 7) / 8;
+  void (*kern)(AttnParams, CUtensorMap, CUtensorMap) = nullptr;
+  switch (NT) {
+    case 1: kern = k_attn<1>; break;
+    case 2: kern = k_attn<2>; break;
+    case 3: kern = k_attn<3>; break;
+    case 4: kern = k_attn<4>; break;
+    case 5: kern = k_attn<5>; break;
+    case 6: kern = k_attn<6>; break;
+    case 7: kern = k_attn<7>; break;
+    default: kern = k_attn<8>; break;
+  }
   int dev = 0;
   cudaGetDevice(&dev);
-  static unsigned configured = 0;
-  if (!(configured & (1u << dev))) {
-    cudaError_t e = cudaFuncSetAttribute(k_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  static unsigned configured[8] = {};
+  if (!(configured[NT - 1] & (1u << dev))) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     if (e != cudaSuccess) return e;
-    configured |= 1u << dev;
+    configured[NT - 1] |= 1u << dev;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.split, p.n_kv, batch);
@@ -444,7 +457,7 @@ int attn_launch(const AttnParams& p, int batch, bool pdl, cudaStream_t stream) {
   }
   cfg.attrs = attrs;
   cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, k_attn, p, tmk, tmv);
+  return cudaLaunchKernelEx(&cfg, kern, p, tmk, tmv);
 }
 
 }  // namespace sb
