@@ -23,27 +23,31 @@
 //    of e4m3 values are exact, so the result differs from the dequantised
 //    fp32 reference only by fp32 accumulation order.
 //
-// Kernel (192 threads, one CTA per SM):
-//  * warp 4 (one thread) streams (A block, B block) pairs into a ring of
+// Kernel (320 threads, one CTA per SM):
+//  * warp 8 (one thread) streams (A block, B block) pairs into a ring of
 //    shared-memory stages with bulk copies completing on mbarriers; the weight
 //    blocks of the first ring are issued BEFORE griddepcontrol.wait, so they
-//    overlap the previous kernel;
-//  * warp 5 (one thread) issues four tcgen05.mma (K = 32 bytes each) per
-//    stage and frees the stage with tcgen05.commit;
-//  * warps 0-3 read the 128 x N fp32 accumulator (warp w owns TMEM lanes
-//    32w..32w+31 = tile rows), undo the activation scaling and run the fused
-//    epilogue.
+//    overlap the previous kernel.  CTAs start their K loop at different
+//    blocks so that they do not all read the same activation block from L2;
+//  * warp 9 (one thread) issues four tcgen05.mma (K = 32 bytes each) per
+//    stage into one of two TMEM accumulators and frees the stage with
+//    tcgen05.commit;
+//  * warps 0-7 read the 128 x N fp32 accumulator (warps w and w + 4 share
+//    TMEM lanes 32w..32w+31 = tile rows and split the tokens), undo the
+//    activation scaling and run the fused row-owned epilogue (tc_epi.cuh).
 // With many tiles (lm_head, gate/up) each CTA is persistent over tiles and the
-// epilogue of one tile overlaps the weight stream of the next.  With few tiles
-// a cluster of `split` CTAs shares a tile, each taking a contiguous K range;
-// the partial tiles are reduced over distributed shared memory in rank order
-// (deterministic), each CTA finishing 128/split rows.
+// epilogue of one tile overlaps the MMAs of the next (double-buffered
+// accumulator).  With few tiles a cluster of `split` (<= 4) CTAs shares a
+// tile, each taking a contiguous K range; every CTA pushes its partial rows
+// to the rank that finishes them (distributed shared memory), which sums them
+// in rank order (deterministic) and runs the epilogue on 128/split rows.
 // Every wait is bounded (2 s of %globaltimer); on expiry the kernel records
 // SB_CTRL_ERR = 2 and carries on with invalid results instead of hanging.
 #include <cooperative_groups.h>
 
 #include "gemm_tc.cuh"
 #include "gemv_epi.cuh"
+#include "tc_epi.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -145,7 +149,7 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t* r) {
                : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kTcEpiWarps * 32) : "memory"); }
 
 // fixed-order block reductions over 256 threads
 __device__ __forceinline__ float block_sum256(float v, float* s_red) {
@@ -185,22 +189,28 @@ struct TcArgs {
 };
 
 // ---- B operand: prologue + layout ------------------------------------------------
-// One CTA per (padded) token row.  Rows >= m are written as zeros.
+// One CTA per (padded) token row; the row is read once into registers (16
+// consecutive elements per thread and chunk), then RMSNorm statistics, the
+// power-of-two scale and the e4m3 split are all computed from registers.
+// Rows >= m are written as zeros.
+constexpr int kPrepThreads = 256;
+constexpr int kPrepChunks = 4;  // 16-element chunks per thread: K <= 16384
+
 template <int FMT>
-__global__ void __launch_bounds__(256) k_tc_prep(const __grid_constant__ GemvParams p, uint8_t* xq, int32_t* xshift,
-                                                  int mp, int np) {
-  constexpr int CE = FMT == SB_FMT_BF16 ? 8 : 16;  // elements per 16-byte chunk
-  __shared__ float s_red[8];
+__global__ void __launch_bounds__(kPrepThreads) k_tc_prep(const __grid_constant__ GemvParams p, uint8_t* xq,
+                                                           int32_t* xshift, int mp, int np) {
+  __shared__ float s_red[kPrepThreads / 32];
   const int m = blockIdx.x, tid = threadIdx.x, K = p.k;
-  const int nch = K / CE;
+  const int n16 = K / 16;
   const size_t kb_bytes = static_cast<size_t>(np) * 128;
-  auto off = [&](int n, int c) -> size_t {
+  auto off = [&](int n, int c) -> size_t {  // 16-byte chunk c (along K bytes) of B-operand row n
     return static_cast<size_t>(c >> 3) * kb_bytes + static_cast<size_t>(n >> 3) * 1024 + (c & 7) * 128 + (n & 7) * 16;
   };
+  constexpr int CPE = FMT == SB_FMT_BF16 ? 2 : 1;  // 16-byte output chunks per 16 elements and term
   pdl_wait();
   pdl_launch();
   if (m >= p.m) {
-    for (int c = tid; c < nch; c += blockDim.x) {
+    for (int c = tid; c < n16 * CPE; c += kPrepThreads) {
       *reinterpret_cast<uint4*>(xq + off(m, c)) = make_uint4(0, 0, 0, 0);
       if (FMT == SB_FMT_FP8) *reinterpret_cast<uint4*>(xq + off(mp + m, c)) = make_uint4(0, 0, 0, 0);
     }
@@ -216,100 +226,105 @@ __global__ void __launch_bounds__(256) k_tc_prep(const __grid_constant__ GemvPar
   } else {
     src = p.x + static_cast<size_t>(m) * K;
   }
-  auto load_h = [&](int k, float* h) {  // the residual-stream value (embedding x 12 for layer 0)
-    unpack8(*reinterpret_cast<const uint4*>(src + k), h);
-    if (embed) {
+  float f[kPrepChunks][16];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) h[e] = bf(h[e] * p.emb_mult);  // llm_mega.py:514
+  for (int j = 0; j < kPrepChunks; ++j) {
+    const int c16 = tid + j * kPrepThreads;
+    if (c16 < n16) {
+      unpack8(*reinterpret_cast<const uint4*>(src + c16 * 16), f[j]);
+      unpack8(*reinterpret_cast<const uint4*>(src + c16 * 16 + 8), f[j] + 8);
+      if (embed) {  // embed_tokens(ids) * 12 (llm_mega.py:514): the residual stream of layer 0
+#pragma unroll
+        for (int e = 0; e < 16; ++e) f[j][e] = bf(f[j][e] * p.emb_mult);
+        if (p.hidden_out) {
+          uint4* ho = reinterpret_cast<uint4*>(p.hidden_out + static_cast<size_t>(m) * K + c16 * 16);
+          ho[0] = pack8(f[j]);
+          ho[1] = pack8(f[j] + 8);
+        }
+      }
     }
-  };
-  float rstd = 1.f;
-  if (p.pro != PRO_NONE) {
+  }
+  if (p.pro != PRO_NONE) {  // weight * bf16(x * rstd)  (modeling_granite.py:192-197)
     float ss = 0.f;
-    for (int k = tid * 8; k < K; k += blockDim.x * 8) {
-      float h[8];
-      load_h(k, h);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) ss += h[e] * h[e];
-    }
+    for (int j = 0; j < kPrepChunks; ++j)
+      if (tid + j * kPrepThreads < n16)
+#pragma unroll
+        for (int e = 0; e < 16; ++e) ss += f[j][e] * f[j][e];
     ss = block_sum256(ss, s_red);
-    rstd = 1.f / sqrtf(ss / static_cast<float>(K) + p.eps);
-  }
-  auto norm8 = [&](int k, float* f) {  // weight * bf16(x * rstd)  (modeling_granite.py:192-197)
-    load_h(k, f);
-    if (p.pro != PRO_NONE) {
-      float wn[8];
-      unpack8(*reinterpret_cast<const uint4*>(p.norm_w + k), wn);
+    const float rstd = 1.f / sqrtf(ss / static_cast<float>(K) + p.eps);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) f[e] = bf(wn[e] * bf(f[e] * rstd));
-    }
-  };
-  if (embed && p.hidden_out) {
-    for (int k = tid * 8; k < K; k += blockDim.x * 8) {
-      float h[8];
-      load_h(k, h);
-      *reinterpret_cast<uint4*>(p.hidden_out + static_cast<size_t>(m) * K + k) = pack8(h);
+    for (int j = 0; j < kPrepChunks; ++j) {
+      const int c16 = tid + j * kPrepThreads;
+      if (c16 < n16) {
+        float wn[16];
+        unpack8(*reinterpret_cast<const uint4*>(p.norm_w + c16 * 16), wn);
+        unpack8(*reinterpret_cast<const uint4*>(p.norm_w + c16 * 16 + 8), wn + 8);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) f[j][e] = bf(wn[e] * bf(f[j][e] * rstd));
+      }
     }
   }
-  int shift = 0;
-  if (FMT == SB_FMT_FP8) {
+  if constexpr (FMT == SB_FMT_BF16) {
+#pragma unroll
+    for (int j = 0; j < kPrepChunks; ++j) {
+      const int c16 = tid + j * kPrepThreads;
+      if (c16 < n16) {
+        *reinterpret_cast<uint4*>(xq + off(m, 2 * c16)) = pack8(f[j]);
+        *reinterpret_cast<uint4*>(xq + off(m, 2 * c16 + 1)) = pack8(f[j] + 8);
+      }
+    }
+  } else {
     float am = 0.f;
-    for (int k = tid * 8; k < K; k += blockDim.x * 8) {
-      float f[8];
-      norm8(k, f);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) am = fmaxf(am, fabsf(f[e]));
-    }
+    for (int j = 0; j < kPrepChunks; ++j)
+      if (tid + j * kPrepThreads < n16)
+#pragma unroll
+        for (int e = 0; e < 16; ++e) am = fmaxf(am, fabsf(f[j][e]));
     am = block_max256(am, s_red);
     int e2 = 0;
     if (am > 0.f) frexpf(am, &e2);
-    shift = 8 - e2;  // max |x| 2^shift in [128, 256)
+    const int shift = 8 - e2;  // max |x| 2^shift in [128, 256)
     if (tid == 0) xshift[m] = shift;
-  }
-  for (int c = tid; c < nch; c += blockDim.x) {
-    const int k = c * CE;
-    if constexpr (FMT == SB_FMT_BF16) {
-      float f[8];
-      norm8(k, f);
-      *reinterpret_cast<uint4*>(xq + off(m, c)) = pack8(f);
-    } else {
-      uint8_t q0[16], q1[16];
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        float f[8];
-        norm8(k + 8 * h, f);
+    for (int j = 0; j < kPrepChunks; ++j) {
+      const int c16 = tid + j * kPrepThreads;
+      if (c16 < n16) {
+        uint8_t q0[16], q1[16];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float v = ldexpf(f[e], shift);  // exact
-          const float t0 = e4m3_round(v, q0[8 * h + e]);
-          e4m3_round((v - t0) * 16.f, q1[8 * h + e]);  // exact residual
+        for (int e = 0; e < 16; ++e) {
+          const float v = ldexpf(f[j][e], shift);  // exact
+          const float t0 = e4m3_round(v, q0[e]);
+          e4m3_round((v - t0) * 16.f, q1[e]);  // exact residual
         }
+        *reinterpret_cast<uint4*>(xq + off(m, c16)) = *reinterpret_cast<const uint4*>(q0);
+        *reinterpret_cast<uint4*>(xq + off(mp + m, c16)) = *reinterpret_cast<const uint4*>(q1);
       }
-      *reinterpret_cast<uint4*>(xq + off(m, c)) = *reinterpret_cast<const uint4*>(q0);
-      *reinterpret_cast<uint4*>(xq + off(mp + m, c)) = *reinterpret_cast<const uint4*>(q1);
     }
   }
 }
 
 // ---- the GEMM ----------------------------------------------------------------------
 template <int FMT>
-__global__ void __launch_bounds__(192, 1) k_tc_gemm(const __grid_constant__ GemvParams p, const __grid_constant__ TcArgs a) {
+__global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant__ GemvParams p, const __grid_constant__ TcArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int M = p.m;
   const TcLayout L = tc_layout(a.np, a.stages, M, a.split);
   uint8_t* ring = smem;
-  float* part = reinterpret_cast<float*>(smem + L.part);  // [128][M] this CTA's tile (partial if split)
-  float* outb = reinterpret_cast<float*>(smem + L.out);   // [128/split][M] reduced rows (split > 1)
+  float* part = reinterpret_cast<float*>(smem + L.part);  // split: inbox [src rank][row][ms]
+  const int ms = tc_inbox_stride(M);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
   uint64_t* empty = full + a.stages;
-  uint64_t* acc_full = empty + a.stages;
-  uint64_t* acc_empty = acc_full + 1;
+  uint64_t* acc_full = empty + a.stages;  // [2]: double-buffered accumulator
+  uint64_t* acc_empty = acc_full + 2;     // [2]
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + L.tmem);
   int* s_flag = reinterpret_cast<int*>(smem + L.flag);
   int* s_best = reinterpret_cast<int*>(smem + L.best);
   float* s_bval = reinterpret_cast<float*>(smem + L.bval);
   int* s_shift = reinterpret_cast<int*>(smem + L.shift);
+  float* wb_val = reinterpret_cast<float*>(smem + L.wbv);
+  int* wb_idx = reinterpret_cast<int*>(smem + L.wbi);
   int32_t* err = p.ctrl ? p.ctrl + SB_CTRL_ERR : nullptr;
 
   const int S = a.split;
@@ -318,31 +333,44 @@ __global__ void __launch_bounds__(192, 1) k_tc_gemm(const __grid_constant__ Gemv
   const int kb0 = q * a.kb / S, kb1 = (q + 1) * a.kb / S, nk = kb1 - kb0;
   const int my_tiles = cid < a.tiles ? (a.tiles - cid + ncl - 1) / ncl : 0;
   const uint32_t a_bytes = 16384u, b_bytes = static_cast<uint32_t>(a.np) * 128u;
+  // CTAs start their K blocks at different offsets so that they do not all read
+  // the same activation block from L2 at the same time
+  const int rot = cid % nk;
+  const uint32_t half_cols = static_cast<uint32_t>(a.ncols) / 2;  // accumulator buffer stride
 
-  if (warp == 4 && lane == 0) {
+  constexpr int kProd = kTcEpiWarps, kMma = kTcEpiWarps + 1;  // warp roles
+  if (warp == kProd && lane == 0) {
     for (int s = 0; s < a.stages; ++s) {
       mbar_init(full + s, 1);
       mbar_init(empty + s, 1);
     }
-    mbar_init(acc_full, 1);
-    mbar_init(acc_empty, 128);
+    for (int b2 = 0; b2 < 2; ++b2) {
+      mbar_init(acc_full + b2, 1);
+      mbar_init(acc_empty + b2, kTcEpiWarps * 32);
+    }
     mbar_fence_init();
   }
-  if (warp == 5) tmem_alloc(s_tmem, static_cast<uint32_t>(a.ncols));
+  if (warp == kMma) tmem_alloc(s_tmem, static_cast<uint32_t>(a.ncols));
+  if (p.epi == EPI_ARGMAX)
+    for (int i = tid; i < (kTcEpiWarps + 2) * 128; i += blockDim.x) {
+      wb_val[i] = -INFINITY;
+      wb_idx[i] = 0x7fffffff;
+    }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *s_tmem;
 
-  if (warp == 4) {
+  if (warp == kProd) {
     // ---- producer ----
     if (lane == 0) {
       const int total = my_tiles * nk;
+      auto kb_of = [&](int it) { return kb0 + (it % nk + rot) % nk; };
       auto a_src = [&](int it) {
-        const int t = cid + (it / nk) * ncl, kbi = kb0 + it % nk;
-        return a.wt + (static_cast<size_t>(t) * a.kb + kbi) * 16384;
+        const int t = cid + (it / nk) * ncl;
+        return a.wt + (static_cast<size_t>(t) * a.kb + kb_of(it)) * 16384;
       };
-      auto b_src = [&](int it) { return a.xq + static_cast<size_t>(kb0 + it % nk) * b_bytes; };
+      auto b_src = [&](int it) { return a.xq + static_cast<size_t>(kb_of(it)) * b_bytes; };
       const int pre = total < a.stages ? total : a.stages;
       for (int it = 0; it < pre; ++it) {  // weights do not depend on the previous kernel
         mbar_expect_tx(full + it, a_bytes + b_bytes);
@@ -361,15 +389,17 @@ __global__ void __launch_bounds__(192, 1) k_tc_gemm(const __grid_constant__ Gemv
     __syncwarp();
     pdl_wait();
     pdl_launch();
-  } else if (warp == 5) {
+  } else if (warp == kMma) {
     // ---- MMA issuer ----
     pdl_wait();
     pdl_launch();
     if (lane == 0) {
       int it = 0;
       for (int tc = 0; tc < my_tiles; ++tc) {
-        if (tc > 0) wait_bounded(acc_empty, static_cast<uint32_t>((tc - 1) & 1), err);
+        const int buf = tc & 1;
+        if (tc >= 2) wait_bounded(acc_empty + buf, static_cast<uint32_t>((tc / 2 - 1) & 1), err);
         tc_fence_after();
+        const uint32_t dacc = tmem + buf * half_cols;
         for (int j = 0; j < nk; ++j, ++it) {
           const int s = it % a.stages;
           wait_bounded(full + s, static_cast<uint32_t>((it / a.stages) & 1), err);
@@ -377,73 +407,101 @@ __global__ void __launch_bounds__(192, 1) k_tc_gemm(const __grid_constant__ Gemv
           const uint32_t sa = su32(ring + s * L.stage_bytes), sbb = sa + 16384u;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            tc_mma<FMT>(tmem, sdesc(sa + kk * 256u, 128u, 1024u), sdesc(sbb + kk * 256u, 128u, 1024u), a.idesc,
+            tc_mma<FMT>(dacc, sdesc(sa + kk * 256u, 128u, 1024u), sdesc(sbb + kk * 256u, 128u, 1024u), a.idesc,
                         (j > 0 || kk > 0) ? 1u : 0u);
           tc_commit(empty + s);  // the stage is free once these MMAs have read it
         }
-        tc_commit(acc_full);
+        tc_commit(acc_full + buf);
       }
     }
     __syncwarp();
   } else {
-    // ---- epilogue warps 0-3: TMEM lanes 32w.. = tile rows ----
+    // ---- epilogue warps 0-7: warp w reads TMEM lanes 32 (w % 4).. (tile rows) and
+    // the 8-token chunks h, h + 2, ... with h = w / 4 ----
     pdl_wait();
     pdl_launch();
-    if (FMT == SB_FMT_FP8)
-      for (int i = tid; i < M; i += 128) s_shift[i] = a.xshift[i];
+    if (FMT == SB_FMT_FP8)  // 2^-shift per token: exact power of two
+      for (int i = tid; i < M; i += kTcEpiWarps * 32) reinterpret_cast<float*>(s_shift)[i] = ldexpf(1.f, -a.xshift[i]);
     epi_sync();
-    const int row = warp * 32 + lane;
-    const uint32_t taddr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    const float* s_unscale = reinterpret_cast<const float*>(s_shift);
+    const int lq = warp & 3, h = warp >> 2;
+    const int lrow = lq * 32 + lane;
+    const int rp = tc_rows_per_rank(S);
     for (int tc = 0; tc < my_tiles; ++tc) {
-      const int t = cid + tc * ncl;
-      wait_bounded(acc_full, static_cast<uint32_t>(tc & 1), err);
+      const int t = cid + tc * ncl, buf = tc & 1;
+      const uint32_t taddr = tmem + buf * half_cols + (static_cast<uint32_t>(lq * 32) << 16);
+      wait_bounded(acc_full + buf, static_cast<uint32_t>((tc / 2) & 1), err);
       tc_fence_after();
-      for (int m0 = 0; m0 < a.mp; m0 += 8) {
+      for (int m0 = h * 8; m0 < M; m0 += 16) {
+        // 8 tokens of this lane's row: D0 (and D1 for the fp8 split) columns
         uint32_t d0[8], d1[8];
         tmem_ld8(taddr + m0, d0);
         if (FMT == SB_FMT_FP8) tmem_ld8(taddr + a.mp + m0, d1);
         tmem_wait_ld();
+        float v[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          const int m = m0 + i;
-          if (m < M) {
-            float v = __uint_as_float(d0[i]);
-            if (FMT == SB_FMT_FP8) v = ldexpf(v + __uint_as_float(d1[i]) * 0.0625f, -s_shift[m]);
-            part[row * M + m] = v;
+          v[i] = __uint_as_float(d0[i]);
+          if (FMT == SB_FMT_FP8) {
+            const int m = m0 + i < M ? m0 + i : M - 1;
+            v[i] = fmaf(__uint_as_float(d1[i]), 0.0625f, v[i]) * s_unscale[m];  // (D0 + D1/16) 2^-s
           }
+        }
+        if (S == 1) {
+          const int row = t * 128 + lrow;
+          tc_epi<FMT, 8>(p, row, row < p.n, v, m0, M, wb_val, wb_idx, warp);
+        } else {
+          // push this K partial to the rank that finishes the row (16-byte DSMEM stores)
+          float* dst = cg::this_cluster().map_shared_rank(part, lrow / rp) + (q * rp + lrow % rp) * ms + m0;
+          reinterpret_cast<float4*>(dst)[0] = make_float4(v[0], v[1], v[2], v[3]);
+          reinterpret_cast<float4*>(dst)[1] = make_float4(v[4], v[5], v[6], v[7]);
         }
       }
       tc_fence_before();
-      mbar_arrive(acc_empty);  // the MMA warp may overwrite the accumulator
-      if (S == 1) {
-        epi_sync();
-        gemv_epilogue<FMT>(p, part, t * 128, 128, M, s_best, s_bval, tc == 0, tc == my_tiles - 1, tid, 128);
-        epi_sync();
-      }
+      mbar_arrive(acc_empty + buf);  // the MMA warp may overwrite this accumulator
     }
   }
 
-  if (S > 1) {  // one tile per cluster: reduce the K partials in rank order
-    cg::cluster_group cl = cg::this_cluster();
-    cl.sync();
-    const int rp = (128 + S - 1) / S, r0 = q * rp;
+  if (S > 1) {  // one tile per cluster: sum the pushed K partials in rank order, then the epilogue
+    cg::this_cluster().sync();  // every partial has landed in its owner's inbox
+    const int rp = tc_rows_per_rank(S), r0 = q * rp;
     const int nr = r0 >= 128 ? 0 : (r0 + rp > 128 ? 128 - r0 : rp);
-    for (int i = tid; i < nr * M; i += blockDim.x) {
-      const int r = r0 + i / M, m = i % M;
-      float s = 0.f;
-      for (int c = 0; c < S; ++c) s += cl.map_shared_rank(part, c)[r * M + m];
-      outb[i] = s;
+    const int nw = blockDim.x >> 5, ngrp = (nr + 31) / 32, nch = (M + 15) / 16;
+    for (int item = warp; item < ngrp * nch; item += nw) {
+      const int rg = item / nch, m0 = (item % nch) * 16;
+      const int lr = rg * 32 + lane;
+      const bool ok = lr < nr;
+      float v[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        float s = 0.f;
+        if (ok && m0 + i < M)
+          for (int c = 0; c < S; ++c) s += part[(c * rp + lr) * ms + m0 + i];
+        v[i] = s;
+      }
+      const int row = cid * 128 + r0 + lr;
+      tc_epi<FMT, 16>(p, row, ok && row < p.n, v, m0, M, wb_val, wb_idx, warp);
     }
+  }
+  if (p.epi == EPI_ARGMAX) {  // combine the warps' running bests (order-independent total order)
     __syncthreads();
-    if (my_tiles > 0 && nr > 0)
-      gemv_epilogue<FMT>(p, outb, cid * 128 + r0, nr, M, s_best, s_bval, true, true, tid, blockDim.x);
-    cl.sync();  // the peers have finished reading this CTA's partials
+    for (int m = tid; m < M; m += blockDim.x) {
+      float bv = -INFINITY;
+      int bi = 0x7fffffff;
+      for (int w = 0; w < kTcEpiWarps + 2; ++w)
+        if (am_better(wb_val[w * 128 + m], wb_idx[w * 128 + m], bv, bi)) {
+          bv = wb_val[w * 128 + m];
+          bi = wb_idx[w * 128 + m];
+        }
+      s_bval[m] = bv;
+      s_best[m] = bi;
+    }
   }
   __syncthreads();
   gemv_argmax_finish(p, s_best, s_bval, M, my_tiles > 0, s_flag);
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kMma) {
     tc_fence_after();
     tmem_dealloc(tmem, static_cast<uint32_t>(a.ncols));
   }
@@ -466,7 +524,7 @@ size_t tc_operand_bytes(int fmt, int k, int m) {
 bool tc_plan(int fmt, int n, int k, int m, TcPlan& pl) {
   if (!tc_format(fmt) || m < 1 || m > 128 || n < 1) return false;
   const int eb = elem_bytes(fmt);
-  if ((k * eb) % 128 != 0) return false;
+  if ((k * eb) % 128 != 0 || k > 16 * kPrepThreads * kPrepChunks) return false;
   pl.mp = pad_rows(fmt, m);
   pl.np = fmt == SB_FMT_FP8 ? 2 * pl.mp : pl.mp;
   if (pl.np < 16 || pl.np > 256) return false;
@@ -476,15 +534,16 @@ bool tc_plan(int fmt, int n, int k, int m, TcPlan& pl) {
     pl.split = 1;
     pl.n_ctas = pl.tiles < kSMs ? pl.tiles : kSMs;
   } else {
+    // clusters of more than 4 CTAs of ~200 KiB do not all fit at once
     int s = kSMs / pl.tiles;
-    if (s > 8) s = 8;
+    if (s > 4) s = 4;
     if (s > pl.kb) s = pl.kb;
     if (s < 1) s = 1;
     pl.split = s;
     pl.n_ctas = pl.tiles * s;
   }
   pl.ncols = 32;
-  while (pl.ncols < pl.np) pl.ncols *= 2;
+  while (pl.ncols < 2 * pl.np) pl.ncols *= 2;  // two accumulator buffers
   pl.stages = 0;
   for (int st = 8; st >= 2; --st)
     if (tc_layout(pl.np, st, m, pl.split).total <= kTcSmem) {
@@ -518,7 +577,7 @@ static int tc_launch_t(const GemvParams& p0, const void* w_tc, void* operand, co
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(pl.mp);
-  cfg.blockDim = dim3(256);
+  cfg.blockDim = dim3(kPrepThreads);
   cfg.stream = stream;
   cfg.attrs = at;
   cfg.numAttrs = pdl ? 1 : 0;
@@ -540,7 +599,7 @@ static int tc_launch_t(const GemvParams& p0, const void* w_tc, void* operand, co
   a.stages = pl.stages;
   a.ncols = pl.ncols;
   cfg.gridDim = dim3(pl.n_ctas);
-  cfg.blockDim = dim3(192);
+  cfg.blockDim = dim3(kTcThreads);
   cfg.dynamicSmemBytes = pl.smem;
   int na = 0;
   if (pdl) at[na++] = at[0];

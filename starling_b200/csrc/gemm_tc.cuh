@@ -23,23 +23,35 @@ struct TcPlan {
 
 // Shared-memory layout, computed identically on the host and in the kernel.
 struct TcLayout {
-  size_t stage_bytes, part, out, bars, tmem, flag, best, bval, shift, total;
+  size_t stage_bytes, part, out, bars, tmem, flag, best, bval, shift, wbv, wbi, total;
 };
+__host__ __device__ inline int tc_rows_per_rank(int split) {
+  const int rp = (128 + split - 1) / split;
+  return (rp + 1) & ~1;  // even: RoPE / gate-up row pairs stay in one CTA
+}
+// floats per inbox row: whole 8-token chunks (16-byte aligned stores) + 4 (bank spread)
+__host__ __device__ inline int tc_inbox_stride(int m) { return (m + 7) / 8 * 8 + 4; }
+// warps of the GEMM block: 8 epilogue warps (two per TMEM lane quarter), producer, MMA
+constexpr int kTcEpiWarps = 8;
+constexpr int kTcThreads = (kTcEpiWarps + 2) * 32;
 __host__ __device__ inline TcLayout tc_layout(int np, int stages, int m, int split) {
   auto up = [](size_t x, size_t a) { return (x + a - 1) & ~(a - 1); };
   TcLayout L;
   L.stage_bytes = 16384 + static_cast<size_t>(np) * 128;
   L.part = L.stage_bytes * stages;
-  const size_t part_bytes = static_cast<size_t>(128) * m * 4;
+  // split > 1: inbox [split source ranks][rows per rank][tc_inbox_stride(m)] of K partials
+  const size_t part_bytes =
+      split > 1 ? static_cast<size_t>(split) * tc_rows_per_rank(split) * tc_inbox_stride(m) * 4 : 0;
   L.out = up(L.part + part_bytes, 16);
-  const int rows_out = split > 1 ? (128 + split - 1) / split : 0;
-  L.bars = up(L.out + static_cast<size_t>(rows_out) * m * 4, 16);
-  L.tmem = up(L.bars + 8 * static_cast<size_t>(2 * stages + 2), 16);
+  L.bars = L.out;
+  L.tmem = up(L.bars + 8 * static_cast<size_t>(2 * stages + 4), 16);
   L.flag = L.tmem + 16;
   L.best = L.flag + 16;
   L.bval = L.best + 128 * 4;
   L.shift = L.bval + 128 * 4;
-  L.total = L.shift + 128 * 4;
+  L.wbv = L.shift + 128 * 4;                    // [warps][128] running argmax value
+  L.wbi = L.wbv + (kTcEpiWarps + 2) * 128 * 4;  // [warps][128] running argmax index
+  L.total = L.wbi + (kTcEpiWarps + 2) * 128 * 4;
   return L;
 }
 
