@@ -466,21 +466,24 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
     cg::this_cluster().sync();  // every partial has landed in its owner's inbox
     const int rp = tc_rows_per_rank(S), r0 = q * rp;
     const int nr = r0 >= 128 ? 0 : (r0 + rp > 128 ? 128 - r0 : rp);
-    const int nw = blockDim.x >> 5, ngrp = (nr + 31) / 32, nch = (M + 15) / 16;
+    // items of (32-row group, 4 tokens) over all warps; one float4 (16-byte,
+    // conflict-free) inbox read per source rank
+    const int nw = blockDim.x >> 5, ngrp = (nr + 31) / 32, nch = (M + 3) / 4;
     for (int item = warp; item < ngrp * nch; item += nw) {
-      const int rg = item / nch, m0 = (item % nch) * 16;
+      const int rg = item / nch, m0 = (item % nch) * 4;
       const int lr = rg * 32 + lane;
       const bool ok = lr < nr;
-      float v[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        float s = 0.f;
-        if (ok && m0 + i < M)
-          for (int c = 0; c < S; ++c) s += part[(c * rp + lr) * ms + m0 + i];
-        v[i] = s;
-      }
+      float v[4] = {0.f, 0.f, 0.f, 0.f};
+      if (ok)
+        for (int c = 0; c < S; ++c) {
+          const float4 x4 = *reinterpret_cast<const float4*>(part + (c * rp + lr) * ms + m0);
+          v[0] += x4.x;
+          v[1] += x4.y;
+          v[2] += x4.z;
+          v[3] += x4.w;
+        }
       const int row = cid * 128 + r0 + lr;
-      tc_epi<FMT, 16>(p, row, ok && row < p.n, v, m0, M, wb_val, wb_idx, warp);
+      tc_epi<FMT, 4>(p, row, ok && row < p.n, v, m0, M, wb_val, wb_idx, warp);
     }
   }
   if (p.epi == EPI_ARGMAX) {  // combine the warps' running bests (order-independent total order)
