@@ -287,8 +287,8 @@ static int launch_attention(const SbModel* md, const SbState* st, int l, cudaStr
   a.prompt_len = st->prompt_len;
   a.split = attn_split(st->batch * md->n_kv, md->max_len);
   a.chunk_cap = attn_key_capacity(md->max_len, a.split);
-  const int tiles = a.chunk_cap / 64;  // K tiles per CTA at most (as many V tiles)
-  a.slots = 2 * tiles < 4 ? 2 * tiles : 4;
+  const int tiles = a.chunk_cap / attn_tile_keys(a.split);  // K tiles per CTA at most (as many V tiles)
+  a.slots = 2 * tiles < 3 ? 2 * tiles : 3;
   if (a.slots < 2) a.slots = 2;
   a.cache_rows = static_cast<long long>(md->max_batch) * md->n_kv * md->max_len;
   const int rc = attn_launch(a, st->batch, st->use_pdl != 0, s);

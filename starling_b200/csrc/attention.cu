@@ -97,38 +97,40 @@ __device__ __forceinline__ uint32_t swz(int row, int chunk) {
   return static_cast<uint32_t>(row * 128 + ((chunk ^ (row & 7)) << 4));
 }
 
-constexpr int kTK = 64;                // keys per tile
-constexpr int kTileBytes = kTK * 256;  // two swizzled 64-dim boxes of 8 KiB
+
 
 }  // namespace
 
 // Shared-memory layout (offsets from a 1024-byte-aligned base), identical on
-// host and device.  cap = keys per CTA at most (a multiple of 64).
+// host and device.  cap = keys per CTA at most (a multiple of the tile size tk).
 struct AttnLayout {
-  size_t ring, bars, qb, sc, pb, outp, stat, zero, total;
+  size_t ring, bars, qb, sc, outp, wmax, psum, stat, zero, total;
 };
-__host__ __device__ inline AttnLayout attn_layout(int R, int cap, int slots) {
+__host__ __device__ inline AttnLayout attn_layout(int R, int cap, int slots, int tk) {
   auto up = [](size_t x) { return (x + 15) & ~size_t(15); };
-  const int R16 = (R + 15) / 16 * 16;
   AttnLayout L;
   L.ring = 0;
-  L.bars = static_cast<size_t>(slots) * kTileBytes;
+  L.bars = static_cast<size_t>(slots) * tk * 256;
   L.qb = up(L.bars + 8 * static_cast<size_t>(slots));
-  L.sc = up(L.qb + static_cast<size_t>(R16) * 136 * 2);            // q bf16 [R16][136]
-  L.pb = up(L.sc + static_cast<size_t>(R) * cap * 4);              // scores f32 [R][cap]
-  L.outp = up(L.pb + static_cast<size_t>(R) * (cap + 8) * 2);      // p bf16 [R][cap + 8]
-  L.stat = up(L.outp + static_cast<size_t>(R) * 128 * 4);          // P.V f32 [R][128]
-  L.zero = up(L.stat + 2 * static_cast<size_t>(R) * 4);            // max, sum [R]
-  L.total = up(L.zero + 16) + 1024;                                // + alignment slack
+  L.sc = up(L.qb + static_cast<size_t>(R) * 136 * 2);           // q bf16 [R][136]
+  L.outp = up(L.sc + static_cast<size_t>(R) * (cap + 8) * 2);   // scores, then p, bf16 [R][cap + 8]
+  L.wmax = up(L.outp + static_cast<size_t>(R) * 128 * 4);       // P.V f32 [R][128]
+  L.psum = up(L.wmax + 8 * static_cast<size_t>(R) * 4);         // per-warp row max [8][R]
+  L.stat = up(L.psum + 8 * static_cast<size_t>(R) * 4);         // per-warp row sum [R][8]
+  L.zero = up(L.stat + 2 * static_cast<size_t>(R) * 4);         // max, sum [R]
+  L.total = up(L.zero + 16) + 1024;                             // + alignment slack
   return L;
 }
 
-// NT = ceil(R / 8) q-row tiles of the score MMA (R = query rows per KV head).
-template <int NT>
+// NT = ceil(R / 8) q-row tiles of the score MMA (R = query rows per KV head);
+// TK keys per tile (a tile is two swizzled 64-dim boxes of TK * 128 bytes).
+template <int NT, int TK>
 __global__ void __launch_bounds__(256, 2)
     k_attn(const __grid_constant__ AttnParams p, const __grid_constant__ CUtensorMap tmk,
            const __grid_constant__ CUtensorMap tmv) {
   constexpr int MT = (NT + 1) / 2;  // q-row m-tiles of the P.V MMA
+  constexpr int kTK = TK;
+  constexpr int kTileBytes = TK * 256;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (su32(smem_raw) & 1023)) & 1023);
   const int split = p.split;
@@ -139,14 +141,15 @@ __global__ void __launch_bounds__(256, 2)
   const int G = p.n_q / p.n_kv;
   const int R = G * p.m_per;
   const int cap = p.chunk_cap;
-  const int pst = cap + 8;  // p row stride (elements): 16 mod 128 bytes -> conflict-free ldmatrix
-  const AttnLayout L = attn_layout(R, cap, p.slots);
+  const int cst = cap + 8;  // score/p row stride (elements): 16 mod 128 bytes -> conflict-free ldmatrix
+  const AttnLayout L = attn_layout(R, cap, p.slots, TK);
   uint8_t* ring = smem + L.ring;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
   uint16_t* qb = reinterpret_cast<uint16_t*>(smem + L.qb);
-  float* sc = reinterpret_cast<float*>(smem + L.sc);
-  uint16_t* pb = reinterpret_cast<uint16_t*>(smem + L.pb);
+  uint16_t* sc = reinterpret_cast<uint16_t*>(smem + L.sc);
   float* outp = reinterpret_cast<float*>(smem + L.outp);
+  float* wmax = reinterpret_cast<float*>(smem + L.wmax);
+  float* psum = reinterpret_cast<float*>(smem + L.psum);
   float* smax = reinterpret_cast<float*>(smem + L.stat);
   float* ssum = smax + R;
   uint16_t* zrow = reinterpret_cast<uint16_t*>(smem + L.zero);  // 16 zero bytes
@@ -166,6 +169,7 @@ __global__ void __launch_bounds__(256, 2)
   const int per = (t1 + t2 + split - 1) / split;
   const int i0 = rank * per < t1 + t2 ? rank * per : t1 + t2;
   const int nT = (i0 + per < t1 + t2 ? i0 + per : t1 + t2) - i0;  // this CTA's tiles
+  const int nk = nT * kTK;                                          // CTA-local key slots
   auto tstart = [&](int u) { const int i = i0 + u; return i < t1 ? kTK * i : g0 + kTK * (i - t1); };
   auto trows = [&](int u) {
     const int i = i0 + u;
@@ -203,17 +207,13 @@ __global__ void __launch_bounds__(256, 2)
     for (int it = 0; it < first; ++it)
       if (fresh(it)) issue(it);
 
-  // q rows of this KV group (row r = (token mi, head gi)) as bf16; rows >= R zero
-  const int R16 = (R + 15) / 16 * 16;
-  for (int i = tid; i < R16 * 64; i += blockDim.x) {
+  // q rows of this KV group (row r = (token mi, head gi)) as bf16
+  for (int i = tid; i < R * 64; i += blockDim.x) {
     const int r = i >> 6, d2 = (i & 63) * 2;
-    uint32_t v = 0;
-    if (r < R) {
-      const int mi = r / G, gi = r % G;
-      const size_t t = static_cast<size_t>(b) * p.m_per + mi;
-      v = *reinterpret_cast<const uint32_t*>(p.q + t * p.n_q * 128 + (kvh * G + gi) * 128 + d2);
-    }
-    *reinterpret_cast<uint32_t*>(qb + r * 136 + d2) = v;
+    const int mi = r / G, gi = r % G;
+    const size_t t = static_cast<size_t>(b) * p.m_per + mi;
+    *reinterpret_cast<uint32_t*>(qb + r * 136 + d2) =
+        *reinterpret_cast<const uint32_t*>(p.q + t * p.n_q * 128 + (kvh * G + gi) * 128 + d2);
   }
   if (tid < 4) reinterpret_cast<uint32_t*>(zrow)[tid] = 0u;
   __syncthreads();
@@ -227,44 +227,76 @@ __global__ void __launch_bounds__(256, 2)
       for (int e = 0; e < 4; ++e) acc[a][n][e] = 0.f;
   // the q rows this lane's score fragments hold: row n*8 + 2c + h; causal limit slot + token
   int lim[NT][2];
+  float lmax[NT][2];  // running max of this lane's scores per row
 #pragma unroll
   for (int n = 0; n < NT; ++n)
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int r = n * 8 + 2 * c + h;
       lim[n][h] = r < R ? slot + r / G : -1;  // -1: padding row, never stored
+      lmax[n][h] = -INFINITY;
     }
 
+  // softmax work split: wpr warps per row (R < 8), else one warp per row
+  const int wpr = R < 8 ? 8 / R : 1;
   auto softmax = [&]() {
-    const int nk = nT * kTK;
-    for (int r = warp; r < R; r += 8) {
+    // row max: lanes sharing c hold the same rows -> reduce over g, then over warps
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float m = lmax[n][h];
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 8));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 16));
+        const int r = n * 8 + 2 * c + h;
+        if (g == 0 && r < R) wmax[warp * R + r] = m;
+      }
+    __syncthreads();
+    for (int r = tid; r < R; r += blockDim.x) {
       float m = -INFINITY;
-      for (int jj = lane; jj < nk; jj += 32) m = fmaxf(m, sc[r * cap + jj]);
-      m = warp_max(m);
-      if (lane == 0) smax[r] = m;
+      for (int w = 0; w < 8; ++w) m = fmaxf(m, wmax[w * R + r]);
+      smax[r] = m;
     }
     if (split > 1) cg::this_cluster().sync(); else __syncthreads();
-    for (int r = warp; r < R; r += 8) {
+    // sum of exp(s - max): (row, part) per warp, 8 keys per lane-step
+    for (int r = warp / wpr; r < R && warp < R * wpr; r += (R < 8 ? R : 8)) {
       float gm = -INFINITY;
       for (int q = 0; q < split; ++q)
         gm = fmaxf(gm, split > 1 ? cg::this_cluster().map_shared_rank(smax, q)[r] : smax[r]);
+      const int sub = warp % wpr;
       float s = 0.f;
-      for (int jj = lane; jj < nk; jj += 32) {
-        float* e = sc + r * cap + jj;
-        const float ev = gm == -INFINITY ? 0.f : expf(*e - gm);
-        *e = ev;
-        s += ev;
+      for (int ch = sub * 32 + lane; ch * 8 < nk; ch += wpr * 32) {
+        float f[8];
+        unpack8(*reinterpret_cast<const uint4*>(sc + r * cst + ch * 8), f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) s += gm == -INFINITY ? 0.f : expf(f[e] - gm);
       }
       s = warp_sum(s);
-      if (lane == 0) ssum[r] = s;
+      if (lane == 0) psum[r * 8 + sub] = s;
+      if (lane == 0 && sub == 0) smax[r] = gm;  // the global max, for the normalisation below
+    }
+    __syncthreads();
+    for (int r = tid; r < R; r += blockDim.x) {
+      float s = 0.f;
+      for (int q = 0; q < wpr; ++q) s += psum[r * 8 + q];
+      ssum[r] = s;
     }
     if (split > 1) cg::this_cluster().sync(); else __syncthreads();
-    for (int r = warp; r < R; r += 8) {
+    // p = bf16(exp(s - max) * (1/sum)), in place of the scores
+    for (int r = warp / wpr; r < R && warp < R * wpr; r += (R < 8 ? R : 8)) {
       float gs = 0.f;
       for (int q = 0; q < split; ++q) gs += split > 1 ? cg::this_cluster().map_shared_rank(ssum, q)[r] : ssum[r];
-      const float inv = 1.f / gs;
-      for (int jj = lane; jj < nk; jj += 32)
-        pb[r * pst + jj] = f_to_bf16_bits(sc[r * cap + jj] * inv);  // softmax(..., float32).to(bf16)
+      const float gm = smax[r], inv = 1.f / gs;
+      const int sub = warp % wpr;
+      for (int ch = sub * 32 + lane; ch * 8 < nk; ch += wpr * 32) {
+        uint4* ptr8 = reinterpret_cast<uint4*>(sc + r * cst + ch * 8);
+        float f[8];
+        unpack8(*ptr8, f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) f[e] = gm == -INFINITY ? 0.f : expf(f[e] - gm) * inv;  // softmax(..., float32)
+        *ptr8 = pack8(f);                                                                  // .to(bf16)
+      }
     }
     __syncthreads();
   };
@@ -274,39 +306,48 @@ __global__ void __launch_bounds__(256, 2)
     ring_wait(bars + (it % p.slots), static_cast<uint32_t>((it / p.slots) & 1), err);
     const uint32_t tile = su32(ring + static_cast<size_t>(it % p.slots) * kTileBytes);
     if (it < nT) {
-      // ---- scores^T[key][row] = K . Q^T: warp w < 4 takes keys 16w..16w+15 of the tile
-      if (warp < 4) {
-        const int u = it;
-        float d[NT][4];
+      // ---- scores^T[key][row] = K . Q^T: warp w takes keys 16w..16w+15 of the tile
+      const int u = it;
+      if (warp * 16 < kTK) {
+      float d[NT][4];
+#pragma unroll
+      for (int n = 0; n < NT; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) d[n][e] = 0.f;
+      const int arow = warp * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        uint32_t a[4];
+        ldsm_x4(tile + (ks >> 2) * (kTileBytes / 2) + swz(arow, (ks & 3) * 2 + (lane >> 4)), a);
+#pragma unroll
+        for (int n = 0; n < NT; ++n) {
+          const int qr = n * 8 + g;
+          uint32_t b0 = 0, b1 = 0;
+          if (qr < R) {
+            const uint16_t* qp = qb + qr * 136 + ks * 16 + 2 * c;
+            b0 = *reinterpret_cast<const uint32_t*>(qp);
+            b1 = *reinterpret_cast<const uint32_t*>(qp + 8);
+          }
+          mma_bf16(d[n], a, b0, b1);
+        }
+      }
+      const int rows = trows(u), k0 = tstart(u);
+#pragma unroll
+      for (int h8 = 0; h8 < 2; ++h8) {
+        const int key = warp * 16 + g + h8 * 8;  // key within the tile
+        const int pk = key < rows ? k0 + key : 0x7fffffff;
+        uint16_t* srow = sc + u * kTK + key;
 #pragma unroll
         for (int n = 0; n < NT; ++n)
 #pragma unroll
-          for (int e = 0; e < 4; ++e) d[n][e] = 0.f;
-        const int arow = warp * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
-        const uint16_t* qrow = qb + g * 136 + 2 * c;
-#pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
-          uint32_t a[4];
-          ldsm_x4(tile + (ks >> 2) * (kTileBytes / 2) + swz(arow, (ks & 3) * 2 + (lane >> 4)), a);
-#pragma unroll
-          for (int n = 0; n < NT; ++n) {
-            const uint16_t* qr = qrow + n * 8 * 136 + ks * 16;
-            mma_bf16(d[n], a, *reinterpret_cast<const uint32_t*>(qr), *reinterpret_cast<const uint32_t*>(qr + 8));
-          }
-        }
-        const int rows = trows(u), k0 = tstart(u);
-#pragma unroll
-        for (int h8 = 0; h8 < 2; ++h8) {
-          const int key = warp * 16 + g + h8 * 8;  // key within the tile
-          const int pk = key < rows ? k0 + key : 0x7fffffff;
-          float* srow = sc + u * kTK + key;
-#pragma unroll
-          for (int n = 0; n < NT; ++n)
-#pragma unroll
-            for (int h = 0; h < 2; ++h)
-              if (lim[n][h] >= 0)
-                srow[(n * 8 + 2 * c + h) * cap] = pk <= lim[n][h] ? bf(bf(d[n][h8 * 2 + h]) * p.attn_mult) : -INFINITY;
-        }
+          for (int h = 0; h < 2; ++h)
+            if (lim[n][h] >= 0) {
+              const bool ok = pk <= lim[n][h];
+              const float sv = ok ? bf(bf(d[n][h8 * 2 + h]) * p.attn_mult) : -INFINITY;
+              if (ok) lmax[n][h] = fmaxf(lmax[n][h], sv);
+              srow[(n * 8 + 2 * c + h) * cst] = ok ? f_to_bf16_bits(sv) : static_cast<uint16_t>(0xFF80u);
+            }
+      }
       }
     } else {
       // ---- out[row][dim] += P . V: warp w takes dims 16w..16w+15 (two n-tiles)
@@ -314,14 +355,14 @@ __global__ void __launch_bounds__(256, 2)
       const int vrow_l = (lane & 7) + 8 * ((lane >> 3) & 1);
       const int dchunk = warp * 2 + (lane >> 4);  // 8-dim chunk 0..15
 #pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
+      for (int ks = 0; ks < kTK / 16; ++ks) {
         uint32_t bv[4];
         ldsm_x4_t(tile + (dchunk >> 3) * (kTileBytes / 2) + swz(ks * 16 + vrow_l, dchunk & 7), bv);
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt) {
           const int prow = mt * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
           const int pkey = u * kTK + ks * 16 + 8 * (lane >> 4);
-          const uint16_t* pa = prow < R ? pb + prow * pst + pkey : zrow;
+          const uint16_t* pa = prow < R ? sc + prow * cst + pkey : zrow;
           uint32_t a[4];
           ldsm_x4(su32(pa), a);
           mma_bf16(acc[mt][0], a, bv[0], bv[1]);
@@ -376,11 +417,14 @@ __global__ void __launch_bounds__(256, 2)
 }
 
 // ---- host side ------------------------------------------------------------------
-size_t attn_smem_bytes(int R, int chunk_cap, int slots) { return attn_layout(R, chunk_cap, slots).total; }
+int attn_tile_keys(int split) { return split > 1 ? 64 : 128; }
+
+size_t attn_smem_bytes(int R, int chunk_cap, int slots, int tk) { return attn_layout(R, chunk_cap, slots, tk).total; }
 
 int attn_key_capacity(int max_len, int split) {
-  const int tiles = (max_len + kTK - 1) / kTK + 1;  // the padding hole can cut one tile in two
-  return (tiles + split - 1) / split * kTK;
+  const int tk = attn_tile_keys(split);
+  const int tiles = (max_len + tk - 1) / tk + 1;  // the padding hole can cut one tile in two
+  return (tiles + split - 1) / split * tk;
 }
 
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -395,13 +439,13 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// [rows][128] bf16 cache viewed as a 2D tensor; box {64 dims, 64 keys}, 128B swizzle.
-static int cache_map(CUtensorMap* tm, const uint16_t* base, long long rows) {
+// [rows][128] bf16 cache viewed as a 2D tensor; box {64 dims, tk keys}, 128B swizzle.
+static int cache_map(CUtensorMap* tm, const uint16_t* base, long long rows, int tk) {
   auto fn = encode_fn();
   if (!fn) return SB_ERR_CONFIG;
   cuuint64_t dims[2] = {128, static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[1] = {256};
-  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(kTK)};
+  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(tk)};  // 128 B x tk keys
   cuuint32_t estr[2] = {1, 1};
   const CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(base), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -411,30 +455,45 @@ static int cache_map(CUtensorMap* tm, const uint16_t* base, long long rows) {
 
 int attn_launch(const AttnParams& p, int batch, bool pdl, cudaStream_t stream) {
   const int R = (p.n_q / p.n_kv) * p.m_per;
-  if (R > 64 || R < 1 || p.split < 1 || p.split > 8 || p.slots < 2 || p.chunk_cap % kTK) return SB_ERR_CONFIG;
-  const size_t smem = attn_smem_bytes(R, p.chunk_cap, p.slots);
+  const int tk = attn_tile_keys(p.split);
+  if (R > 64 || R < 1 || p.split < 1 || p.split > 8 || p.slots < 2 || p.chunk_cap % tk) return SB_ERR_CONFIG;
+  const size_t smem = attn_smem_bytes(R, p.chunk_cap, p.slots, tk);
   if (smem > 200 * 1024) return SB_ERR_CONFIG;
   CUtensorMap tmk, tmv;
-  if (cache_map(&tmk, p.k_cache, p.cache_rows) || cache_map(&tmv, p.v_cache, p.cache_rows)) return SB_ERR_CONFIG;
+  if (cache_map(&tmk, p.k_cache, p.cache_rows, tk) || cache_map(&tmv, p.v_cache, p.cache_rows, tk)) return SB_ERR_CONFIG;
   const int NT = (R + 7) / 8;
   void (*kern)(AttnParams, CUtensorMap, CUtensorMap) = nullptr;
-  switch (NT) {
-    case 1: kern = k_attn<1>; break;
-    case 2: kern = k_attn<2>; break;
-    case 3: kern = k_attn<3>; break;
-    case 4: kern = k_attn<4>; break;
-    case 5: kern = k_attn<5>; break;
-    case 6: kern = k_attn<6>; break;
-    case 7: kern = k_attn<7>; break;
-    default: kern = k_attn<8>; break;
+  if (tk == 64) {
+    switch (NT) {
+      case 1: kern = k_attn<1, 64>; break;
+      case 2: kern = k_attn<2, 64>; break;
+      case 3: kern = k_attn<3, 64>; break;
+      case 4: kern = k_attn<4, 64>; break;
+      case 5: kern = k_attn<5, 64>; break;
+      case 6: kern = k_attn<6, 64>; break;
+      case 7: kern = k_attn<7, 64>; break;
+      default: kern = k_attn<8, 64>; break;
+    }
+  } else {
+    switch (NT) {
+      case 1: kern = k_attn<1, 128>; break;
+      case 2: kern = k_attn<2, 128>; break;
+      case 3: kern = k_attn<3, 128>; break;
+      case 4: kern = k_attn<4, 128>; break;
+      case 5: kern = k_attn<5, 128>; break;
+      case 6: kern = k_attn<6, 128>; break;
+      case 7: kern = k_attn<7, 128>; break;
+      default: kern = k_attn<8, 128>; break;
+    }
   }
   int dev = 0;
   cudaGetDevice(&dev);
-  static unsigned configured[8] = {};
-  if (!(configured[NT - 1] & (1u << dev))) {
+  static unsigned configured[16] = {};
+  const int ki = (NT - 1) + (tk == 64 ? 0 : 8);
+  if (!(configured[ki] & (1u << dev))) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     if (e != cudaSuccess) return e;
-    configured[NT - 1] |= 1u << dev;
+    configured[ki] |= 1u << dev;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.split, p.n_kv, batch);

@@ -19,8 +19,9 @@ struct AttnParams {
   long long cache_rows;       // max_batch * n_kv * max_len (rows of 128 of each cache)
 };
 
+int attn_tile_keys(int split);
 int attn_key_capacity(int max_len, int split);
-size_t attn_smem_bytes(int R, int chunk_cap, int slots);
+size_t attn_smem_bytes(int R, int chunk_cap, int slots, int tk);
 int attn_launch(const AttnParams& p, int batch, bool pdl, cudaStream_t stream);
 
 }  // namespace sb
