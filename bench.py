@@ -173,7 +173,9 @@ def run_native(args, rank, world, local_rank):
 
     reset()
     for _ in range(2):  # eager warm-up of every kernel configuration before capture
+        n0 = int(eng.lib.sb_launch_count())
         eng.decode_step(st, 0)
+        launches_per_step = int(eng.lib.sb_launch_count()) - n0
     torch.cuda.synchronize()
     graphs[kr] = capture(kr)
     if K % kr:
@@ -204,9 +206,11 @@ def run_native(args, rank, world, local_rank):
     barrier()
     torch.cuda.synchronize()
     with ClockSampler(local_rank) as clk:
+        torch.cuda.nvtx.range_push("timed_steps")  # ncu --nvtx-include "timed_steps/" selects these launches
         ev0.record(stream)
         run_steps(K)
         ev1.record(stream)
+        torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
     barrier()
     ms = ev0.elapsed_time(ev1)
@@ -219,7 +223,7 @@ def run_native(args, rank, world, local_rank):
 
     # ---- dominant kernel, timed live on the launching stream ----------------------
     peak, peak_kind = _peaks()
-    dom = dominant_kernel(eng, st, d, B, T, fmt, reset)
+    dom = dominant_kernel(eng, st, d, B, T, fmt, reset, args.workload)
 
     # ---- e2e through the public API with host (pinned) buffers --------------------
     e2e = run_e2e(eng, wl, inp, B, K, dev, world)
@@ -252,7 +256,7 @@ def run_native(args, rank, world, local_rank):
             "parallelism": f"stream sharding x{world}, no collective", "l2": "inputs larger than L2 (weights "
             f"{eng.weight_bytes / 1e9:.2f} GB/step)",
         },
-        "gpu_launches": K * (5 * d.layers + 1),
+        "gpu_launches": K * launches_per_step,
         "clocks": clk.summary(),
         "roofline": dom["roofline"],
         "dominant_kernel": dom["info"],
@@ -264,7 +268,18 @@ def run_native(args, rank, world, local_rank):
     return out
 
 
-def dominant_kernel(eng, st, d, B, T, fmt, reset):
+# DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) from
+# one ncu capture of the same kernel and shape (profiles/), with the
+# algorithmic bytes of the captured case: the bench scales the traffic to its
+# own launch by the ratio of algorithmic bytes (same kernel, same tiling).
+PROFILED_TRAFFIC = {
+    ("b48", "attention"): (80.179456e6 + 2.41664e6, 61.5e6, "profiles/attention_b48_decode.md"),
+    ("b48", "gate_up"): (33.9008e6, 33.62e6, "profiles/tcgen05_gemm_gate_up_fp8_b48.md"),
+    ("b1", "gate_up"): (18.93376e6, 18.87e6, "profiles/gemv_gate_up_nvfp4_b1.md"),
+}
+
+
+def dominant_kernel(eng, st, d, B, T, fmt, reset, workload=None):
     """Time the step's largest kernel alone (same configuration), rotating over
     the 40 layers so its operands come from HBM.  Returns the roofline entry."""
     from starling_b200 import _lib
@@ -275,7 +290,10 @@ def dominant_kernel(eng, st, d, B, T, fmt, reset):
     stream = torch.cuda.current_stream()
     L = d.layers
     ctx = T  # decode position at the first timed step
-    kv_bytes = 2 * d.n_kv * 128 * 2 * B * (ctx + 1)
+    # K and V rows of the valid keys only: each stream's prompt part plus the new slot
+    plens = getattr(st, "prompt_len", None)
+    valid = int(plens[:B].sum().item()) + B if plens is not None else B * (ctx + 1)
+    kv_bytes = 2 * d.n_kv * 128 * 2 * valid
     cands = {}
     for name, op in (("gate_up", _lib.SB_OP_GATE_UP), ("attention", _lib.SB_OP_ATTN), ("down", _lib.SB_OP_DOWN)):
         if name == "attention":
@@ -311,9 +329,14 @@ def dominant_kernel(eng, st, d, B, T, fmt, reset):
     # dominant = largest total time per step
     name = max(cands, key=lambda n: cands[n]["us"])
     c = cands[name]
+    traffic, tsrc = None, None
+    prof = PROFILED_TRAFFIC.get((workload, name))
+    if prof is not None:
+        traffic = round(prof[0] * c["bytes"] / prof[1])
+        tsrc = f"ncu capture in {prof[2]}, scaled by algorithmic bytes"
     return {
         "roofline": {"bound": "hbm", "achieved": round(c["gbs"], 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(c["gbs"] / peak, 4), "traffic": None, "kernel": name,
+                     "frac": round(c["gbs"] / peak, 4), "traffic": traffic, "traffic_source": tsrc, "kernel": name,
                      "algorithmic_bytes_per_launch": c["bytes"], "avg_launch_us": round(c["us"], 3)},
         "info": {k: {kk: round(vv, 3) for kk, vv in v.items()} for k, v in cands.items()},
     }

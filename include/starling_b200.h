@@ -136,6 +136,9 @@ typedef struct SbState {
 /* ---- library ------------------------------------------------------------ */
 const char* sb_last_error(void);
 int sb_version(void);
+/* kernels this library has launched so far in this process (host counter; a
+ * launch recorded into a CUDA graph counts once, at capture) */
+uint64_t sb_launch_count(void);
 /* scratch bytes an SbState needs for (model, batch*m tokens) */
 size_t sb_workspace_bytes(const SbModel* model, int32_t tokens);
 

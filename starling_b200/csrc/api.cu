@@ -22,9 +22,13 @@
 #include "gemv.cuh"
 #include "glue.cuh"
 
+#include <atomic>
+
 using namespace sb;
 
 static thread_local char g_err[1024] = "";
+static std::atomic<unsigned long long> g_launches{0};
+void sb::note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 static int fail(int code, const char* fmt, ...) {
   va_list ap;
@@ -377,6 +381,7 @@ static int launch_op(const SbModel* md, const SbState* st, int l, int op, int st
 extern "C" {
 
 const char* sb_last_error(void) { return g_err; }
+uint64_t sb_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 int sb_version(void) { return 1; }
 
 size_t sb_workspace_bytes(const SbModel* md, int32_t tokens) {

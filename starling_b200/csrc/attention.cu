@@ -516,6 +516,7 @@ int attn_launch(const AttnParams& p, int batch, bool pdl, cudaStream_t stream) {
   }
   cfg.attrs = attrs;
   cfg.numAttrs = na;
+  note_launch();
   return cudaLaunchKernelEx(&cfg, kern, p, tmk, tmv);
 }
 

@@ -14,6 +14,9 @@ namespace sb {
 
 typedef __nv_bfloat16 bf16;
 
+// Kernels launched by this library (host-side counter, reported by sb_launch_count).
+void note_launch();
+
 // ---- rounding helpers -----------------------------------------------------
 // Every reference op rounds its result to bf16; these make the rounding
 // points explicit.

@@ -584,6 +584,7 @@ static int tc_launch_t(const GemvParams& p0, const void* w_tc, void* operand, co
   cfg.stream = stream;
   cfg.attrs = at;
   cfg.numAttrs = pdl ? 1 : 0;
+  note_launch();
   cudaError_t e = cudaLaunchKernelEx(&cfg, k_tc_prep<FMT>, p, xq, xshift, pl.mp, pl.np);
   if (e != cudaSuccess) return e;
 
@@ -614,6 +615,7 @@ static int tc_launch_t(const GemvParams& p0, const void* w_tc, void* operand, co
     ++na;
   }
   cfg.numAttrs = na;
+  note_launch();
   return cudaLaunchKernelEx(&cfg, k_tc_gemm<FMT>, p, a);
 }
 

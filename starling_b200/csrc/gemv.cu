@@ -574,6 +574,7 @@ static int launch_t(const GemvParams& p, const GemvCfg& c, bool pdl, cudaStream_
   }
   cfg.attrs = attrs;
   cfg.numAttrs = na;
+  note_launch();
   return cudaLaunchKernelEx(&cfg, k_gemv<FMT, NT>, p);
 }
 

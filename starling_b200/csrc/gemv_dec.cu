@@ -364,6 +364,7 @@ static int dec_launch_t(const GemvParams& p, const DecPlan& pl, bool pdl, cudaSt
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = pdl ? 1 : 0;
+  note_launch();
   return cudaLaunchKernelEx(&cfg, k_gemv_dec<FMT, KSW>, p, pl.slots, pl.batch);
 }
 

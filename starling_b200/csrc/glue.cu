@@ -236,6 +236,7 @@ int dequant_launch(const SbLinear& lin, void* out, bool f32, cudaStream_t s) {
   const size_t total = static_cast<size_t>(lin.n_pad / 16) * (lin.k / kge) * 32;
   const int bs = 256;
   const unsigned grid = static_cast<unsigned>((total + bs - 1) / bs);
+  note_launch();
   if (f32)
     k_dequant<float><<<grid, bs, 0, s>>>(lin, static_cast<float*>(out));
   else
@@ -256,29 +257,35 @@ int norm_rows_launch(const uint16_t* x, const int64_t* ids, const uint16_t* embe
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = pdl ? 1 : 0;
+  note_launch();
   return cudaLaunchKernelEx(&cfg, k_norm_rows, x, ids, embed, embed_rows, mult, w, y, h_out, n, eps);
 }
 
 int rmsnorm_launch(const uint16_t* x, const uint16_t* w, uint16_t* y, int rows, int n, float eps, cudaStream_t s) {
+  note_launch();
   k_rmsnorm<<<rows, 256, 0, s>>>(x, w, y, n, eps);
   return cudaGetLastError();
 }
 int silu_mul_launch(const uint16_t* g, const uint16_t* u, uint16_t* o, int64_t count, cudaStream_t s) {
   const int grid = static_cast<int>(std::min<int64_t>((count + 255) / 256, 148 * 16));
+  note_launch();
   k_silu_mul<<<grid > 0 ? grid : 1, 256, 0, s>>>(g, u, o, count);
   return cudaGetLastError();
 }
 int residual_launch(const uint16_t* x, const uint16_t* y, uint16_t* z, int64_t count, float alpha, cudaStream_t s) {
   const int grid = static_cast<int>(std::min<int64_t>((count + 255) / 256, 148 * 16));
+  note_launch();
   k_residual<<<grid > 0 ? grid : 1, 256, 0, s>>>(x, y, z, count, alpha);
   return cudaGetLastError();
 }
 int rope_launch(uint16_t* x, int rows, int heads, const int32_t* pos, const uint16_t* cs, const uint16_t* sn,
                 cudaStream_t s) {
+  note_launch();
   k_rope<<<rows, 64, 0, s>>>(x, rows, heads, pos, cs, sn);
   return cudaGetLastError();
 }
 int argmax_launch(const uint16_t* x, int rows, int n, int64_t* out, cudaStream_t s) {
+  note_launch();
   k_argmax<<<rows, 1024, 0, s>>>(x, n, out);
   return cudaGetLastError();
 }

@@ -1,0 +1,188 @@
+"""Per-kernel timings of the decode path on one GPU (also the small cases the
+ncu summaries under profiles/ are captured on).
+
+    python -m starling_b200.kernel_bench ops --workload b48        # every op of a step, graphs of 40 launches
+    python -m starling_b200.kernel_bench attention --batch 48      # sb_attention alone
+    python -m starling_b200.kernel_bench linear --fmt fp8 --n 16384 --k 2048 --m 48
+    python -m starling_b200.kernel_bench step --workload b48 --layers 4   # one eager step in NVTX range "step"
+
+Workloads (same as bench.py): b48 = 48 streams, FP8 weights, prompts
+U[300,900]; b1 = one stream, NVFP4 weights, 320 prompt positions.  Weights are
+seeded random-init N(0,0.02); every time is taken with CUDA events on the
+launching stream after warm-up, device time per launch.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import sys
+
+import torch
+
+from . import _lib, pack
+from . import synthetic as syn
+from ._lib import check, ptr
+from .batched import BatchedLLMMega
+from .engine import GraniteDims, GraniteEngine
+from .multistep import MultiStepLLMMega
+
+WORKLOADS = {"b48": (48, "fp8", 1040), "b1": (1, "nvfp4", 640)}
+OPS = ["qkv", "attention", "o", "gate_up", "down"]
+
+
+def _graph_time(fn, reps: int = 5) -> float:
+    """Device microseconds of one call of fn (captured once into a graph)."""
+    fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) * 1000.0 / reps
+
+
+def _decoder(workload: str, layers: int):
+    B, fmt, max_len = WORKLOADS[workload]
+    dev = torch.device("cuda")
+    d = GraniteDims(layers=layers)
+    w = syn.make_weights(d, seed=0, device=dev)
+    eng = GraniteEngine(d, w, fmt, max_cache_len=max_len, max_batch=B, device=dev)
+    emb = w["embed_tokens.weight"]
+    del w
+    torch.cuda.empty_cache()
+    if B == 1:
+        inp = syn.b1_inputs(emb, seed=0)
+        dec = MultiStepLLMMega(engine=eng, steps_per_replay=8)
+        dec.prefill(inp.inputs_embeds.to(dev))
+    else:
+        inp = syn.batched_inputs(d.hidden, batch=B, seed=0)
+        dec = BatchedLLMMega(engine=eng, max_batch_size=B, steps_per_replay=8)
+        dec.prefill(inp.inputs_embeds.to(dev), inp.prompt_lengths)
+    return eng, dec.state, inp.T, d
+
+
+def cmd_ops(a) -> None:
+    eng, st, T, d = _decoder(a.workload, a.layers)
+    lib = eng.lib
+    total = 0.0
+    for op, name in enumerate(OPS):
+        def run(op=op):
+            for layer in range(d.layers):
+                check(lib.sb_decode_op(C.byref(eng.cmodel), C.byref(st.c), layer, op, 0, _lib.current_stream()))
+        st.set_slot(T, pad_len=T)
+        us = _graph_time(run) / d.layers
+        total += us * d.layers
+        print(f"{a.workload} {name:9s} {us:9.2f} us per launch (mean over {d.layers} layers)")
+    st.set_slot(T, pad_len=T)
+    lm = _graph_time(lambda: check(lib.sb_decode_op(C.byref(eng.cmodel), C.byref(st.c), 0, _lib.SB_OP_LM_HEAD, 0,
+                                                    _lib.current_stream())))
+    print(f"{a.workload} lm_head   {lm:9.2f} us")
+    st.set_slot(T, pad_len=T)
+    step = _graph_time(lambda: eng.decode_step(st, 0))
+    print(f"{a.workload} sum of ops {total + lm:9.1f} us; one graphed step {step:9.1f} us")
+
+
+def cmd_step(a) -> None:
+    eng, st, T, d = _decoder(a.workload, a.layers)
+    for _ in range(2):
+        eng.decode_step(st, 0)
+    torch.cuda.synchronize()
+    n0 = int(eng.lib.sb_launch_count())
+    torch.cuda.nvtx.range_push("step")
+    eng.decode_step(st, 0)
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    print(f"{a.workload}: one step, {d.layers} layers, {int(eng.lib.sb_launch_count()) - n0} launches")
+
+
+def cmd_attention(a) -> None:
+    B = a.batch
+    layers = 4  # rotate over 4 layers' caches (> L2 at B=48)
+    max_len = 1040 if B > 1 else 640
+    d = GraniteDims(layers=layers, inter=256, vocab=256)
+    g = torch.Generator(device="cuda").manual_seed(1)
+    w = {"embed_tokens.weight": (256, 2048), "norm.weight": (2048,)}
+    for i in range(layers):
+        p = f"layers.{i}."
+        w.update({p + "input_layernorm.weight": (2048,), p + "post_attention_layernorm.weight": (2048,),
+                  p + "self_attn.q_proj.weight": (2048, 2048), p + "self_attn.k_proj.weight": (512, 2048),
+                  p + "self_attn.v_proj.weight": (512, 2048), p + "self_attn.o_proj.weight": (2048, 2048),
+                  p + "mlp.gate_proj.weight": (256, 2048), p + "mlp.up_proj.weight": (256, 2048),
+                  p + "mlp.down_proj.weight": (2048, 256)})
+    w = {k: (torch.randn(s, generator=g, device="cuda") * 0.02).to(torch.bfloat16) for k, s in w.items()}
+    eng = GraniteEngine(d, w, "bf16", max_cache_len=max_len, max_batch=B, tensor_cores=False)
+    gen = torch.Generator().manual_seed(0)
+    if B > 1:
+        pl = torch.randint(300, 901, (B,), generator=gen)
+        T = int(pl.max())
+    else:
+        pl, T = torch.tensor([320]), 320
+    st = eng.new_state(B, 1, _lib.SB_MODE_DECODE, out_steps=1, prompt_len=pl, rope_off=T - pl)
+    eng.kv.normal_()
+    st.q.normal_()
+    st.set_slot(T, pad_len=T)
+
+    def run():
+        for layer in range(a.reps):
+            check(eng.lib.sb_attention(C.byref(eng.cmodel), C.byref(st.c), layer % layers, _lib.current_stream()))
+
+    us = _graph_time(run) / a.reps
+    nbytes = (int(pl.sum()) + B) * d.n_kv * 2 * 256
+    print(f"attention B={B} ctx<= {T}: {us:.2f} us per launch; valid K/V bytes {nbytes / 1e6:.1f} MB "
+          f"-> {nbytes / us / 1e3:.0f} GB/s; err={int(st.ctrl[_lib.SB_CTRL_ERR])}")
+
+
+def cmd_linear(a) -> None:
+    lib = _lib.load()
+    w = (torch.randn(a.n, a.k, device="cuda") * 0.02).to(torch.bfloat16)
+    copies = [pack.pack_matrix(w, a.fmt, tc=True) for _ in range(4)]  # rotate: 4 copies > L2 at large n
+    cs = [p.c_struct() for p in copies]
+    x = torch.randn(a.m, a.k, device="cuda").to(torch.bfloat16)
+    y = torch.empty(a.m, a.n, dtype=torch.bfloat16, device="cuda")
+    need = int(lib.sb_linear_workspace_bytes(C.byref(cs[0]), a.m))
+    ws = torch.empty(max(need, 16), dtype=torch.uint8, device="cuda")
+
+    def run():
+        for i in range(a.reps):
+            check(lib.sb_linear_ex(C.byref(cs[i % 4]), ptr(x), ptr(y), a.m, ptr(ws), need, 1, _lib.current_stream()))
+
+    us = _graph_time(run) / a.reps
+    nbytes = copies[0].nbytes
+    path = "tcgen05" if need else "gemv"
+    print(f"linear {a.fmt} n={a.n} k={a.k} m={a.m} ({path}): {us:.2f} us per launch; weight bytes "
+          f"{nbytes / 1e6:.2f} MB -> {nbytes / us / 1e3:.0f} GB/s")
+
+
+def main(argv=None) -> None:
+    ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
+    sub = ap.add_subparsers(dest="cmd", required=True)
+    p = sub.add_parser("ops")
+    p.add_argument("--workload", choices=list(WORKLOADS), default="b48")
+    p.add_argument("--layers", type=int, default=40)
+    p = sub.add_parser("step")
+    p.add_argument("--workload", choices=list(WORKLOADS), default="b48")
+    p.add_argument("--layers", type=int, default=4)
+    p = sub.add_parser("attention")
+    p.add_argument("--batch", type=int, default=48)
+    p.add_argument("--reps", type=int, default=20)
+    p = sub.add_parser("linear")
+    p.add_argument("--fmt", default="fp8")
+    p.add_argument("--n", type=int, default=16384)
+    p.add_argument("--k", type=int, default=2048)
+    p.add_argument("--m", type=int, default=48)
+    p.add_argument("--reps", type=int, default=20)
+    a = ap.parse_args(argv)
+    torch.set_grad_enabled(False)
+    {"ops": cmd_ops, "step": cmd_step, "attention": cmd_attention, "linear": cmd_linear}[a.cmd](a)
+
+
+if __name__ == "__main__":
+    sys.exit(main())
