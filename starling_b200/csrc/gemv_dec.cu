@@ -230,9 +230,8 @@ __global__ void __launch_bounds__(512, 1) k_gemv_dec(const __grid_constant__ Gem
       const int j = jb + jj;
       const uint8_t* slot = ring + static_cast<size_t>(j % slots) * slot_bytes;
       ring_wait(bars + (j % slots), static_cast<uint32_t>((j / slots) & 1), err);
-      float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 1
-      for (int q = 0; q < KPW; ++q) {
+      // one kgroup of this warp's K slice into acc (decode + mma.sync chain)
+      auto kg_step = [&](int q, float* acc) {
         const int kg = warp * KPW + q;
         const uint4 a = *reinterpret_cast<const uint4*>(slot + static_cast<size_t>(kg) * 512 + lane * 16);
         const uint16_t* xq = xb + q * KGE;
@@ -273,7 +272,16 @@ __global__ void __launch_bounds__(512, 1) k_gemv_dec(const __grid_constant__ Gem
           const uint32_t A[4] = {a.x, a.y, a.z, a.w};
           mma_bf16(acc, A, *reinterpret_cast<const uint32_t*>(xq), *reinterpret_cast<const uint32_t*>(xq + 8));
         }
+      };
+      // two independent accumulator chains (kgroups in pairs), summed at the end
+      float acc[4] = {0.f, 0.f, 0.f, 0.f}, acc2[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+      for (int q = 0; q < KPW; q += 2) {
+        kg_step(q, acc);
+        kg_step(q + 1, acc2);
       }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[e] += acc2[e];
       // undo this warp's activation scale, store the partial of tile jj
       float* rw = red + (static_cast<size_t>(jj) * W + warp) * 16 * M;
       const int col = 2 * c;
