@@ -184,7 +184,7 @@ int sb_lm_head_argmax_static(const SbModel* model, const SbState* state, int32_t
 
 /* ---- single ops (each one replaces one reference call site) ------------- */
 /* y[m, :] = x[m, :] W^T, bf16 out: nn.Linear (llm_mega.py:534-536,560,572-573,579,588).
- * Any m >= 1 (processed in blocks of 64 rows); y columns in packed row order.
+ * Any m >= 1; y columns in packed row order.
  * GEMV kernels only (no workspace). */
 int sb_linear(const SbLinear* lin, const uint16_t* x, uint16_t* y, int32_t m, int32_t use_pdl,
               sb_stream_t stream);
@@ -192,7 +192,8 @@ int sb_linear(const SbLinear* lin, const uint16_t* x, uint16_t* y, int32_t m, in
  * GEMM (0: that path does not serve it) */
 size_t sb_linear_workspace_bytes(const SbLinear* lin, int32_t m);
 /* sb_linear with operand scratch: with lin->w_tc set and m > 8 the rows go
- * through the tcgen05 GEMM in blocks of 128 (prefill projections) */
+ * through the tcgen05 GEMM (token tiles of 128 in one launch, blocks of up to
+ * 8192 rows; prefill projections) */
 int sb_linear_ex(const SbLinear* lin, const uint16_t* x, uint16_t* y, int32_t m, void* workspace,
                  size_t workspace_bytes, int32_t use_pdl, sb_stream_t stream);
 /* exact dequantisation of a packed layer to fp32 [n, k] (rows in packed order,

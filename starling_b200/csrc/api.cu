@@ -414,9 +414,13 @@ int sb_linear(const SbLinear* lin, const uint16_t* x, uint16_t* y, int32_t m, in
   return sb_linear_ex(lin, x, y, m, nullptr, 0, use_pdl, stream);
 }
 
+// sb_linear_ex runs the tensor-core GEMM on blocks of at most this many rows
+// (one activation preparation + one launch each; weights re-streamed per block)
+static const int kLinearBlockRows = 8192;
+
 size_t sb_linear_workspace_bytes(const SbLinear* lin, int32_t m) {
   if (!lin || m < 1) return 0;
-  return tc_scratch_need(*lin, m > 128 ? 128 : m);
+  return tc_scratch_need(*lin, m > kLinearBlockRows ? kLinearBlockRows : m);
 }
 
 int sb_linear_ex(const SbLinear* lin, const uint16_t* x, uint16_t* y, int32_t m, void* workspace,
@@ -425,10 +429,10 @@ int sb_linear_ex(const SbLinear* lin, const uint16_t* x, uint16_t* y, int32_t m,
   if (m < 1) return fail(SB_ERR_ARG, "sb_linear: m must be >= 1");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   TcPlan pl;
-  if (workspace && tc_plan_for(*lin, m > 128 ? 128 : m, pl)) {
-    // tensor-core path in blocks of at most 128 token rows
-    for (int r0 = 0; r0 < m; r0 += 128) {
-      const int mr = m - r0 < 128 ? m - r0 : 128;
+  if (workspace && tc_plan_for(*lin, m > kLinearBlockRows ? kLinearBlockRows : m, pl)) {
+    // tensor-core path: token tiles of 128 inside one launch, blocks of kLinearBlockRows
+    for (int r0 = 0; r0 < m; r0 += kLinearBlockRows) {
+      const int mr = m - r0 < kLinearBlockRows ? m - r0 : kLinearBlockRows;
       GemvParams p = base_params(*lin, mr);
       p.pro = PRO_NONE;
       p.x = x + static_cast<size_t>(r0) * lin->k;

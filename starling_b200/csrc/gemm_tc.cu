@@ -186,6 +186,7 @@ struct TcArgs {
   const int32_t* xshift;  // fp8: per-row power-of-two scale of the activations
   uint32_t idesc;
   int mp, np, tiles, kb, split, stages, ncols;
+  int mtiles;  // token tiles of mp rows (EPI_STORE only when > 1: prefill projections)
 };
 
 // ---- B operand: prologue + layout ------------------------------------------------
@@ -200,9 +201,12 @@ template <int FMT>
 __global__ void __launch_bounds__(kPrepThreads) k_tc_prep(const __grid_constant__ GemvParams p, uint8_t* xq,
                                                            int32_t* xshift, int mp, int np) {
   __shared__ float s_red[kPrepThreads / 32];
-  const int m = blockIdx.x, tid = threadIdx.x, K = p.k;
+  const int m = blockIdx.x, tid = threadIdx.x, K = p.k;  // m: token (padded to whole token tiles)
   const int n16 = K / 16;
   const size_t kb_bytes = static_cast<size_t>(np) * 128;
+  // token tile m / mp holds rows mp * tile .. of the operand, each tile [kb][np/8][8][8][16 B]
+  uint8_t* xt = xq + static_cast<size_t>(m / mp) * (K * (FMT == SB_FMT_BF16 ? 2 : 1) / 128) * kb_bytes;
+  const int ml = m % mp;  // row of the token within its tile
   auto off = [&](int n, int c) -> size_t {  // 16-byte chunk c (along K bytes) of B-operand row n
     return static_cast<size_t>(c >> 3) * kb_bytes + static_cast<size_t>(n >> 3) * 1024 + (c & 7) * 128 + (n & 7) * 16;
   };
@@ -211,8 +215,8 @@ __global__ void __launch_bounds__(kPrepThreads) k_tc_prep(const __grid_constant_
   pdl_launch();
   if (m >= p.m) {
     for (int c = tid; c < n16 * CPE; c += kPrepThreads) {
-      *reinterpret_cast<uint4*>(xq + off(m, c)) = make_uint4(0, 0, 0, 0);
-      if (FMT == SB_FMT_FP8) *reinterpret_cast<uint4*>(xq + off(mp + m, c)) = make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4*>(xt + off(ml, c)) = make_uint4(0, 0, 0, 0);
+      if (FMT == SB_FMT_FP8) *reinterpret_cast<uint4*>(xt + off(mp + ml, c)) = make_uint4(0, 0, 0, 0);
     }
     if (FMT == SB_FMT_FP8 && tid == 0) xshift[m] = 0;
     return;
@@ -270,8 +274,8 @@ __global__ void __launch_bounds__(kPrepThreads) k_tc_prep(const __grid_constant_
     for (int j = 0; j < kPrepChunks; ++j) {
       const int c16 = tid + j * kPrepThreads;
       if (c16 < n16) {
-        *reinterpret_cast<uint4*>(xq + off(m, 2 * c16)) = pack8(f[j]);
-        *reinterpret_cast<uint4*>(xq + off(m, 2 * c16 + 1)) = pack8(f[j] + 8);
+        *reinterpret_cast<uint4*>(xt + off(ml, 2 * c16)) = pack8(f[j]);
+        *reinterpret_cast<uint4*>(xt + off(ml, 2 * c16 + 1)) = pack8(f[j] + 8);
       }
     }
   } else {
@@ -297,8 +301,8 @@ __global__ void __launch_bounds__(kPrepThreads) k_tc_prep(const __grid_constant_
           const float t0 = e4m3_round(v, q0[e]);
           e4m3_round((v - t0) * 16.f, q1[e]);  // exact residual
         }
-        *reinterpret_cast<uint4*>(xq + off(m, c16)) = *reinterpret_cast<const uint4*>(q0);
-        *reinterpret_cast<uint4*>(xq + off(mp + m, c16)) = *reinterpret_cast<const uint4*>(q1);
+        *reinterpret_cast<uint4*>(xt + off(ml, c16)) = *reinterpret_cast<const uint4*>(q0);
+        *reinterpret_cast<uint4*>(xt + off(mp + ml, c16)) = *reinterpret_cast<const uint4*>(q1);
       }
     }
   }
@@ -331,7 +335,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
   const int q = S > 1 ? static_cast<int>(cg::this_cluster().block_rank()) : 0;
   const int cid = blockIdx.x / S, ncl = gridDim.x / S;
   const int kb0 = q * a.kb / S, kb1 = (q + 1) * a.kb / S, nk = kb1 - kb0;
-  const int my_tiles = cid < a.tiles ? (a.tiles - cid + ncl - 1) / ncl : 0;
+  // work items (weight tile, token tile), token tiles inner so that the CTAs
+  // working at the same time share weight tiles (L2 hits)
+  const int items = a.tiles * a.mtiles;
+  const int my_tiles = cid < items ? (items - cid + ncl - 1) / ncl : 0;
   const uint32_t a_bytes = 16384u, b_bytes = static_cast<uint32_t>(a.np) * 128u;
   // CTAs start their K blocks at different offsets so that they do not all read
   // the same activation block from L2 at the same time
@@ -367,10 +374,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
       const int total = my_tiles * nk;
       auto kb_of = [&](int it) { return kb0 + (it % nk + rot) % nk; };
       auto a_src = [&](int it) {
-        const int t = cid + (it / nk) * ncl;
+        const int t = (cid + (it / nk) * ncl) / a.mtiles;
         return a.wt + (static_cast<size_t>(t) * a.kb + kb_of(it)) * 16384;
       };
-      auto b_src = [&](int it) { return a.xq + static_cast<size_t>(kb_of(it)) * b_bytes; };
+      auto b_src = [&](int it) {
+        const int tt = (cid + (it / nk) * ncl) % a.mtiles;
+        return a.xq + (static_cast<size_t>(tt) * a.kb + kb_of(it)) * b_bytes;
+      };
       const int pre = total < a.stages ? total : a.stages;
       for (int it = 0; it < pre; ++it) {  // weights do not depend on the previous kernel
         mbar_expect_tx(full + it, a_bytes + b_bytes);
@@ -420,19 +430,23 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
     // the 8-token chunks h, h + 2, ... with h = w / 4 ----
     pdl_wait();
     pdl_launch();
-    if (FMT == SB_FMT_FP8)  // 2^-shift per token: exact power of two
-      for (int i = tid; i < M; i += kTcEpiWarps * 32) reinterpret_cast<float*>(s_shift)[i] = ldexpf(1.f, -a.xshift[i]);
-    epi_sync();
-    const float* s_unscale = reinterpret_cast<const float*>(s_shift);
+    float* s_unscale = reinterpret_cast<float*>(s_shift);  // 2^-shift per token of the tile: exact
     const int lq = warp & 3, h = warp >> 2;
     const int lrow = lq * 32 + lane;
     const int rp = tc_rows_per_rank(S);
     for (int tc = 0; tc < my_tiles; ++tc) {
-      const int t = cid + tc * ncl, buf = tc & 1;
+      const int item = cid + tc * ncl, buf = tc & 1;
+      const int t = item / a.mtiles, tok0 = (item % a.mtiles) * a.mp;
+      const int Mt = M - tok0 < a.mp ? M - tok0 : a.mp;  // tokens of this tile
+      if (FMT == SB_FMT_FP8) {
+        epi_sync();  // every warp is done with the previous tile's scales
+        for (int i = tid; i < Mt; i += kTcEpiWarps * 32) s_unscale[i] = ldexpf(1.f, -a.xshift[tok0 + i]);
+        epi_sync();
+      }
       const uint32_t taddr = tmem + buf * half_cols + (static_cast<uint32_t>(lq * 32) << 16);
       wait_bounded(acc_full + buf, static_cast<uint32_t>((tc / 2) & 1), err);
       tc_fence_after();
-      for (int m0 = h * 8; m0 < M; m0 += 16) {
+      for (int m0 = h * 8; m0 < Mt; m0 += 16) {
         // 8 tokens of this lane's row: D0 (and D1 for the fp8 split) columns
         uint32_t d0[8], d1[8];
         tmem_ld8(taddr + m0, d0);
@@ -443,13 +457,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
         for (int i = 0; i < 8; ++i) {
           v[i] = __uint_as_float(d0[i]);
           if (FMT == SB_FMT_FP8) {
-            const int m = m0 + i < M ? m0 + i : M - 1;
+            const int m = m0 + i < Mt ? m0 + i : Mt - 1;
             v[i] = fmaf(__uint_as_float(d1[i]), 0.0625f, v[i]) * s_unscale[m];  // (D0 + D1/16) 2^-s
           }
         }
         if (S == 1) {
           const int row = t * 128 + lrow;
-          tc_epi<FMT, 8>(p, row, row < p.n, v, m0, M, wb_val, wb_idx, warp);
+          tc_epi<FMT, 8>(p, row, row < p.n, v, m0, Mt, wb_val, wb_idx, warp, tok0);
         } else {
           // push this K partial to the rank that finishes the row (16-byte DSMEM stores)
           float* dst = cg::this_cluster().map_shared_rank(part, lrow / rp) + (q * rp + lrow % rp) * ms + m0;
@@ -483,7 +497,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
           v[3] += x4.w;
         }
       const int row = cid * 128 + r0 + lr;
-      tc_epi<FMT, 4>(p, row, ok && row < p.n, v, m0, M, wb_val, wb_idx, warp);
+      tc_epi<FMT, 4>(p, row, ok && row < p.n, v, m0, M, wb_val, wb_idx, warp, 0);
     }
   }
   if (p.epi == EPI_ARGMAX) {  // combine the warps' running bests (order-independent total order)
@@ -517,23 +531,31 @@ static const size_t kTcSmem = 220 * 1024;
 static int elem_bytes(int fmt) { return fmt == SB_FMT_BF16 ? 2 : 1; }
 static int pad_rows(int fmt, int m) { return fmt == SB_FMT_BF16 ? (m + 15) / 16 * 16 : (m + 7) / 8 * 8; }
 
+// token rows above 128 are processed in tiles of 128 (one launch)
+static int tile_rows(int fmt, int m) { return m > 128 ? 128 : pad_rows(fmt, m); }
+
 size_t tc_operand_bytes(int fmt, int k, int m) {
   if (!tc_format(fmt) || m < 1) return 0;
-  const int mp = pad_rows(fmt, m);
+  const int mp = tile_rows(fmt, m), mtiles = (m + mp - 1) / mp;
   const int np = fmt == SB_FMT_FP8 ? 2 * mp : mp;
-  return static_cast<size_t>(np) * k * elem_bytes(fmt) + 128 * 4;
+  return static_cast<size_t>(mtiles) * np * k * elem_bytes(fmt) + static_cast<size_t>(mtiles) * mp * 4;
 }
 
 bool tc_plan(int fmt, int n, int k, int m, TcPlan& pl) {
-  if (!tc_format(fmt) || m < 1 || m > 128 || n < 1) return false;
+  if (!tc_format(fmt) || m < 1 || n < 1) return false;
   const int eb = elem_bytes(fmt);
   if ((k * eb) % 128 != 0 || k > 16 * kPrepThreads * kPrepChunks) return false;
-  pl.mp = pad_rows(fmt, m);
+  pl.mp = tile_rows(fmt, m);
+  pl.mtiles = (m + pl.mp - 1) / pl.mp;
   pl.np = fmt == SB_FMT_FP8 ? 2 * pl.mp : pl.mp;
   if (pl.np < 16 || pl.np > 256) return false;
   pl.tiles = (n + 127) / 128;
   pl.kb = k * eb / 128;
-  if (pl.tiles * 4 >= kSMs * 3) {  // enough tiles: persistent, no K split
+  if (pl.mtiles > 1) {  // many token tiles (prefill): persistent over (weight tile, token tile)
+    pl.split = 1;
+    const int items = pl.tiles * pl.mtiles;
+    pl.n_ctas = items < kSMs ? items : kSMs;
+  } else if (pl.tiles * 4 >= kSMs * 3) {  // enough tiles: persistent, no K split
     pl.split = 1;
     pl.n_ctas = pl.tiles < kSMs ? pl.tiles : kSMs;
   } else {
@@ -548,13 +570,14 @@ bool tc_plan(int fmt, int n, int k, int m, TcPlan& pl) {
   pl.ncols = 32;
   while (pl.ncols < 2 * pl.np) pl.ncols *= 2;  // two accumulator buffers
   pl.stages = 0;
+  const int ml = m < pl.mp ? m : pl.mp;  // token rows of one tile
   for (int st = 8; st >= 2; --st)
-    if (tc_layout(pl.np, st, m, pl.split).total <= kTcSmem) {
+    if (tc_layout(pl.np, st, ml, pl.split).total <= kTcSmem) {
       pl.stages = st;
       break;
     }
   if (!pl.stages) return false;
-  pl.smem = tc_layout(pl.np, pl.stages, m, pl.split).total;
+  pl.smem = tc_layout(pl.np, pl.stages, ml, pl.split).total;
   return true;
 }
 
@@ -573,13 +596,14 @@ static int tc_launch_t(const GemvParams& p0, const void* w_tc, void* operand, co
   GemvParams p = p0;
   p.n_ctas = pl.n_ctas;
   uint8_t* xq = static_cast<uint8_t*>(operand);
-  int32_t* xshift = reinterpret_cast<int32_t*>(xq + static_cast<size_t>(pl.np) * p.k * elem_bytes(FMT));
+  int32_t* xshift =
+      reinterpret_cast<int32_t*>(xq + static_cast<size_t>(pl.mtiles) * pl.np * p.k * elem_bytes(FMT));
 
   cudaLaunchAttribute at[2];
   at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(pl.mp);
+  cfg.gridDim = dim3(pl.mp * pl.mtiles);
   cfg.blockDim = dim3(kPrepThreads);
   cfg.stream = stream;
   cfg.attrs = at;
@@ -602,6 +626,7 @@ static int tc_launch_t(const GemvParams& p0, const void* w_tc, void* operand, co
   a.split = pl.split;
   a.stages = pl.stages;
   a.ncols = pl.ncols;
+  a.mtiles = pl.mtiles;
   cfg.gridDim = dim3(pl.n_ctas);
   cfg.blockDim = dim3(kTcThreads);
   cfg.dynamicSmemBytes = pl.smem;

@@ -14,6 +14,7 @@ struct TcPlan {
   int np;      // MMA N = B-operand rows: 2*mp (fp8: two e4m3 terms) or mp (bf16)
   int tiles;   // 128-row weight tiles
   int kb;      // 128-byte K blocks
+  int mtiles;  // token tiles of mp rows (> 1 only for the store epilogue: prefill)
   int split;   // CTAs per cluster splitting K (1 = persistent over tiles)
   int stages;  // ring depth
   int ncols;   // TMEM columns allocated

@@ -14,11 +14,12 @@ namespace sb {
 
 // v[i]: dot product of this lane's row and token m0 + i, activation scaling
 // undone, weight scale not yet applied.  row_ok: the row exists (row < n).
+// tok0: first token of the token tile (the store epilogue only; 0 otherwise).
 // Must be called by full warps with warp-uniform m0.  ARGMAX keeps a running
 // best per (warp, token) in wb_val/wb_idx[warp * 128 + m].
 template <int FMT, int CNT>
 __device__ __forceinline__ void tc_epi(const GemvParams& p, int row, bool row_ok, float* v, int m0, int M,
-                                       float* wb_val, int* wb_idx, int warp) {
+                                       float* wb_val, int* wb_idx, int warp, int tok0) {
   const int lane = threadIdx.x & 31;
   float rs = 1.f;
   if (row_ok) {
@@ -30,7 +31,7 @@ __device__ __forceinline__ void tc_epi(const GemvParams& p, int row, bool row_ok
   if (p.epi == EPI_STORE) {
 #pragma unroll
     for (int i = 0; i < CNT; ++i)
-      if (row_ok && m0 + i < M) p.y[static_cast<size_t>(m0 + i) * p.n + row] = f_to_bf16_bits(v[i]);
+      if (row_ok && m0 + i < M) p.y[static_cast<size_t>(tok0 + m0 + i) * p.n + row] = f_to_bf16_bits(v[i]);
   } else if (p.epi == EPI_RESID) {
     // hidden = hidden + bf16(res_mult * bf16(y))   (llm_kernels.py:306-313)
     float h[CNT];

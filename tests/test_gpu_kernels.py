@@ -114,7 +114,7 @@ def _linear_tc(p, x, pdl=0):
 @pytest.mark.parametrize("fmt", ["bf16", "fp8"])
 @pytest.mark.parametrize("n,k,m", [(3072, 2048, 48), (2048, 8192, 48), (16384, 2048, 48), (2051, 512, 9),
                                    (4096, 1024, 16), (1000, 2048, 33), (2048, 2048, 64), (640, 1024, 128),
-                                   (384, 512, 300)])
+                                   (384, 512, 300), (2048, 2048, 1000), (1000, 1024, 8300)])
 def test_linear_tensor_cores(fmt, n, k, m):
     """tcgen05 GEMM (9..128 rows per block, fp8 activations as two e4m3 terms)
     vs the fp32 reference over the exactly dequantised weight: same bar as the
