@@ -182,6 +182,28 @@ int sb_lm_head_argmax(const SbModel* model, const SbState* state, int32_t step, 
  * array: calls that overlap on the GPU race. */
 int sb_lm_head_argmax_static(const SbModel* model, const SbState* state, int32_t step, sb_stream_t stream);
 
+/* ---- prefill --------------------------------------------------------------
+ * Prefill of `batch` right-padded prompts of T positions each, the eager
+ * GraniteModel forward of LLMMega.prefill / BatchedLLMMega.prefill
+ * (llm_mega.py:176-202, batched.py:222-276) on the library's kernels: per
+ * layer q/k/v (RMSNorm prologue, RoPE at positions 0..T-1, K/V written to
+ * cache slots 0..T-1 of streams 0..batch-1), causal attention over each
+ * stream's keys [0, prompt_len[b]), o + residual, gate/up (RMSNorm, SwiGLU),
+ * down + residual.  hidden [batch*T, hidden] bf16 holds the input embeddings
+ * times the embedding multiplier on entry and the last layer's output rows on
+ * exit (the caller applies the final norm / lm_head to the rows it needs).
+ * T must be a multiple of 8 and <= max_len (pad the prompts; prompt_len
+ * masks the padding); prompt_len: device int32 [batch], or NULL = T for all.
+ * Scratch: q and attn [batch*T, n_q*128], act [sb_prefill_block_rows(), inter],
+ * workspace of sb_prefill_workspace_bytes().  Every projection must be served
+ * by the tensor-core GEMM (tile copies present; > 64 rows per block for
+ * NVFP4 / INT8), else SB_ERR_CONFIG. */
+size_t sb_prefill_workspace_bytes(const SbModel* model, int32_t batch, int32_t T);
+int32_t sb_prefill_block_rows(const SbModel* model, int32_t batch, int32_t T);
+int sb_prefill(const SbModel* model, uint16_t* hidden, int32_t batch, int32_t T, const int32_t* prompt_len,
+               uint16_t* q, uint16_t* attn, uint16_t* act, void* workspace, size_t workspace_bytes,
+               sb_stream_t stream);
+
 /* ---- single ops (each one replaces one reference call site) ------------- */
 /* y[m, :] = x[m, :] W^T, bf16 out: nn.Linear (llm_mega.py:534-536,560,572-573,579,588).
  * Any m >= 1; y columns in packed row order.

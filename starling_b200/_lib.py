@@ -66,6 +66,7 @@ EXPORTS = [
     "sb_linear", "sb_dequant_f32", "sb_dequant_bf16", "sb_rmsnorm", "sb_silu_mul",
     "sb_residual_scale", "sb_rope", "sb_argmax_bf16", "sb_attention", "sb_decode_op",
     "sb_lm_head_argmax_static", "sb_linear_ex", "sb_linear_workspace_bytes", "sb_launch_count",
+    "sb_prefill", "sb_prefill_workspace_bytes", "sb_prefill_block_rows",
 ]
 
 
@@ -89,6 +90,11 @@ def load() -> C.CDLL:
     lib = C.CDLL(str(LIB_PATH))
     lib.sb_last_error.restype = C.c_char_p
     lib.sb_launch_count.restype = C.c_uint64
+    lib.sb_prefill_workspace_bytes.restype = C.c_size_t
+    lib.sb_prefill_workspace_bytes.argtypes = [C.POINTER(SbModel), C.c_int32, C.c_int32]
+    lib.sb_prefill_block_rows.restype = C.c_int32
+    lib.sb_prefill_block_rows.argtypes = [C.POINTER(SbModel), C.c_int32, C.c_int32]
+    lib.sb_prefill.argtypes = [C.POINTER(SbModel), vp, C.c_int32, C.c_int32, vp, vp, vp, vp, vp, C.c_size_t, vp]
     lib.sb_workspace_bytes.restype = C.c_size_t
     lib.sb_workspace_bytes.argtypes = [C.POINTER(SbModel), C.c_int32]
     lib.sb_decode_step.argtypes = [C.POINTER(SbModel), C.POINTER(SbState), C.c_int32, vp]

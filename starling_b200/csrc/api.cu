@@ -94,9 +94,13 @@ static bool use_tc_kernel() {
   return v == 1;
 }
 
-// The tcgen05 path serves a linear with a tile copy for 9..128 token rows.
+// The tcgen05 path serves a linear with a tile copy above 8 token rows (FP8,
+// bf16: the copy has the packed weight's bytes) or above 64 rows (NVFP4, INT8:
+// the bf16 copy has 4x / 2x the bytes, worth it only where the work is
+// compute-bound, i.e. prefill).
 static bool tc_plan_for(const SbLinear& l, int m, TcPlan& pl) {
-  return m > 8 && l.w_tc && use_tc_kernel() && tc_plan(l.fmt, l.n, l.k, m, pl);
+  const int min_rows = (l.fmt == SB_FMT_NVFP4 || l.fmt == SB_FMT_INT8) ? 64 : 8;
+  return m > min_rows && l.w_tc && use_tc_kernel() && tc_plan(l.fmt, l.n, l.k, m, pl);
 }
 
 static int run_gemv(GemvParams& p, int fmt, bool pdl, cudaStream_t s) {
@@ -295,6 +299,7 @@ static int launch_attention(const SbModel* md, const SbState* st, int l, cudaStr
   a.slots = 2 * tiles < 3 ? 2 * tiles : 3;
   if (a.slots < 2) a.slots = 2;
   a.cache_rows = static_cast<long long>(md->max_batch) * md->n_kv * md->max_len;
+  a.qblocks = 1;
   const int rc = attn_launch(a, st->batch, st->use_pdl != 0, s);
   if (rc == SB_ERR_CONFIG) return fail(rc, "no attention configuration (rows=%d)", (md->n_q / md->n_kv) * st->m);
   if (rc != 0) return fail(rc, "attention launch: %s", cudaGetErrorString((cudaError_t)rc));
@@ -448,6 +453,168 @@ int sb_linear_ex(const SbLinear* lin, const uint16_t* x, uint16_t* y, int32_t m,
   p.epi = EPI_STORE;
   p.y = y;
   return run_gemv(p, lin->fmt, use_pdl != 0, s);
+}
+
+// ---- native prefill -------------------------------------------------------------
+// Query tokens per attention CTA (R = n_q / n_kv * 8 query rows <= 64) and the
+// projection rows per launch (whole streams).
+static const int kPrefillQBlock = 8;
+static const int kPrefillBlockRows = 8192;
+
+static int prefill_streams_per_block(int B, int T) {
+  int spb = kPrefillBlockRows / T;
+  if (spb < 1) spb = 1;
+  return spb < B ? spb : B;
+}
+
+struct PrefillWs {
+  int32_t* ctrl;
+  void* tc;
+  size_t tc_bytes, total;
+};
+static PrefillWs prefill_ws(const SbModel* md, int B, int T, void* base) {
+  PrefillWs w;
+  const int rows = prefill_streams_per_block(B, T) * T;
+  size_t need = 0;
+  for (int l = 0; md->layers && l < md->n_layers; ++l) {
+    const SbLayer& L = md->layers[l];
+    const SbLinear* lins[4] = {&L.qkv, &L.o, &L.gate_up, &L.down};
+    for (const SbLinear* x : lins) {
+      const size_t b = tc_scratch_need(*x, rows);
+      if (b > need) need = b;
+    }
+  }
+  w.ctrl = static_cast<int32_t*>(base);
+  w.tc = base ? static_cast<char*>(base) + 256 : nullptr;
+  w.tc_bytes = need;
+  w.total = 256 + need;
+  return w;
+}
+
+static int check_prefill(const SbModel* md, int B, int T) {
+  if (!md || !md->layers || md->n_layers < 1) return fail(SB_ERR_ARG, "sb_prefill: no model");
+  if (B < 1 || B > md->max_batch) return fail(SB_ERR_ARG, "sb_prefill: batch %d outside [1, %d]", B, md->max_batch);
+  if (T < kPrefillQBlock || T % kPrefillQBlock || T > md->max_len)
+    return fail(SB_ERR_ARG, "sb_prefill: T=%d must be a multiple of %d and <= max_len %d", T, kPrefillQBlock,
+                md->max_len);
+  if (md->head_dim != 128 || md->n_q % md->n_kv || (md->n_q / md->n_kv) * kPrefillQBlock > 64)
+    return fail(SB_ERR_CONFIG, "sb_prefill: needs head_dim 128 and n_q / n_kv <= 8");
+  // the blocks are spb streams each, the last one batch % spb streams if not zero
+  const int spb = prefill_streams_per_block(B, T);
+  const int rows = spb * T, tail = (B % spb) * T;
+  for (int l = 0; l < md->n_layers; ++l) {
+    const SbLayer& L = md->layers[l];
+    const SbLinear* lins[4] = {&L.qkv, &L.o, &L.gate_up, &L.down};
+    for (const SbLinear* x : lins) {
+      TcPlan pl;
+      if (!lin_ok(*x)) return fail(SB_ERR_ARG, "sb_prefill: layer %d: bad packed linear", l);
+      if (!tc_plan_for(*x, rows, pl) || (tail && !tc_plan_for(*x, tail, pl)))
+        return fail(SB_ERR_CONFIG, "sb_prefill: layer %d: the tensor-core GEMM does not serve blocks of %d / %d "
+                    "rows (no tile copy, or too few rows for this format)", l, rows, tail);
+    }
+  }
+  return 0;
+}
+
+extern "C" size_t sb_prefill_workspace_bytes(const SbModel* md, int32_t batch, int32_t T) {
+  if (!md || batch < 1 || T < 1) return 0;
+  return prefill_ws(md, batch, T, nullptr).total;
+}
+
+extern "C" int32_t sb_prefill_block_rows(const SbModel* md, int32_t batch, int32_t T) {
+  if (!md || batch < 1 || T < 1) return 0;
+  return prefill_streams_per_block(batch, T) * T;
+}
+
+extern "C" int sb_prefill(const SbModel* md, uint16_t* hidden, int32_t batch, int32_t T, const int32_t* prompt_len,
+                          uint16_t* q, uint16_t* attn, uint16_t* act, void* workspace, size_t workspace_bytes,
+                          sb_stream_t stream) {
+  SB_TRY(check_prefill(md, batch, T));
+  if (!hidden || !q || !attn || !act || !workspace) return fail(SB_ERR_ARG, "sb_prefill: buffer missing");
+  const PrefillWs ws = prefill_ws(md, batch, T, workspace);
+  if (workspace_bytes < ws.total)
+    return fail(SB_ERR_ARG, "sb_prefill: workspace too small (%zu < %zu)", workspace_bytes, ws.total);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int H = md->hidden, NQ = md->n_q * 128, spb = prefill_streams_per_block(batch, T);
+  const size_t head_rows = static_cast<size_t>(md->n_kv) * md->max_len * 128;  // cache elements per stream
+  const size_t tcb = workspace_bytes - 256;
+  SB_TRY(set_ctrl_launch(ws.ctrl, 0, T, s));
+  for (int l = 0; l < md->n_layers; ++l) {
+    const SbLayer& L = md->layers[l];
+    // q/k/v: RMSNorm prologue, RoPE (positions 0..T-1) + K/V written to cache slots 0..T-1
+    for (int b0 = 0; b0 < batch; b0 += spb) {
+      const int nb = batch - b0 < spb ? batch - b0 : spb;
+      const size_t r0 = static_cast<size_t>(b0) * T;
+      GemvParams p = base_params(L.qkv, nb * T);
+      p.pro = PRO_RMSNORM;
+      p.x = hidden + r0 * H;
+      p.norm_w = L.in_norm;
+      p.eps = md->eps;
+      p.epi = EPI_QKV;
+      p.q_out = q + r0 * NQ;
+      p.k_cache = L.k_cache + b0 * head_rows;
+      p.v_cache = L.v_cache + b0 * head_rows;
+      p.n_q = md->n_q;
+      p.n_kv = md->n_kv;
+      p.max_len = md->max_len;
+      p.m_per = T;
+      p.cos_tab = md->rope_cos;
+      p.sin_tab = md->rope_sin;
+      p.rope_max = md->rope_max_pos;
+      p.ctrl = ws.ctrl;
+      SB_TRY(run_linear(L.qkv, p, ws.tc, tcb, false, s));
+    }
+    // causal attention over the right-padded prompts: query blocks of kPrefillQBlock tokens
+    AttnParams a;
+    memset(&a, 0, sizeof(a));
+    a.q = q;
+    a.k_cache = L.k_cache;
+    a.v_cache = L.v_cache;
+    a.out = attn;
+    a.n_q = md->n_q;
+    a.n_kv = md->n_kv;
+    a.max_len = md->max_len;
+    a.m_per = kPrefillQBlock;
+    a.qblocks = T / kPrefillQBlock;
+    a.attn_mult = md->attn_mult;
+    a.ctrl = ws.ctrl;
+    a.prompt_len = prompt_len;
+    a.split = 1;
+    a.chunk_cap = attn_key_capacity(T, 1);
+    a.slots = 2;
+    a.cache_rows = static_cast<long long>(md->max_batch) * md->n_kv * md->max_len;
+    const int rc = attn_launch(a, batch, false, s);
+    if (rc == SB_ERR_CONFIG) return fail(rc, "sb_prefill: no attention configuration for T=%d", T);
+    if (rc != 0) return fail(rc, "sb_prefill: attention launch: %s", cudaGetErrorString((cudaError_t)rc));
+    // per block of streams: o (+ residual), gate/up (RMSNorm, SwiGLU), down (+ residual)
+    for (int b0 = 0; b0 < batch; b0 += spb) {
+      const int nb = batch - b0 < spb ? batch - b0 : spb;
+      const size_t r0 = static_cast<size_t>(b0) * T;
+      GemvParams p = base_params(L.o, nb * T);
+      p.pro = PRO_NONE;
+      p.x = attn + r0 * NQ;
+      p.epi = EPI_RESID;
+      p.y = hidden + r0 * H;
+      p.res_mult = md->res_mult;
+      SB_TRY(run_linear(L.o, p, ws.tc, tcb, false, s));
+      p = base_params(L.gate_up, nb * T);
+      p.pro = PRO_RMSNORM;
+      p.x = hidden + r0 * H;
+      p.norm_w = L.post_norm;
+      p.eps = md->eps;
+      p.epi = EPI_SWIGLU;
+      p.y = act;
+      SB_TRY(run_linear(L.gate_up, p, ws.tc, tcb, false, s));
+      p = base_params(L.down, nb * T);
+      p.pro = PRO_NONE;
+      p.x = act;
+      p.epi = EPI_RESID;
+      p.y = hidden + r0 * H;
+      p.res_mult = md->res_mult;
+      SB_TRY(run_linear(L.down, p, ws.tc, tcb, false, s));
+    }
+  }
+  return 0;
 }
 
 int sb_dequant_f32(const SbLinear* lin, float* out, sb_stream_t stream) {

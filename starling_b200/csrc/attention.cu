@@ -135,7 +135,8 @@ __global__ void __launch_bounds__(256, 2)
   uint8_t* smem = smem_raw + ((1024 - (su32(smem_raw) & 1023)) & 1023);
   const int split = p.split;
   const int rank = split > 1 ? static_cast<int>(cg::this_cluster().block_rank()) : 0;
-  const int kvh = blockIdx.y, b = blockIdx.z;
+  // z = stream * qblocks + query block; q / out rows of the block start at z * m_per
+  const int kvh = blockIdx.y, zb = blockIdx.z, b = zb / p.qblocks, qblk = zb % p.qblocks;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, c = lane & 3;
   const int G = p.n_q / p.n_kv;
@@ -157,7 +158,7 @@ __global__ void __launch_bounds__(256, 2)
 
   // ---- this CTA's tiles (device values that are stable before the wait: the
   // slot and the lengths were written by kernels that precede the q/k/v GEMM)
-  const int slot = p.ctrl[SB_CTRL_SLOT];
+  const int slot = p.ctrl[SB_CTRL_SLOT] + qblk * p.m_per;
   const int pad_len = p.ctrl[SB_CTRL_PADLEN];
   int kv_len = slot + p.m_per;
   kv_len = kv_len > p.max_len ? p.max_len : kv_len;
@@ -211,7 +212,7 @@ __global__ void __launch_bounds__(256, 2)
   for (int i = tid; i < R * 64; i += blockDim.x) {
     const int r = i >> 6, d2 = (i & 63) * 2;
     const int mi = r / G, gi = r % G;
-    const size_t t = static_cast<size_t>(b) * p.m_per + mi;
+    const size_t t = static_cast<size_t>(zb) * p.m_per + mi;
     *reinterpret_cast<uint32_t*>(qb + r * 136 + d2) =
         *reinterpret_cast<const uint32_t*>(p.q + t * p.n_q * 128 + (kvh * G + gi) * 128 + d2);
   }
@@ -409,7 +410,7 @@ __global__ void __launch_bounds__(256, 2)
       for (int q = 0; q < split; ++q) s += split > 1 ? cg::this_cluster().map_shared_rank(outp, q)[i] : outp[i];
       const int r = i >> 7, dd = i & 127;
       const int mi = r / G, gi = r % G;
-      const size_t t = static_cast<size_t>(b) * p.m_per + mi;
+      const size_t t = static_cast<size_t>(zb) * p.m_per + mi;
       p.out[t * p.n_q * 128 + (kvh * G + gi) * 128 + dd] = f_to_bf16_bits(s);
     }
   }
@@ -496,7 +497,7 @@ int attn_launch(const AttnParams& p, int batch, bool pdl, cudaStream_t stream) {
     configured[ki] |= 1u << dev;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(p.split, p.n_kv, batch);
+  cfg.gridDim = dim3(p.split, p.n_kv, batch * p.qblocks);
   cfg.blockDim = dim3(256);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;

@@ -17,6 +17,8 @@ struct AttnParams {
   int chunk_cap;              // keys per CTA at most: attn_key_capacity(max_len, split)
   int slots;                  // ring slots of 64 keys (K or V)
   long long cache_rows;       // max_batch * n_kv * max_len (rows of 128 of each cache)
+  int qblocks;                // query blocks of m_per tokens per stream: block qb has its tokens
+                              // at cache slots ctrl[SLOT] + qb * m_per + (0..m_per-1) (prefill); 1 otherwise
 };
 
 int attn_tile_keys(int split);

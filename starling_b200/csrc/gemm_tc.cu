@@ -125,7 +125,7 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t
 }
 template <int FMT>
 __device__ __forceinline__ void tc_mma(uint32_t tmem, uint64_t ad, uint64_t bd, uint32_t idesc, uint32_t acc) {
-  if constexpr (FMT == SB_FMT_BF16) {
+  if constexpr (tc_bf16_operand(FMT)) {
     asm volatile(
         "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
         " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
@@ -205,12 +205,12 @@ __global__ void __launch_bounds__(kPrepThreads) k_tc_prep(const __grid_constant_
   const int n16 = K / 16;
   const size_t kb_bytes = static_cast<size_t>(np) * 128;
   // token tile m / mp holds rows mp * tile .. of the operand, each tile [kb][np/8][8][8][16 B]
-  uint8_t* xt = xq + static_cast<size_t>(m / mp) * (K * (FMT == SB_FMT_BF16 ? 2 : 1) / 128) * kb_bytes;
+  uint8_t* xt = xq + static_cast<size_t>(m / mp) * (K * (tc_bf16_operand(FMT) ? 2 : 1) / 128) * kb_bytes;
   const int ml = m % mp;  // row of the token within its tile
   auto off = [&](int n, int c) -> size_t {  // 16-byte chunk c (along K bytes) of B-operand row n
     return static_cast<size_t>(c >> 3) * kb_bytes + static_cast<size_t>(n >> 3) * 1024 + (c & 7) * 128 + (n & 7) * 16;
   };
-  constexpr int CPE = FMT == SB_FMT_BF16 ? 2 : 1;  // 16-byte output chunks per 16 elements and term
+  constexpr int CPE = tc_bf16_operand(FMT) ? 2 : 1;  // 16-byte output chunks per 16 elements and term
   pdl_wait();
   pdl_launch();
   if (m >= p.m) {
@@ -269,7 +269,7 @@ __global__ void __launch_bounds__(kPrepThreads) k_tc_prep(const __grid_constant_
       }
     }
   }
-  if constexpr (FMT == SB_FMT_BF16) {
+  if constexpr (tc_bf16_operand(FMT)) {
 #pragma unroll
     for (int j = 0; j < kPrepChunks; ++j) {
       const int c16 = tid + j * kPrepThreads;
@@ -528,8 +528,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
 static const int kSMs = 148;
 static const size_t kTcSmem = 220 * 1024;
 
-static int elem_bytes(int fmt) { return fmt == SB_FMT_BF16 ? 2 : 1; }
-static int pad_rows(int fmt, int m) { return fmt == SB_FMT_BF16 ? (m + 15) / 16 * 16 : (m + 7) / 8 * 8; }
+static int elem_bytes(int fmt) { return tc_bf16_operand(fmt) ? 2 : 1; }
+static int pad_rows(int fmt, int m) { return tc_bf16_operand(fmt) ? (m + 15) / 16 * 16 : (m + 7) / 8 * 8; }
 
 // token rows above 128 are processed in tiles of 128 (one launch)
 static int tile_rows(int fmt, int m) { return m > 128 ? 128 : pad_rows(fmt, m); }
@@ -617,7 +617,7 @@ static int tc_launch_t(const GemvParams& p0, const void* w_tc, void* operand, co
   a.xq = xq;
   a.xshift = xshift;
   // instruction descriptor: D f32, A/B K-major, A/B e4m3 (f8f6f4) or bf16 (f16), N, M = 128
-  const uint32_t ab = FMT == SB_FMT_BF16 ? 1u : 0u;
+  const uint32_t ab = tc_bf16_operand(FMT) ? 1u : 0u;
   a.idesc = (1u << 4) | (ab << 7) | (ab << 10) | (static_cast<uint32_t>(pl.np >> 3) << 17) | ((128u >> 4) << 24);
   a.mp = pl.mp;
   a.np = pl.np;
@@ -649,6 +649,8 @@ int tc_launch(const GemvParams& p, const void* w_tc, void* operand, const TcPlan
   switch (fmt) {
     case SB_FMT_BF16: return tc_launch_t<SB_FMT_BF16>(p, w_tc, operand, pl, pdl, stream);
     case SB_FMT_FP8: return tc_launch_t<SB_FMT_FP8>(p, w_tc, operand, pl, pdl, stream);
+    case SB_FMT_INT8: return tc_launch_t<SB_FMT_INT8>(p, w_tc, operand, pl, pdl, stream);
+    case SB_FMT_NVFP4: return tc_launch_t<SB_FMT_NVFP4>(p, w_tc, operand, pl, pdl, stream);
   }
   return SB_ERR_ARG;
 }

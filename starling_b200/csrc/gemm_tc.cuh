@@ -5,8 +5,12 @@
 
 namespace sb {
 
-// Formats with a tensor-core tile copy of the weight (SbLinear.w_tc).
-__host__ __device__ inline bool tc_format(int fmt) { return fmt == SB_FMT_FP8 || fmt == SB_FMT_BF16; }
+// Every format can carry a tensor-core tile copy of the weight (SbLinear.w_tc):
+// FP8 as its e4m3 bytes (the activations then enter as two e4m3 terms), the
+// others as bf16 values (bf16 weights; INT8 codes; NVFP4 code x block scale,
+// all exact in bf16), their fp32 row / tensor scale applied in the epilogue.
+__host__ __device__ inline bool tc_format(int fmt) { return fmt >= SB_FMT_BF16 && fmt <= SB_FMT_NVFP4; }
+__host__ __device__ constexpr bool tc_bf16_operand(int fmt) { return fmt != SB_FMT_FP8; }
 
 // Geometry of one launch.
 struct TcPlan {

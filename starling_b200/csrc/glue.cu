@@ -291,3 +291,19 @@ int argmax_launch(const uint16_t* x, int rows, int n, int64_t* out, cudaStream_t
 }
 
 }  // namespace sb
+
+namespace sb {
+
+// Control block of a prefill: cache slot of token 0, padded prompt length, the rest zero.
+__global__ void k_set_ctrl(int32_t* ctrl, int slot, int padlen) {
+  const int i = threadIdx.x;
+  if (i < SB_CTRL_WORDS) ctrl[i] = i == SB_CTRL_SLOT ? slot : (i == SB_CTRL_PADLEN ? padlen : 0);
+}
+
+int set_ctrl_launch(int32_t* ctrl, int slot, int padlen, cudaStream_t s) {
+  note_launch();
+  k_set_ctrl<<<1, 32, 0, s>>>(ctrl, slot, padlen);
+  return cudaGetLastError();
+}
+
+}  // namespace sb

@@ -14,7 +14,8 @@ namespace sb {
 
 // v[i]: dot product of this lane's row and token m0 + i, activation scaling
 // undone, weight scale not yet applied.  row_ok: the row exists (row < n).
-// tok0: first token of the token tile (the store epilogue only; 0 otherwise).
+// tok0: first token of the token tile (token m0 + i of the call is row
+// tok0 + m0 + i of the outputs; argmax needs tok0 = 0).
 // Must be called by full warps with warp-uniform m0.  ARGMAX keeps a running
 // best per (warp, token) in wb_val/wb_idx[warp * 128 + m].
 template <int FMT, int CNT>
@@ -37,11 +38,11 @@ __device__ __forceinline__ void tc_epi(const GemvParams& p, int row, bool row_ok
     float h[CNT];
 #pragma unroll
     for (int i = 0; i < CNT; ++i)
-      h[i] = (row_ok && m0 + i < M) ? u16_to_f(p.y[static_cast<size_t>(m0 + i) * p.n + row]) : 0.f;
+      h[i] = (row_ok && m0 + i < M) ? u16_to_f(p.y[static_cast<size_t>(tok0 + m0 + i) * p.n + row]) : 0.f;
 #pragma unroll
     for (int i = 0; i < CNT; ++i)
       if (row_ok && m0 + i < M)
-        p.y[static_cast<size_t>(m0 + i) * p.n + row] = f_to_bf16_bits(h[i] + bf(p.res_mult * bf(v[i])));
+        p.y[static_cast<size_t>(tok0 + m0 + i) * p.n + row] = f_to_bf16_bits(h[i] + bf(p.res_mult * bf(v[i])));
   } else if (p.epi == EPI_SWIGLU) {
     // act = bf16(bf16(silu(gate)) * up) (llm_kernels.py:252-260); gate row 2i, up row 2i+1
     const int inter = p.n / 2;
@@ -51,7 +52,7 @@ __device__ __forceinline__ void tc_epi(const GemvParams& p, int row, bool row_ok
       if (row_ok && !(row & 1) && m0 + i < M) {
         const float gv = bf(v[i]);
         const float sg = bf(gv / (1.f + expf(-gv)));
-        p.y[static_cast<size_t>(m0 + i) * inter + row / 2] = f_to_bf16_bits(sg * bf(up));
+        p.y[static_cast<size_t>(tok0 + m0 + i) * inter + row / 2] = f_to_bf16_bits(sg * bf(up));
       }
     }
   } else if (p.epi == EPI_QKV) {
@@ -69,7 +70,7 @@ __device__ __forceinline__ void tc_epi(const GemvParams& p, int row, bool row_ok
       cs[i] = 0.f;
       sn[i] = 0.f;
       if (is_qk && row_ok && m0 + i < M) {
-        const int m = m0 + i, b = m / p.m_per, mi = m % p.m_per;
+        const int m = tok0 + m0 + i, b = m / p.m_per, mi = m % p.m_per;
         int pos = slot_base + mi - (p.rope_off ? p.rope_off[b] : 0);
         pos = pos < 0 ? 0 : (pos >= p.rope_max ? p.rope_max - 1 : pos);
         cs[i] = u16_to_f(p.cos_tab[pos * 64 + j]);
@@ -79,8 +80,8 @@ __device__ __forceinline__ void tc_epi(const GemvParams& p, int row, bool row_ok
 #pragma unroll
     for (int i = 0; i < CNT; ++i) {
       const float other = __shfl_xor_sync(0xffffffffu, v[i], 1);
-      const int m = m0 + i;
-      if (!row_ok || m >= M) continue;
+      if (!row_ok || m0 + i >= M) continue;
+      const int m = tok0 + m0 + i;
       const int b = m / p.m_per, mi = m % p.m_per;
       const int slot = slot_base + mi;
       const bool slot_ok = slot >= 0 && slot < p.max_len;

@@ -249,16 +249,60 @@ class GraniteEngine:
 
     @torch.inference_mode()
     def prefill(self, inputs_embeds: torch.Tensor, prompt_lengths: Optional[torch.Tensor] = None,
-                chunk_streams: int = 8) -> torch.Tensor:
-        """Eager prefill over ``inputs_embeds`` (B, T, H) (before the x12
-        embedding multiplier), writing cache slots [0, T) of streams 0..B-1.
-        Mirrors ``GraniteModel.forward`` with a causal (+ right-padding) mask
-        (llm_mega.py:176-202, batched.py:222-276).  Returns the last real
-        position's hidden row per stream, before the final norm: (B, H)."""
-        d = self.dims
+                chunk_streams: int = 8, native: Optional[bool] = None) -> torch.Tensor:
+        """Prefill over ``inputs_embeds`` (B, T, H) (before the x12 embedding
+        multiplier), writing cache slots [0, T) of streams 0..B-1: the
+        ``GraniteModel.forward`` with a causal (+ right-padding) mask of
+        llm_mega.py:176-202 / batched.py:222-276.  Returns the last real
+        position's hidden row per stream, before the final norm: (B, H).
+
+        native=None: the library's ``sb_prefill`` when every projection has a
+        tensor-core tile copy that serves the shape, else the eager path below
+        (torch attention and glue, projections through ``sb_linear_ex``);
+        native=True requires the former, native=False forces the latter."""
         B, T, _ = inputs_embeds.shape
         if T >= self.max_cache_len:
             raise ValueError(f"prompt {T} >= max_cache_len {self.max_cache_len}")
+        if native is not False:
+            out = self._prefill_native(inputs_embeds, prompt_lengths, required=native is True)
+            if out is not None:
+                return out
+        return self._prefill_eager(inputs_embeds, prompt_lengths, chunk_streams)
+
+    def _prefill_native(self, inputs_embeds, prompt_lengths, required: bool):
+        d = self.dims
+        B, T, _ = inputs_embeds.shape
+        Tp = (T + 7) // 8 * 8  # sb_prefill takes whole query blocks of 8 positions
+        if Tp > self.max_cache_len or B > self.max_batch:
+            if required:
+                raise ValueError(f"native prefill needs T rounded to 8 ({Tp}) <= max_cache_len and B <= max_batch")
+            return None
+        dev = self.device
+        hidden = torch.zeros(B, Tp, d.hidden, dtype=BF16, device=dev)
+        hidden[:, :T] = inputs_embeds.to(dev, BF16) * d.emb_mult
+        pl = None
+        if prompt_lengths is not None:
+            pl = prompt_lengths.to(dev, torch.int32).contiguous()
+        elif Tp != T:
+            pl = torch.full((B,), T, dtype=torch.int32, device=dev)
+        m = C.byref(self.cmodel)
+        ws_bytes = int(self.lib.sb_prefill_workspace_bytes(m, B, Tp))
+        rows = int(self.lib.sb_prefill_block_rows(m, B, Tp))
+        q = torch.empty(B * Tp, d.n_q * d.head_dim, dtype=BF16, device=dev)
+        attn = torch.empty_like(q)
+        act = torch.empty(rows, d.inter, dtype=BF16, device=dev)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+        rc = self.lib.sb_prefill(m, ptr(hidden), B, Tp, ptr(pl), ptr(q), ptr(attn), ptr(act), ptr(ws), ws_bytes,
+                                 _lib.current_stream())
+        if rc == 1002 and not required:  # SB_ERR_CONFIG: a projection is not served by the tensor-core GEMM
+            return None
+        check(rc, "sb_prefill")
+        last = (pl.long() - 1) if pl is not None else torch.full((B,), T - 1, device=dev)
+        return hidden[torch.arange(B, device=dev), last, :].contiguous()
+
+    def _prefill_eager(self, inputs_embeds, prompt_lengths, chunk_streams):
+        d = self.dims
+        B, T, _ = inputs_embeds.shape
         dev = self.device
         hidden = inputs_embeds.to(dev, BF16) * d.emb_mult
         pl = None if prompt_lengths is None else prompt_lengths.to(dev).long()

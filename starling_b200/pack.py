@@ -20,8 +20,10 @@ dim ``j+64``) so that the GEMV epilogue holds both operands of each RoPE pair;
 ``gate_up`` interleaves gate row ``i`` (``2i``) and up row ``i`` (``2i+1``) for the
 SwiGLU epilogue.  Quantised fused matrices are quantised as one tensor.
 
-Tensor-core tile copy (``w_tc``, fp8 and bf16): the same packed rows as raw
-bytes (e4m3 codes / bf16), rows padded to a multiple of 128, cut into
+Tensor-core tile copy (``w_tc``): the same packed rows as raw bytes (e4m3
+codes for fp8; bf16 values otherwise: the weights, the int8 codes, or the
+nvfp4 code x block scale, all exact in bf16, with the row / tensor scale kept
+for the epilogue), rows padded to a multiple of 128, cut into
 128-row x 128-byte blocks, each block in the no-swizzle K-major canonical
 layout of ``tcgen05.mma``: byte ``(row, kbyte)`` of block ``(tile, kb)`` sits at
 ``rg*1024 + kc*128 + r*16 + b`` with ``row = 128*tile + 8*rg + r`` and
@@ -79,7 +81,14 @@ def _frag_order(q: torch.Tensor, kge: int) -> torch.Tensor:
     return v.reshape(-1)
 
 
-TC_FORMATS = ("fp8", "bf16")
+TC_FORMATS = ("fp8", "bf16", "int8", "nvfp4")
+
+
+def _bf16_rows(v: torch.Tensor) -> torch.Tensor:
+    """fp32 values exactly representable in bf16 [n, k] -> bf16 bytes [n, 2k]."""
+    b = v.to(torch.bfloat16)
+    assert torch.equal(b.float(), v), "tile-copy values must be exact in bf16"
+    return b.view(torch.int16).view(torch.uint8).reshape(v.shape[0], 2 * v.shape[1])
 
 
 def tc_tiles(rows: torch.Tensor) -> torch.Tensor:
@@ -124,14 +133,21 @@ def pack_matrix(w: torch.Tensor, fmt: str, tc: bool = False) -> PackedLinear:
     parts = quant.quantize(fmt, w)
     if fmt in ("fp8", "int8"):
         q, s = parts
+        if tc:  # fp8: the e4m3 bytes; int8: the integer codes as bf16 (exact)
+            w_tc = tc_tiles(q.view(torch.uint8)) if fmt == "fp8" else tc_tiles(_bf16_rows(q.float()))
+        else:
+            w_tc = None
         q = q.view(torch.uint8)
-        w_tc = tc_tiles(q) if tc else None
         if n_pad != n:
             q = torch.cat([q, torch.zeros(n_pad - n, k, dtype=torch.uint8, device=dev)])
             s = torch.cat([s, torch.ones(n_pad - n, dtype=torch.float32, device=dev)])
         packed = _frag_order(q, kge).contiguous()
         return PackedLinear(fmt, n, k, n_pad, packed, s.contiguous(), w_tc=w_tc)
     codes, sb, g = parts
+    w_tc = None
+    if tc:  # code x block scale as bf16 (<= 6 significant bits: exact); the tensor scale stays apart
+        cb = quant.e2m1_to_f32(codes).view(n, k // 16, 16) * quant.e4m3_to_f32(sb)[:, :, None]
+        w_tc = tc_tiles(_bf16_rows(cb.view(n, k)))
     if n_pad != n:
         codes = torch.cat([codes, torch.zeros(n_pad - n, k, dtype=torch.uint8, device=dev)])
         sb = torch.cat([sb, torch.zeros(n_pad - n, k // 16, dtype=torch.uint8, device=dev)])
@@ -139,7 +155,7 @@ def pack_matrix(w: torch.Tensor, fmt: str, tc: bool = False) -> PackedLinear:
     packed = (e[:, 0] | (e[:, 1] << 4)).contiguous()
     T, KG = n_pad // 16, k // 64
     sv = sb.reshape(T, 2, 8, KG, 4).permute(0, 3, 2, 4, 1).contiguous().view(-1)
-    return PackedLinear(fmt, n, k, n_pad, packed, sv, g)
+    return PackedLinear(fmt, n, k, n_pad, packed, sv, g, w_tc=w_tc)
 
 
 def rope_pair_perm(n_heads: int, head_dim: int = 128) -> torch.Tensor:

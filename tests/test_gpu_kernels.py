@@ -129,6 +129,20 @@ def test_linear_tensor_cores(fmt, n, k, m):
     _close_bf16(y.cpu(), ref)
 
 
+@pytest.mark.parametrize("fmt", ["int8", "nvfp4"])
+@pytest.mark.parametrize("n,k,m", [(2048, 2048, 65), (3072, 2048, 300), (1000, 1024, 1000), (2051, 512, 128)])
+def test_linear_tensor_cores_bf16_copy(fmt, n, k, m):
+    """INT8 / NVFP4 above 64 rows (prefill): tcgen05 GEMM on the bf16 tile copy
+    (codes, code x block scale), fp32 row / tensor scale in the epilogue."""
+    w = _w(n, k, seed=n + k + m)
+    x = torch.randn(m, k, generator=torch.Generator().manual_seed(6)).to(BF16)
+    p = _to_dev(pack.pack_matrix(w, fmt, tc=True))
+    p.w_tc = p.w_tc.cuda()
+    y = _linear_tc(p, x.cuda())
+    ref = (x.float() @ _oracle_dense(w, fmt).T).to(BF16)
+    _close_bf16(y.cpu(), ref)
+
+
 def test_linear_tensor_cores_wide_range_rows():
     """fp8 activation split: rows spanning many binades (and an all-zero row)
     still match the fp32 reference."""

@@ -108,20 +108,34 @@ def test_row_permutations():
     assert gu.tolist() == [0, 4, 1, 5, 2, 6, 3, 7]
 
 
-@pytest.mark.parametrize("fmt", ["bf16", "fp8"])
+def _bf16_bytes(v: np.ndarray) -> torch.Tensor:
+    t = torch.from_numpy(np.ascontiguousarray(v, dtype=np.float32)).to(torch.bfloat16)
+    assert torch.equal(t.float(), torch.from_numpy(np.ascontiguousarray(v, dtype=np.float32)))
+    return t.view(torch.int16).view(torch.uint8).reshape(v.shape[0], 2 * v.shape[1])
+
+
+@pytest.mark.parametrize("fmt", ["bf16", "fp8", "int8", "nvfp4"])
 def test_tensor_core_tile_layout(fmt):
     """w_tc: byte (row, kbyte) of block (tile, kb) at rg*1024 + kc*128 + r*16 + b
     (the no-swizzle K-major canonical layout of tcgen05.mma), padded rows zero,
-    holding the same (quantised) row bytes as the GEMV packing."""
+    holding the oracle's quantised rows: e4m3 bytes for fp8; bf16 values for
+    the others (the weights, the int8 codes, the nvfp4 code x block scale)."""
     n, k = 200, 256
     w = _w(n, k, seed=9)
     p = pack.pack_matrix(w, fmt, tc=True)
     assert p.w_tc is not None
     if fmt == "bf16":
         rows = w.view(torch.int16).view(torch.uint8).reshape(n, 2 * k)
-    else:
+    elif fmt == "fp8":
         q, _ = qr.quantize("fp8", w.float().numpy())
         rows = torch.from_numpy(q.view(np.uint8).copy()).reshape(n, k)
+    elif fmt == "int8":
+        q, _ = qr.quantize("int8", w.float().numpy())
+        rows = _bf16_bytes(q.astype(np.float32))
+    else:
+        codes, sb, _ = qr.quantize("nvfp4", w.float().numpy())
+        cb = qr.e2m1_decode(codes).reshape(n, k // 16, 16) * qr.e4m3_decode(sb)[:, :, None]
+        rows = _bf16_bytes(cb.reshape(n, k))
     kbytes = rows.shape[1]
     t = p.w_tc
     assert t.numel() == 256 * kbytes  # 200 rows -> 2 tiles of 128
@@ -138,4 +152,3 @@ def test_tensor_core_tile_layout(fmt):
         want = int(rows[row, kb_]) if row < n else 0
         assert int(t[off]) == want
     assert torch.equal(pack.tc_untile(t, n, kbytes), rows)
-    assert pack.pack_matrix(w, "nvfp4", tc=True).w_tc is None  # no tile copy for nvfp4
