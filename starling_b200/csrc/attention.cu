@@ -57,7 +57,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// 2D TMA tile load (no multicast) of box {64 dims, 64 keys} at (x, y).
+// 2D TMA tile load of one box (64 dims x tile keys) at (x, y) into this CTA's shared memory.
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, int x, int y, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
