@@ -84,7 +84,7 @@ __device__ __forceinline__ void ring_wait(uint64_t* bar, uint32_t parity, int32_
 }  // namespace
 
 template <int FMT, int KSW>
-__global__ void __launch_bounds__(512, 1) k_gemv_dec(const __grid_constant__ GemvParams p, int slots, int batch) {
+__global__ void __launch_bounds__(512, 2) k_gemv_dec(const __grid_constant__ GemvParams p, int slots, int batch) {
   constexpr int KGE = KG<FMT>::E;
   constexpr int KS = KGE / 16;
   constexpr int KPW = KSW / KS;  // kgroups per warp
@@ -331,9 +331,13 @@ bool gemv_dec_plan(int fmt, int n_tiles, int k, int m, DecPlan& pl) {
   const size_t wbytes = static_cast<size_t>(k / kge) * 512;
   const size_t sbytes = fmt == SB_FMT_NVFP4 ? static_cast<size_t>(k / 64) * 64 : 0;
   const size_t slot = (wbytes + sbytes + 127) & ~size_t(127);  // = dec_layout().slot_bytes
-  const int n_ctas = n_tiles < kSMs ? n_tiles : kSMs;
+  // Two CTAs per SM (16 warps per SM on independent tiles) when two rings of
+  // <= 88 KiB fit; else one CTA per SM with a deep ring.
+  const bool two = 2 * slot <= 88 * 1024 && W <= 8;
+  const int cap = two ? 2 * kSMs : kSMs;
+  const int n_ctas = n_tiles < cap ? n_tiles : cap;
   const int per = (n_tiles + n_ctas - 1) / n_ctas;
-  int slots = static_cast<int>(160 * 1024 / slot);
+  int slots = static_cast<int>((two ? 88 : 160) * 1024 / slot);
   if (slots > 2 * per) slots = 2 * per;
   if (slots > 16) slots = 16;
   if (slots < 2) return false;
@@ -341,7 +345,7 @@ bool gemv_dec_plan(int fmt, int n_tiles, int k, int m, DecPlan& pl) {
   // reduction buffers: batch * (W + 1) * 16 * m floats
   while (batch > 1 && static_cast<size_t>(batch) * (W + 1) * 16 * m * 4 > 48 * 1024) --batch;
   const size_t smem = dec_layout(wbytes + sbytes, slots, batch, W, m, ksw * 16).total;
-  if (smem > kDecSmem) return false;
+  if (smem > (two ? kDecSmem / 2 : kDecSmem)) return false;
   pl.ksw = ksw;
   pl.warps = W;
   pl.slots = slots;
