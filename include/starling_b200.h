@@ -103,7 +103,7 @@ typedef struct SbModel {
 #define SB_CTRL_PADLEN 1  /* padded prompt length T (right-padded batches) */
 #define SB_CTRL_ACCEPT 2  /* verify: accepted prefix length (output) */
 #define SB_CTRL_ERR 3     /* set non-zero by a kernel whose bounded wait expired (results invalid):
-                             1 = decode GEMV, 2 = tensor-core GEMM */
+                             1 = decode GEMV, 2 = tensor-core GEMM, 3 = attention, 4 = fused step */
 #define SB_CTRL_WORDS 8
 
 #define SB_MODE_DECODE 0  /* argmax -> out_ids[step], feed back to ids, slot += M */
@@ -150,8 +150,28 @@ size_t sb_workspace_bytes(const SbModel* model, int32_t tokens);
  * (src/starling/granite/multistep.py:157-188); with m > 1 it is the verify
  * forward SpeculativeDecoder._verify_step_fused (speculative.py:598-680) with
  * the acceptance compare of speculative.py:430-459 fused on device.
- * `step` indexes out_ids in DECODE mode.  About 5 launches per layer. */
+ * `step` indexes out_ids in DECODE mode.  About 5 launches per layer; with
+ * the environment variable STARLING_B200_STEP=fused, forwards of up to 8
+ * token rows (batch * m) that the fused step serves run as ONE cooperative
+ * launch instead (weights streamed through shared memory across layers, grid
+ * barriers between dependent phases; needs one weight format for every
+ * projection, hidden / inter 2048 / 8192 or 512 / 1024, max_len <= 1024 and
+ * batch * n_kv * ceil(max_len / 32) <= SMs). */
 int sb_decode_step(const SbModel* model, const SbState* state, int32_t step, sb_stream_t stream);
+
+/* sb_decode_step with the kernel path chosen by the caller:
+ * flags = 0 as sb_decode_step; SB_STEP_PER_OP: per-op kernels only;
+ * SB_STEP_FUSED: the fused step, or SB_ERR_CONFIG where it does not serve
+ * the forward.  No reference counterpart (choice between the two paths). */
+#define SB_STEP_PER_OP 1
+#define SB_STEP_FUSED 2
+int sb_decode_step_ex(const SbModel* model, const SbState* state, int32_t step, int32_t flags, sb_stream_t stream);
+/* 1 when the fused step serves (model, state), else 0 */
+int32_t sb_decode_step_fused_ok(const SbModel* model, const SbState* state);
+/* byte offset inside an SbState workspace of the fused step's scratch (its
+ * first 32-bit word is the grid-barrier counter; all its counters are zero
+ * between forwards), or SIZE_MAX when (model, tokens) has none */
+size_t sb_decode_step_scratch_offset(const SbModel* model, int32_t tokens);
 
 /* Launch ONE kernel of the decode step on its own (profiling / live timing
  * of a single kernel with the step's exact configuration): op = SB_OP_*,

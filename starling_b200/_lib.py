@@ -19,6 +19,7 @@ KGROUP_ELEMS = {"bf16": 16, "fp8": 32, "int8": 32, "nvfp4": 64}
 SB_CTRL_SLOT, SB_CTRL_PADLEN, SB_CTRL_ACCEPT, SB_CTRL_ERR, SB_CTRL_WORDS = 0, 1, 2, 3, 8
 SB_MODE_DECODE, SB_MODE_VERIFY, SB_MODE_FIRST = 0, 1, 2
 SB_OP_QKV, SB_OP_ATTN, SB_OP_O, SB_OP_GATE_UP, SB_OP_DOWN, SB_OP_LM_HEAD = range(6)
+SB_STEP_PER_OP, SB_STEP_FUSED = 1, 2
 
 vp = C.c_void_p
 
@@ -66,7 +67,8 @@ EXPORTS = [
     "sb_linear", "sb_dequant_f32", "sb_dequant_bf16", "sb_rmsnorm", "sb_silu_mul",
     "sb_residual_scale", "sb_rope", "sb_argmax_bf16", "sb_attention", "sb_decode_op",
     "sb_lm_head_argmax_static", "sb_linear_ex", "sb_linear_workspace_bytes", "sb_launch_count",
-    "sb_prefill", "sb_prefill_workspace_bytes", "sb_prefill_block_rows",
+    "sb_prefill", "sb_prefill_workspace_bytes", "sb_prefill_block_rows", "sb_decode_step_ex",
+    "sb_decode_step_fused_ok", "sb_decode_step_scratch_offset",
 ]
 
 
@@ -98,6 +100,11 @@ def load() -> C.CDLL:
     lib.sb_workspace_bytes.restype = C.c_size_t
     lib.sb_workspace_bytes.argtypes = [C.POINTER(SbModel), C.c_int32]
     lib.sb_decode_step.argtypes = [C.POINTER(SbModel), C.POINTER(SbState), C.c_int32, vp]
+    lib.sb_decode_step_ex.argtypes = [C.POINTER(SbModel), C.POINTER(SbState), C.c_int32, C.c_int32, vp]
+    lib.sb_decode_step_fused_ok.argtypes = [C.POINTER(SbModel), C.POINTER(SbState)]
+    lib.sb_decode_step_fused_ok.restype = C.c_int32
+    lib.sb_decode_step_scratch_offset.argtypes = [C.POINTER(SbModel), C.c_int32]
+    lib.sb_decode_step_scratch_offset.restype = C.c_size_t
     lib.sb_lm_head_argmax.argtypes = [C.POINTER(SbModel), C.POINTER(SbState), C.c_int32, vp]
     lib.sb_lm_head_argmax_static.argtypes = [C.POINTER(SbModel), C.POINTER(SbState), C.c_int32, vp]
     lib.sb_attention.argtypes = [C.POINTER(SbModel), C.POINTER(SbState), C.c_int32, vp]

@@ -21,6 +21,7 @@
 #include "gemm_tc.cuh"
 #include "gemv.cuh"
 #include "glue.cuh"
+#include "step.cuh"
 
 #include <atomic>
 
@@ -191,9 +192,9 @@ static LmWork lm_work(const SbModel* md, int tokens, void* base) {
   return w;
 }
 
-// Workspace = [lm_head argmax partials | tensor-core operand scratch].
+// Workspace = [lm_head argmax partials | tensor-core operand scratch | fused-step scratch].
 struct WsLayout {
-  size_t lm_bytes, tc_off, tc_bytes, total;
+  size_t lm_bytes, tc_off, tc_bytes, step_off, step_bytes, total;
 };
 static size_t tc_scratch_need(const SbLinear& l, int tokens) {
   TcPlan pl;
@@ -214,6 +215,9 @@ static WsLayout ws_layout(const SbModel* md, int tokens) {
   }
   w.tc_bytes = need;
   w.total = need ? w.tc_off + need : w.lm_bytes;
+  w.step_bytes = md->n_q > 0 ? step_ws_bytes(md, tokens) : 0;
+  w.step_off = (w.total + 255) & ~size_t(255);
+  if (w.step_bytes) w.total = w.step_off + w.step_bytes;
   return w;
 }
 // The state's workspace must hold ws_layout().total bytes; tc scratch is
@@ -394,10 +398,51 @@ size_t sb_workspace_bytes(const SbModel* md, int32_t tokens) {
   return ws_layout(md, tokens).total;
 }
 
+// sb_decode_step's default path: the per-op kernels; STARLING_B200_STEP=fused
+// selects the fused step wherever it serves the forward.
+static bool use_step_kernel() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("STARLING_B200_STEP");
+    v = (e && strcmp(e, "fused") == 0) ? 1 : 0;
+  }
+  return v == 1;
+}
+
+size_t sb_decode_step_scratch_offset(const SbModel* md, int32_t tokens) {
+  if (!md || tokens < 1) return static_cast<size_t>(-1);
+  const WsLayout w = ws_layout(md, tokens);
+  return w.step_bytes ? w.step_off : static_cast<size_t>(-1);
+}
+
+int32_t sb_decode_step_fused_ok(const SbModel* md, const SbState* st) {
+  if (!md || !st || check_state(md, st) != 0) return 0;
+  StepPlan pl;
+  return step_plan(md, st, pl, nullptr) ? 1 : 0;
+}
+
 int sb_decode_step(const SbModel* md, const SbState* st, int32_t step, sb_stream_t stream) {
+  return sb_decode_step_ex(md, st, step, use_step_kernel() ? 0 : SB_STEP_PER_OP, stream);
+}
+
+int sb_decode_step_ex(const SbModel* md, const SbState* st, int32_t step, int32_t flags, sb_stream_t stream) {
   SB_TRY(check_state(md, st));
   if (!md->layers || md->n_layers < 1) return fail(SB_ERR_ARG, "no layers");
+  if ((flags & SB_STEP_PER_OP) && (flags & SB_STEP_FUSED)) return fail(SB_ERR_ARG, "conflicting step flags");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (!(flags & SB_STEP_PER_OP)) {
+    StepPlan pl;
+    const char* why = "";
+    if (step_plan(md, st, pl, &why)) {
+      const WsLayout w = ws_layout(md, st->batch * st->m);
+      if (st->workspace_bytes < w.total)
+        return fail(SB_ERR_ARG, "workspace too small (%zu < %zu)", st->workspace_bytes, w.total);
+      const int rc = step_launch(md, st, step, static_cast<char*>(st->workspace) + w.step_off, pl, s);
+      if (rc != 0) return fail(rc, "fused step launch: %s", rc < 1000 ? cudaGetErrorString((cudaError_t)rc) : "config");
+      return 0;
+    }
+    if (flags & SB_STEP_FUSED) return fail(SB_ERR_CONFIG, "the fused step does not serve this forward: %s", why);
+  }
   for (int l = 0; l < md->n_layers; ++l)
     for (int op = SB_OP_QKV; op <= SB_OP_DOWN; ++op) SB_TRY(launch_op(md, st, l, op, step, s));
   return launch_op(md, st, 0, SB_OP_LM_HEAD, step, s);

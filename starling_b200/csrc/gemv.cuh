@@ -60,6 +60,10 @@ struct GemvParams {
   int32_t* finished;
   int64_t eos_id;
   int64_t pad_id;
+  // optional shared-memory copies (fused step, step.cu); null elsewhere
+  const uint16_t* rope_cache;  // EPI_QKV: [m][cos 64 | sin 64] at each token's position
+  uint16_t* resid_cache;       // EPI_RESID: [m][rc_stride] rows rc_row0.. of y, kept in step with y
+  int rc_stride, rc_row0;
 };
 
 template <int FMT>

@@ -10,31 +10,37 @@ namespace sb {
 // last block (argmax keeps a running best per token across blocks).  Run by
 // the nthr (a multiple of 32) threads tid = 0..nthr-1 of the block; it has no
 // barrier inside.
-template <int FMT>
+// EPIC >= 0 fixes the epilogue at compile time (only that branch is
+// generated); -1 dispatches on p.epi.
+template <int FMT, int EPIC = -1>
 __device__ __forceinline__ void gemv_epilogue(const GemvParams& p, const float* tot, int row0, int nrow, int M,
                                               int* s_best, float* s_bval, bool first, bool last, int tid, int nthr) {
   const int lane = tid & 31, warp = tid >> 5, W = nthr >> 5;
+  const int epi = EPIC >= 0 ? EPIC : p.epi;
   auto fin = [&](int lrow, int m) -> float {
     float v = tot[lrow * M + m];
     if (FMT == SB_FMT_NVFP4) v *= p.gscale;
     if (FMT == SB_FMT_FP8 || FMT == SB_FMT_INT8) v *= reinterpret_cast<const float*>(p.scale)[row0 + lrow];
     return v;
   };
-  if (p.epi == EPI_STORE) {
+  if (epi == EPI_STORE) {
     for (int i = tid; i < nrow * M; i += nthr) {
       const int m = i / nrow, lrow = i % nrow, row = row0 + lrow;
       if (row < p.n) p.y[static_cast<size_t>(m) * p.n + row] = f_to_bf16_bits(fin(lrow, m));
     }
-  } else if (p.epi == EPI_RESID) {
+  } else if (epi == EPI_RESID) {
     // hidden = hidden + bf16(res_mult * bf16(y))   (llm_kernels.py:306-313)
     for (int i = tid; i < nrow * M; i += nthr) {
       const int m = i / nrow, lrow = i % nrow, row = row0 + lrow;
       if (row < p.n) {
         uint16_t* hp = p.y + static_cast<size_t>(m) * p.n + row;
-        *hp = f_to_bf16_bits(u16_to_f(*hp) + bf(p.res_mult * bf(fin(lrow, m))));
+        uint16_t* cp = p.resid_cache ? p.resid_cache + m * p.rc_stride + (row - p.rc_row0) : nullptr;
+        const uint16_t nv = f_to_bf16_bits(u16_to_f(cp ? *cp : __ldcg(hp)) + bf(p.res_mult * bf(fin(lrow, m))));
+        *hp = nv;
+        if (cp) *cp = nv;
       }
     }
-  } else if (p.epi == EPI_SWIGLU) {
+  } else if (epi == EPI_SWIGLU) {
     // act = bf16(bf16(silu(gate)) * up)   (llm_kernels.py:252-260); rows interleave gate/up
     const int inter = p.n / 2, np = nrow / 2;
     for (int i = tid; i < np * M; i += nthr) {
@@ -46,7 +52,7 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams& p, const float* 
         p.y[static_cast<size_t>(m) * inter + row / 2] = f_to_bf16_bits(sg * uv);
       }
     }
-  } else if (p.epi == EPI_QKV) {
+  } else if (epi == EPI_QKV) {
     // q/k: RoPE with each product rounded to bf16 (llm_mega.py:539-543); k/v
     // to cache slot ctrl[SLOT] + token (StaticLayer.update, cache_utils.py:308-335)
     const int qk_rows = (p.n_q + p.n_kv) * 128;
@@ -65,8 +71,8 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams& p, const float* 
         pos = pos < 0 ? 0 : (pos >= p.rope_max ? p.rope_max - 1 : pos);
         const float x1 = bf(fin(lrow, m));
         const float x2 = bf(fin(lrow + 1, m));
-        const float cs = u16_to_f(p.cos_tab[pos * 64 + j]);
-        const float sn = u16_to_f(p.sin_tab[pos * 64 + j]);
+        const float cs = u16_to_f(p.rope_cache ? p.rope_cache[m * 128 + j] : p.cos_tab[pos * 64 + j]);
+        const float sn = u16_to_f(p.rope_cache ? p.rope_cache[m * 128 + 64 + j] : p.sin_tab[pos * 64 + j]);
         const uint16_t o1 = f_to_bf16_bits(bf(x1 * cs) - bf(x2 * sn));
         const uint16_t o2 = f_to_bf16_bits(bf(x2 * cs) + bf(x1 * sn));
         if (head < p.n_q) {
@@ -83,7 +89,7 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams& p, const float* 
             f_to_bf16_bits(fin(lrow, m));
       }
     }
-  } else if (p.epi == EPI_ARGMAX) {
+  } else if (epi == EPI_ARGMAX) {
     // logits = bf16(bf16(y) * (1/logits_scaling)); running (value, index) best
     for (int m = warp; m < M; m += W) {
       float bv = first ? -INFINITY : s_bval[m];

@@ -200,11 +200,24 @@ class GraniteEngine:
         return EngineState(self, batch, m, mode, **kw)
 
     # ---- native calls ----------------------------------------------------- #
+    # decode-step kernel path: "auto" (the library's default: per-op kernels,
+    # or the fused one-launch step with STARLING_B200_STEP=fused), "fused"
+    # (required), "prefer_fused" (fused where it serves the forward) or "ops"
+    step_path = "auto"
+
     def decode_step(self, st: EngineState, step: int = 0) -> None:
         if not 0 <= step < st.out_ids.numel() // max(st.batch, st.m):
             raise ValueError(f"step {step} outside the state's output ring")
-        check(self.lib.sb_decode_step(C.byref(self.cmodel), C.byref(st.c), int(step), _lib.current_stream()),
-              "sb_decode_step")
+        path = self.step_path
+        if path == "prefer_fused":
+            path = "fused" if self.fused_step_ok(st) else "ops"
+        flags = {"auto": 0, "ops": _lib.SB_STEP_PER_OP, "fused": _lib.SB_STEP_FUSED}[path]
+        check(self.lib.sb_decode_step_ex(C.byref(self.cmodel), C.byref(st.c), int(step), flags,
+                                         _lib.current_stream()), "sb_decode_step")
+
+    def fused_step_ok(self, st: EngineState) -> bool:
+        """Whether the one-launch fused step serves forwards of this state."""
+        return bool(self.lib.sb_decode_step_fused_ok(C.byref(self.cmodel), C.byref(st.c)))
 
     def lm_head_argmax(self, st: EngineState, step: int = 0) -> None:
         check(self.lib.sb_lm_head_argmax(C.byref(self.cmodel), C.byref(st.c), int(step), _lib.current_stream()),

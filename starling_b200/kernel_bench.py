@@ -1,10 +1,12 @@
 """Per-kernel timings of the decode path on one GPU (also the small cases the
 ncu summaries under profiles/ are captured on).
 
-    python -m starling_b200.kernel_bench ops --workload b48        # every op of a step, graphs of 40 launches
+    python -m starling_b200.kernel_bench ops --workload b48        # every op of a step, graphs of 40 launches;
+                                                                   # the whole step per-op and fused (one launch)
     python -m starling_b200.kernel_bench attention --batch 48      # sb_attention alone
     python -m starling_b200.kernel_bench linear --fmt fp8 --n 16384 --k 2048 --m 48
     python -m starling_b200.kernel_bench step --workload b48 --layers 4   # one eager step in NVTX range "step"
+    python -m starling_b200.kernel_bench step --workload b1 --path fused  # the one-launch fused step
 
 Workloads (same as bench.py): b48 = 48 streams, FP8 weights, prompts
 U[300,900]; b1 = one stream, NVFP4 weights, 320 prompt positions.  Weights are
@@ -85,13 +87,21 @@ def cmd_ops(a) -> None:
     lm = _graph_time(lambda: check(lib.sb_decode_op(C.byref(eng.cmodel), C.byref(st.c), 0, _lib.SB_OP_LM_HEAD, 0,
                                                     _lib.current_stream())))
     print(f"{a.workload} lm_head   {lm:9.2f} us")
-    st.set_slot(T, pad_len=T)
-    step = _graph_time(lambda: eng.decode_step(st, 0))
-    print(f"{a.workload} sum of ops {total + lm:9.1f} us; one graphed step {step:9.1f} us")
+    times = {}
+    for path in ("ops", "fused"):
+        eng.step_path = path
+        if path == "fused" and not eng.fused_step_ok(st):
+            continue
+        st.set_slot(T, pad_len=T)
+        times[path] = _graph_time(lambda: eng.decode_step(st, 0))
+    eng.step_path = "auto"
+    print(f"{a.workload} sum of ops {total + lm:9.1f} us; one graphed step: " +
+          ", ".join(f"{k} {v:.1f} us" for k, v in times.items()))
 
 
 def cmd_step(a) -> None:
     eng, st, T, d = _decoder(a.workload, a.layers)
+    eng.step_path = a.path
     for _ in range(2):
         eng.decode_step(st, 0)
     torch.cuda.synchronize()
@@ -170,6 +180,7 @@ def main(argv=None) -> None:
     p = sub.add_parser("step")
     p.add_argument("--workload", choices=list(WORKLOADS), default="b48")
     p.add_argument("--layers", type=int, default=4)
+    p.add_argument("--path", choices=["auto", "ops", "fused"], default="auto")
     p = sub.add_parser("attention")
     p.add_argument("--batch", type=int, default=48)
     p.add_argument("--reps", type=int, default=20)
