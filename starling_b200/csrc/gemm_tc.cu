@@ -211,6 +211,16 @@ __global__ void __launch_bounds__(kPrepThreads) k_tc_prep(const __grid_constant_
     return static_cast<size_t>(c >> 3) * kb_bytes + static_cast<size_t>(n >> 3) * 1024 + (c & 7) * 128 + (n & 7) * 16;
   };
   constexpr int CPE = tc_bf16_operand(FMT) ? 2 : 1;  // 16-byte output chunks per 16 elements and term
+  uint4 nw[kPrepChunks][2];  // RMSNorm weights: constant, read before waiting for the previous kernel
+  if (p.pro != PRO_NONE && m < p.m)
+#pragma unroll
+    for (int j = 0; j < kPrepChunks; ++j) {
+      const int c16 = tid + j * kPrepThreads;
+      if (c16 < n16) {
+        nw[j][0] = __ldg(reinterpret_cast<const uint4*>(p.norm_w + c16 * 16));
+        nw[j][1] = __ldg(reinterpret_cast<const uint4*>(p.norm_w + c16 * 16 + 8));
+      }
+    }
   pdl_wait();
   pdl_launch();
   if (m >= p.m) {
@@ -262,8 +272,8 @@ __global__ void __launch_bounds__(kPrepThreads) k_tc_prep(const __grid_constant_
       const int c16 = tid + j * kPrepThreads;
       if (c16 < n16) {
         float wn[16];
-        unpack8(*reinterpret_cast<const uint4*>(p.norm_w + c16 * 16), wn);
-        unpack8(*reinterpret_cast<const uint4*>(p.norm_w + c16 * 16 + 8), wn + 8);
+        unpack8(nw[j][0], wn);
+        unpack8(nw[j][1], wn + 8);
 #pragma unroll
         for (int e = 0; e < 16; ++e) f[j][e] = bf(wn[e] * bf(f[j][e] * rstd));
       }
@@ -309,7 +319,7 @@ __global__ void __launch_bounds__(kPrepThreads) k_tc_prep(const __grid_constant_
 }
 
 // ---- the GEMM ----------------------------------------------------------------------
-template <int FMT>
+template <int FMT, int EPI>
 __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant__ GemvParams p, const __grid_constant__ TcArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -358,7 +368,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
     mbar_fence_init();
   }
   if (warp == kMma) tmem_alloc(s_tmem, static_cast<uint32_t>(a.ncols));
-  if (p.epi == EPI_ARGMAX)
+  if constexpr (EPI == EPI_ARGMAX)
     for (int i = tid; i < (kTcEpiWarps + 2) * 128; i += blockDim.x) {
       wb_val[i] = -INFINITY;
       wb_idx[i] = 0x7fffffff;
@@ -430,6 +440,29 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
     // the 8-token chunks h, h + 2, ... with h = w / 4 ----
     pdl_wait();
     pdl_launch();
+    // bring the epilogue's global inputs into L1 while the main loop runs: the
+    // residual rows this CTA updates (first tile, or its rank's rows of the
+    // shared tile), and the RoPE rows at each token's position
+    if (a.mtiles > 1) {
+      // prefill token tiles: no prefetch
+    } else if constexpr (EPI == EPI_RESID) {
+      const int rp0 = tc_rows_per_rank(S);
+      const int ra = cid * 128 + (S > 1 ? q * rp0 : 0), nr = S > 1 ? rp0 : 128;
+      const int rb = min(ra + nr, p.n);
+      const int nseg = (rb - ra + 63) / 64;  // 128-byte lines of bf16 rows
+      for (int i = tid; i < M * nseg; i += kTcEpiWarps * 32)
+        if (ra < rb)
+          asm volatile("prefetch.global.L1 [%0];" ::"l"(p.y + static_cast<size_t>(i / nseg) * p.n + ra + (i % nseg) * 64));
+    } else if constexpr (EPI == EPI_QKV) {
+      const int slot_base = p.ctrl[SB_CTRL_SLOT];
+      for (int i = tid; i < M; i += kTcEpiWarps * 32) {
+        const int b = i / p.m_per;
+        int pos = slot_base + i % p.m_per - (p.rope_off ? p.rope_off[b] : 0);
+        pos = pos < 0 ? 0 : (pos >= p.rope_max ? p.rope_max - 1 : pos);
+        asm volatile("prefetch.global.L1 [%0];" ::"l"(p.cos_tab + static_cast<size_t>(pos) * 64));
+        asm volatile("prefetch.global.L1 [%0];" ::"l"(p.sin_tab + static_cast<size_t>(pos) * 64));
+      }
+    }
     float* s_unscale = reinterpret_cast<float*>(s_shift);  // 2^-shift per token of the tile: exact
     const int lq = warp & 3, h = warp >> 2;
     const int lrow = lq * 32 + lane;
@@ -463,7 +496,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
         }
         if (S == 1) {
           const int row = t * 128 + lrow;
-          tc_epi<FMT, 8>(p, row, row < p.n, v, m0, Mt, wb_val, wb_idx, warp, tok0);
+          tc_epi<FMT, 8, EPI>(p, row, row < p.n, v, m0, Mt, wb_val, wb_idx, warp, tok0);
         } else {
           // push this K partial to the rank that finishes the row (16-byte DSMEM stores)
           float* dst = cg::this_cluster().map_shared_rank(part, lrow / rp) + (q * rp + lrow % rp) * ms + m0;
@@ -497,10 +530,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
           v[3] += x4.w;
         }
       const int row = cid * 128 + r0 + lr;
-      tc_epi<FMT, 4>(p, row, ok && row < p.n, v, m0, M, wb_val, wb_idx, warp, 0);
+      tc_epi<FMT, 4, EPI>(p, row, ok && row < p.n, v, m0, M, wb_val, wb_idx, warp, 0);
     }
   }
-  if (p.epi == EPI_ARGMAX) {  // combine the warps' running bests (order-independent total order)
+  if constexpr (EPI == EPI_ARGMAX) {  // combine the warps' running bests (order-independent total order)
     __syncthreads();
     for (int m = tid; m < M; m += blockDim.x) {
       float bv = -INFINITY;
@@ -515,7 +548,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
     }
   }
   __syncthreads();
-  gemv_argmax_finish(p, s_best, s_bval, M, my_tiles > 0, s_flag);
+  if constexpr (EPI == EPI_ARGMAX) gemv_argmax_finish(p, s_best, s_bval, M, my_tiles > 0, s_flag);
   tc_fence_before();
   __syncthreads();
   if (warp == kMma) {
@@ -581,18 +614,30 @@ bool tc_plan(int fmt, int n, int k, int m, TcPlan& pl) {
   return true;
 }
 
-template <int FMT>
-static int tc_launch_t(const GemvParams& p0, const void* w_tc, void* operand, const TcPlan& pl, bool pdl,
-                       cudaStream_t stream) {
+template <int FMT, int EPI>
+static int gemm_configure() {
   int dev = 0;
   cudaGetDevice(&dev);
   static unsigned configured = 0;
   if (!(configured & (1u << dev))) {
-    cudaError_t e = cudaFuncSetAttribute(k_tc_gemm<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(k_tc_gemm<FMT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(kTcSmem));
     if (e != cudaSuccess) return e;
     configured |= 1u << dev;
   }
+  return 0;
+}
+
+template <int FMT, int EPI>
+static int gemm_launch(const cudaLaunchConfig_t& cfg, const GemvParams& p, const TcArgs& a) {
+  const int rc = gemm_configure<FMT, EPI>();
+  if (rc) return rc;
+  return cudaLaunchKernelEx(&cfg, k_tc_gemm<FMT, EPI>, p, a);
+}
+
+template <int FMT>
+static int tc_launch_t(const GemvParams& p0, const void* w_tc, void* operand, const TcPlan& pl, bool pdl,
+                       cudaStream_t stream) {
   GemvParams p = p0;
   p.n_ctas = pl.n_ctas;
   uint8_t* xq = static_cast<uint8_t*>(operand);
@@ -641,7 +686,14 @@ static int tc_launch_t(const GemvParams& p0, const void* w_tc, void* operand, co
   }
   cfg.numAttrs = na;
   note_launch();
-  return cudaLaunchKernelEx(&cfg, k_tc_gemm<FMT>, p, a);
+  switch (p.epi) {
+    case EPI_STORE: return gemm_launch<FMT, EPI_STORE>(cfg, p, a);
+    case EPI_QKV: return gemm_launch<FMT, EPI_QKV>(cfg, p, a);
+    case EPI_RESID: return gemm_launch<FMT, EPI_RESID>(cfg, p, a);
+    case EPI_SWIGLU: return gemm_launch<FMT, EPI_SWIGLU>(cfg, p, a);
+    case EPI_ARGMAX: return gemm_launch<FMT, EPI_ARGMAX>(cfg, p, a);
+  }
+  return SB_ERR_ARG;
 }
 
 int tc_launch(const GemvParams& p, const void* w_tc, void* operand, const TcPlan& pl, int fmt, bool pdl,

@@ -18,7 +18,8 @@ namespace sb {
 // tok0 + m0 + i of the outputs; argmax needs tok0 = 0).
 // Must be called by full warps with warp-uniform m0.  ARGMAX keeps a running
 // best per (warp, token) in wb_val/wb_idx[warp * 128 + m].
-template <int FMT, int CNT>
+// EPI: the epilogue (EPI_*), fixed at compile time.
+template <int FMT, int CNT, int EPI>
 __device__ __forceinline__ void tc_epi(const GemvParams& p, int row, bool row_ok, float* v, int m0, int M,
                                        float* wb_val, int* wb_idx, int warp, int tok0) {
   const int lane = threadIdx.x & 31;
@@ -29,11 +30,11 @@ __device__ __forceinline__ void tc_epi(const GemvParams& p, int row, bool row_ok
   }
 #pragma unroll
   for (int i = 0; i < CNT; ++i) v[i] *= rs;
-  if (p.epi == EPI_STORE) {
+  if constexpr (EPI == EPI_STORE) {
 #pragma unroll
     for (int i = 0; i < CNT; ++i)
       if (row_ok && m0 + i < M) p.y[static_cast<size_t>(tok0 + m0 + i) * p.n + row] = f_to_bf16_bits(v[i]);
-  } else if (p.epi == EPI_RESID) {
+  } else if constexpr (EPI == EPI_RESID) {
     // hidden = hidden + bf16(res_mult * bf16(y))   (llm_kernels.py:306-313)
     float h[CNT];
 #pragma unroll
@@ -43,7 +44,7 @@ __device__ __forceinline__ void tc_epi(const GemvParams& p, int row, bool row_ok
     for (int i = 0; i < CNT; ++i)
       if (row_ok && m0 + i < M)
         p.y[static_cast<size_t>(tok0 + m0 + i) * p.n + row] = f_to_bf16_bits(h[i] + bf(p.res_mult * bf(v[i])));
-  } else if (p.epi == EPI_SWIGLU) {
+  } else if constexpr (EPI == EPI_SWIGLU) {
     // act = bf16(bf16(silu(gate)) * up) (llm_kernels.py:252-260); gate row 2i, up row 2i+1
     const int inter = p.n / 2;
 #pragma unroll
@@ -55,7 +56,7 @@ __device__ __forceinline__ void tc_epi(const GemvParams& p, int row, bool row_ok
         p.y[static_cast<size_t>(tok0 + m0 + i) * inter + row / 2] = f_to_bf16_bits(sg * bf(up));
       }
     }
-  } else if (p.epi == EPI_QKV) {
+  } else if constexpr (EPI == EPI_QKV) {
     // q/k: RoPE with each product rounded to bf16 (llm_mega.py:539-543); k/v to
     // cache slot ctrl[SLOT] + token (StaticLayer.update, cache_utils.py:308-335)
     const int qk_rows = (p.n_q + p.n_kv) * 128;
@@ -101,7 +102,7 @@ __device__ __forceinline__ void tc_epi(const GemvParams& p, int row, bool row_ok
             f_to_bf16_bits(v[i]);
       }
     }
-  } else if (p.epi == EPI_ARGMAX) {
+  } else if constexpr (EPI == EPI_ARGMAX) {
     // logits = bf16(bf16(y) * (1/logits_scaling)); running (value, index) best per (warp, token)
 #pragma unroll
     for (int i = 0; i < CNT; ++i) {
