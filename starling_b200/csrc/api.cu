@@ -422,7 +422,7 @@ int32_t sb_decode_step_fused_ok(const SbModel* md, const SbState* st) {
 }
 
 int sb_decode_step(const SbModel* md, const SbState* st, int32_t step, sb_stream_t stream) {
-  return sb_decode_step_ex(md, st, step, use_step_kernel() ? 0 : SB_STEP_PER_OP, stream);
+  return sb_decode_step_ex(md, st, step, 0, stream);
 }
 
 int sb_decode_step_ex(const SbModel* md, const SbState* st, int32_t step, int32_t flags, sb_stream_t stream) {
@@ -430,7 +430,9 @@ int sb_decode_step_ex(const SbModel* md, const SbState* st, int32_t step, int32_
   if (!md->layers || md->n_layers < 1) return fail(SB_ERR_ARG, "no layers");
   if ((flags & SB_STEP_PER_OP) && (flags & SB_STEP_FUSED)) return fail(SB_ERR_ARG, "conflicting step flags");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (!(flags & SB_STEP_PER_OP)) {
+  // flags 0: the default path (per-op kernels; the fused step where it serves
+  // the forward when STARLING_B200_STEP=fused)
+  if ((flags & SB_STEP_FUSED) || (flags == 0 && use_step_kernel())) {
     StepPlan pl;
     const char* why = "";
     if (step_plan(md, st, pl, &why)) {

@@ -245,7 +245,7 @@ class GraniteEngine:
         need = int(self.lib.sb_linear_workspace_bytes(C.byref(c), x2.shape[0]))
         ws = getattr(self, "_lin_ws", None)
         if need and (ws is None or ws.numel() < need):
-            self._lin_ws = ws = torch.empty(need, dtype=torch.uint8, device=self.device)
+            self._lin_ws = ws = torch.zeros(need, dtype=torch.uint8, device=self.device)
         check(self.lib.sb_linear_ex(C.byref(c), ptr(x2), ptr(y), x2.shape[0], ptr(ws) if need else None,
                                     ws.numel() if need else 0, 0, _lib.current_stream()), "sb_linear_ex")
         if p.row_perm is not None:
@@ -304,7 +304,7 @@ class GraniteEngine:
         q = torch.empty(B * Tp, d.n_q * d.head_dim, dtype=BF16, device=dev)
         attn = torch.empty_like(q)
         act = torch.empty(rows, d.inter, dtype=BF16, device=dev)
-        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+        ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)
         rc = self.lib.sb_prefill(m, ptr(hidden), B, Tp, ptr(pl), ptr(q), ptr(attn), ptr(act), ptr(ws), ws_bytes,
                                  _lib.current_stream())
         if rc == 1002 and not required:  # SB_ERR_CONFIG: a projection is not served by the tensor-core GEMM

@@ -158,7 +158,7 @@ def cmd_linear(a) -> None:
     x = torch.randn(a.m, a.k, device="cuda").to(torch.bfloat16)
     y = torch.empty(a.m, a.n, dtype=torch.bfloat16, device="cuda")
     need = int(lib.sb_linear_workspace_bytes(C.byref(cs[0]), a.m))
-    ws = torch.empty(max(need, 16), dtype=torch.uint8, device="cuda")
+    ws = torch.zeros(max(need, 16), dtype=torch.uint8, device="cuda")
 
     def run():
         for i in range(a.reps):

@@ -105,7 +105,7 @@ def _linear_tc(p, x, pdl=0):
     c = p.c_struct()
     need = int(lib.sb_linear_workspace_bytes(C.byref(c), m))
     assert need > 0, "tensor-core path not selected"
-    ws = torch.empty(need, dtype=torch.uint8, device="cuda")
+    ws = torch.zeros(need, dtype=torch.uint8, device="cuda")  # zeroed once: it holds counters
     y = torch.empty(m, p.n, dtype=BF16, device="cuda")
     check(lib.sb_linear_ex(C.byref(c), ptr(x), ptr(y), m, ptr(ws), need, pdl, S()), "sb_linear_ex")
     return y
