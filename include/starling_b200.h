@@ -168,9 +168,10 @@ int sb_decode_step(const SbModel* model, const SbState* state, int32_t step, sb_
 int sb_decode_step_ex(const SbModel* model, const SbState* state, int32_t step, int32_t flags, sb_stream_t stream);
 /* 1 when the fused step serves (model, state), else 0 */
 int32_t sb_decode_step_fused_ok(const SbModel* model, const SbState* state);
-/* byte offset inside an SbState workspace of the fused step's scratch (its
- * first 32-bit word is the grid-barrier counter; all its counters are zero
- * between forwards), or SIZE_MAX when (model, tokens) has none */
+/* byte offset inside an SbState workspace of the fused step's scratch (32-bit
+ * words: [0..63] step counters, [64..1087] per (stream, KV head) attention
+ * counters; all zero between forwards except word 2, a sequence number), or
+ * SIZE_MAX when (model, tokens) has none */
 size_t sb_decode_step_scratch_offset(const SbModel* model, int32_t tokens);
 
 /* Launch ONE kernel of the decode step on its own (profiling / live timing

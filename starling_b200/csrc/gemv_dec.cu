@@ -275,7 +275,7 @@ __global__ void __launch_bounds__(512, 2) k_gemv_dec(const __grid_constant__ Gem
       };
       // two independent accumulator chains (kgroups in pairs), summed at the end
       float acc[4] = {0.f, 0.f, 0.f, 0.f}, acc2[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 1
+#pragma unroll
       for (int q = 0; q < KPW; q += 2) {
         kg_step(q, acc);
         kg_step(q + 1, acc2);

@@ -1,7 +1,7 @@
 // Fused decode step for up to 8 token rows, sm_100a: one cooperative launch
 // runs a whole forward of sb_decode_step -- every layer's q/k/v, attention,
-// o, gate/up and down and the lm_head argmax -- with grid-wide barriers
-// between dependent phases instead of kernel boundaries.
+// o, gate/up and down and the lm_head argmax -- with no kernel boundary and no
+// grid barrier: each phase hands its output to the next as epoch-tagged words.
 //
 //  * one CTA per SM (cooperative launch: all CTAs resident), 16 consumer
 //    warps and one producer warp;
@@ -26,12 +26,19 @@
 //    p = bf16(exp(s - max) * (1/sum)) with the global max and sum, writes its
 //    partial P.V, and the last split of the head to finish adds the partials
 //    in split order and rounds once;
+//  * hand-over: every activation another CTA reads (q, this forward's k/v
+//    rows, attention output, residual stream, SwiGLU output) is written as
+//    8-byte words {two bf16, epoch}, epochs unique per (launch, layer, phase);
+//    the reader polls the words it needs.  A buffer is rewritten only one
+//    layer later, after every reader of it has fed the all-to-all chain
+//    q/k/v -> attention -> o -> gate/up -> down that the writer depends on;
 //  * lm_head: each CTA keeps a running (value, index) best per token; the last
 //    CTA to finish reduces them (value desc, index asc), applies the decode /
-//    verify feedback and resets the counters for the next launch.
-// Every wait (ring mbarriers, grid barrier, attention counters) is bounded in
-// time; on expiry the kernel records SB_CTRL_ERR = 4, every later wait
-// returns at once, and the forward's results are invalid.
+//    verify feedback, resets the counters and advances the sequence number
+//    for the next launch.
+// Every wait (ring mbarriers, handed-over words, attention counters) is
+// bounded in time; on expiry the kernel records SB_CTRL_ERR = 4, every later
+// wait returns at once, and the forward's results are invalid.
 #include <cstdlib>
 
 #include "gemv_epi.cuh"
@@ -138,6 +145,54 @@ __device__ __forceinline__ bool counter_wait(const unsigned* c, unsigned target,
 
 // the 16 consumer warps only (the producer warp never joins)
 __device__ __forceinline__ void csync() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
+
+// ---- handed-over activations: 8-byte words {2 bf16 (low), epoch (high)} ----------
+// A word is written and read whole (single-copy atomic), so a reader that sees
+// its epoch sees that word's data; no barrier orders writer and reader.
+// Epochs are unique per (launch, layer, phase) and never 0 (zeroed buffers).
+enum { LL_QKV = 0, LL_ATTN = 1, LL_H_O = 2, LL_ACT = 3, LL_H_DOWN = 4 };
+__device__ __forceinline__ unsigned ll_epoch(unsigned seq, int layer, int phase) {
+  return (seq * 64u + static_cast<unsigned>(layer)) * 8u + static_cast<unsigned>(phase) + 1u;
+}
+__device__ __forceinline__ void ll_put(unsigned long long* p, uint32_t data, unsigned epoch) {
+  const unsigned long long v = (static_cast<unsigned long long>(epoch) << 32) | data;
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ll_ld(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+// N words p[0..N) carrying `epoch`: their data (bounded wait)
+template <int N>
+__device__ __forceinline__ void ll_get(const unsigned long long* p, unsigned epoch, uint32_t* out, int32_t* err) {
+  unsigned long long v[N];
+#pragma unroll
+  for (int i = 0; i < N; ++i) v[i] = ll_ld(p + i);
+  bool ok = true;
+#pragma unroll
+  for (int i = 0; i < N; ++i) ok = ok && static_cast<unsigned>(v[i] >> 32) == epoch;
+  if (!ok) {
+    const uint64_t t0 = gtime();
+    for (uint32_t it = 0; !ok; ++it) {
+      ok = true;
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        if (static_cast<unsigned>(v[i] >> 32) != epoch) v[i] = ll_ld(p + i);
+        ok = ok && static_cast<unsigned>(v[i] >> 32) == epoch;
+      }
+      if (!ok && (it & 15) == 15 && (aborted(err) || gtime() - t0 > kWaitNs)) {
+        if (!aborted(err)) fail_wait(err);
+        break;
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < N; ++i) out[i] = static_cast<uint32_t>(v[i]);
+}
+__device__ __forceinline__ uint32_t pack_bf2(float a, float b) {
+  return static_cast<uint32_t>(f_to_bf16_bits(a)) | (static_cast<uint32_t>(f_to_bf16_bits(b)) << 16);
+}
 
 // e2m1x2 bytes of one 32-bit word -> four f16x2 registers (PTX cvt, sm_100a)
 __device__ __forceinline__ void e2m1x8_to_h2x4(uint32_t w, uint32_t& a0, uint32_t& a1, uint32_t& a2, uint32_t& a3) {
@@ -390,15 +445,6 @@ __device__ __forceinline__ void ent_put(const Cx& cx, RingPos& rp) {
   ++rp.ei;
 }
 
-__device__ __forceinline__ void grid_sync(Cx& cx, unsigned* count) {
-  csync();
-  ++cx.nbar;
-  if (cx.tid == 0) {
-    red_release_add(count, 1u);
-    counter_wait(count, cx.nbar * gridDim.x, cx.err);
-  }
-  csync();
-}
 
 // Activation rows -> f16 slices in shared memory (bf16 for bf16 weights):
 // warp w < WT converts K slice w of every token into xs[w][m][kw + 8], with
@@ -407,7 +453,8 @@ __device__ __forceinline__ void grid_sync(Cx& cx, unsigned* count) {
 // scheme); the scales go to s_shift[w][m].  With a prologue, the RMSNorm
 // weights are the next ring entry.  Ends with a consumer barrier.
 template <int FMT, int K>
-__device__ __forceinline__ void load_act(const StepParams& P, const Cx& cx, RingPos& rp, int pro, const uint16_t* x) {
+__device__ __forceinline__ void load_act(const StepParams& P, const Cx& cx, RingPos& rp, int pro,
+                                         const unsigned long long* ll, unsigned epoch) {
   using G = Geo<FMT, K>;
   constexpr int KW = G::KPW * G::KGE;  // K elements per slice
   constexpr int XS = KW + 8;           // row stride (elements)
@@ -422,15 +469,21 @@ __device__ __forceinline__ void load_act(const StepParams& P, const Cx& cx, Ring
       id = id < 0 ? 0 : (id >= P.vocab ? P.vocab - 1 : id);  // never read outside the table
       return P.embed + static_cast<size_t>(id) * K;
     }
-    return x + static_cast<size_t>(m) * K;
+    return nullptr;
   };
   if (warp < G::WT) {
     // raw rows (embedding scaled: embed_tokens(ids) * 12, llm_mega.py:514); all loads in flight together
 #pragma unroll 4
     for (int i = lane; i < M * CPR; i += 32) {
       const int m = i / CPR, k = (i % CPR) * 8;
-      const uint4* src = reinterpret_cast<const uint4*>(row_src(m) + k0 + k);
-      uint4 v = embed ? __ldg(src) : __ldcg(src);  // rows written by this launch: read through L2
+      uint4 v;
+      if (embed) {
+        v = __ldg(reinterpret_cast<const uint4*>(row_src(m) + k0 + k));
+      } else {  // written by other CTAs in this launch: poll the words
+        uint32_t w[4];
+        ll_get<4>(ll + static_cast<size_t>(m) * (K / 2) + (k0 + k) / 2, epoch, w, cx.err);
+        v = make_uint4(w[0], w[1], w[2], w[3]);
+      }
       if (embed) {
         float f[8];
         unpack8(v, f);
@@ -559,10 +612,112 @@ __device__ __forceinline__ void slice_mma(const uint8_t* wsl, const uint8_t* ssl
 // 2^-s as a float (|s| < 127): the exact power of two
 __device__ __forceinline__ float pow2_neg(int s) { return __int_as_float((127 - s) << 23); }
 
-// One projection: this CTA's tiles, activation x (pro: prologue), epilogue
-// EPI (compile time: only its branch is generated) configured in *cx.sp.
+// Epilogues of the fused step: the decode GEMV's operations and rounding
+// (gemv_epi.cuh) on rows row0.. of tot, every output another CTA reads
+// written as handed-over words with `epoch` (rows in pairs / quads so that a
+// word holds two consecutive bf16 outputs).
+template <int FMT, int EPI>
+__device__ __forceinline__ void step_epi(const StepParams& P, const Cx& cx, const float* tot, int row0, int nrow,
+                                         int M, bool first, unsigned epoch) {
+  const GemvParams& p = *cx.sp;
+  const int tid = cx.tid;
+  auto fin = [&](int lrow, int m) -> float {
+    float v = tot[lrow * M + m];
+    if (FMT == SB_FMT_NVFP4) v *= p.gscale;
+    if (FMT == SB_FMT_FP8 || FMT == SB_FMT_INT8) v *= reinterpret_cast<const float*>(p.scale)[row0 + lrow];
+    return v;
+  };
+  if constexpr (EPI == EPI_ARGMAX) {
+    gemv_epilogue<FMT, EPI_ARGMAX>(p, tot, row0, nrow, M, cx.s_best, cx.s_bval, first, false, tid, kCW * 32);
+  } else if constexpr (EPI == EPI_RESID) {
+    // hidden = hidden + bf16(res_mult * bf16(y))   (llm_kernels.py:306-313)
+    const int np = nrow / 2;
+    for (int i = tid; i < np * M; i += kCW * 32) {
+      const int m = i / np, lr = 2 * (i % np), row = row0 + lr;
+      if (row >= p.n) continue;
+      uint16_t* cp = p.resid_cache + m * p.rc_stride + (row - p.rc_row0);
+      const uint32_t w = pack_bf2(u16_to_f(cp[0]) + bf(p.res_mult * bf(fin(lr, m))),
+                                  u16_to_f(cp[1]) + bf(p.res_mult * bf(fin(lr + 1, m))));
+      *reinterpret_cast<uint32_t*>(cp) = w;
+      *reinterpret_cast<uint32_t*>(p.y + static_cast<size_t>(m) * p.n + row) = w;
+      ll_put(P.ll_h + static_cast<size_t>(m) * (p.n / 2) + row / 2, w, epoch);
+    }
+  } else if constexpr (EPI == EPI_SWIGLU) {
+    // act = bf16(bf16(silu(gate)) * up)   (llm_kernels.py:252-260); rows gate 2j, up 2j+1
+    const int nq = nrow / 4, inter = p.n / 2;
+    for (int i = tid; i < nq * M; i += kCW * 32) {
+      const int m = i / nq, lr = 4 * (i % nq), row = row0 + lr;
+      if (row >= p.n) continue;
+      float o[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const float gv = bf(fin(lr + 2 * e, m));
+        const float sg = bf(gv / (1.f + expf(-gv)));
+        o[e] = sg * bf(fin(lr + 2 * e + 1, m));
+      }
+      ll_put(P.ll_act + static_cast<size_t>(m) * (inter / 2) + row / 4, pack_bf2(o[0], o[1]), epoch);
+    }
+  } else if constexpr (EPI == EPI_QKV) {
+    // q/k: RoPE with each product rounded to bf16 (llm_mega.py:539-543); k/v
+    // to cache slot ctrl[SLOT] + token (StaticLayer.update, cache_utils.py:308-335)
+    // and, for this forward's attention, to the handed-over words
+    const int qk_rows = (p.n_q + p.n_kv) * 128;
+    const int nq = nrow / 4;
+    for (int i = tid; i < nq * M; i += kCW * 32) {
+      const int m = i / nq, lr = 4 * (i % nq), row = row0 + lr;
+      if (row >= p.n) continue;
+      const int b = m / p.m_per, slot = cx.slot + m % p.m_per;
+      const bool slot_ok = slot >= 0 && slot < p.max_len;
+      const int head = row >> 7, within = row & 127;
+      if (row < qk_rows) {
+        const int j = within >> 1;  // rows 2j, 2j+1 -> dims j, j+64; rows 2j+2, 2j+3 -> dims j+1, j+65
+        float o1[2], o2[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float x1 = bf(fin(lr + 2 * e, m)), x2 = bf(fin(lr + 2 * e + 1, m));
+          const float cs = u16_to_f(p.rope_cache[m * 128 + j + e]);
+          const float sn = u16_to_f(p.rope_cache[m * 128 + 64 + j + e]);
+          o1[e] = bf(x1 * cs) - bf(x2 * sn);
+          o2[e] = bf(x2 * cs) + bf(x1 * sn);
+        }
+        const uint32_t wlo = pack_bf2(o1[0], o1[1]), whi = pack_bf2(o2[0], o2[1]);
+        if (head < p.n_q) {
+          unsigned long long* q = P.ll_q + (static_cast<size_t>(m) * p.n_q + head) * 64;
+          ll_put(q + j / 2, wlo, epoch);
+          ll_put(q + 32 + j / 2, whi, epoch);
+        } else {
+          const int kh = head - p.n_q;
+          if (slot_ok) {
+            uint16_t* kc = p.k_cache + ((static_cast<size_t>(b) * p.n_kv + kh) * p.max_len + slot) * 128;
+            *reinterpret_cast<uint32_t*>(kc + j) = wlo;
+            *reinterpret_cast<uint32_t*>(kc + j + 64) = whi;
+          }
+          unsigned long long* kv = P.ll_kv + (static_cast<size_t>(m) * p.n_kv + kh) * 128;
+          ll_put(kv + j / 2, wlo, epoch);
+          ll_put(kv + 32 + j / 2, whi, epoch);
+        }
+      } else {
+        const int vh = head - p.n_q - p.n_kv;  // dims within .. within + 3
+        const uint32_t w0 = pack_bf2(fin(lr, m), fin(lr + 1, m)), w1 = pack_bf2(fin(lr + 2, m), fin(lr + 3, m));
+        if (slot_ok) {
+          uint16_t* vc = p.v_cache + ((static_cast<size_t>(b) * p.n_kv + vh) * p.max_len + slot) * 128 + within;
+          *reinterpret_cast<uint32_t*>(vc) = w0;
+          *reinterpret_cast<uint32_t*>(vc + 2) = w1;
+        }
+        unsigned long long* kv = P.ll_kv + (static_cast<size_t>(m) * p.n_kv + vh) * 128 + 64 + within / 2;
+        ll_put(kv, w0, epoch);
+        ll_put(kv + 1, w1, epoch);
+      }
+    }
+  }
+}
+
+// One projection: this CTA's tiles, activation from the handed-over words ll
+// (epoch ep_in; pro: prologue), epilogue EPI (compile time) configured in
+// *cx.sp writing epoch ep_out.  A CTA without tiles reads nothing.
 template <int FMT, int K, int EPI>
-__device__ __forceinline__ void gemv_phase(const StepParams& P, Cx& cx, int n_tiles, int pro, const uint16_t* x) {
+__device__ __forceinline__ void gemv_phase(const StepParams& P, Cx& cx, int n_tiles, int pro,
+                                           const unsigned long long* ll, unsigned ep_in, unsigned ep_out) {
   using G = Geo<FMT, K>;
   constexpr int XS = G::KPW * G::KGE + 8;
   const int M = cx.M, warp = cx.warp, lane = cx.lane, tid = cx.tid;
@@ -573,7 +728,15 @@ __device__ __forceinline__ void gemv_phase(const StepParams& P, Cx& cx, int n_ti
   const int rounds = (nt + G::NG - 1) / G::NG;
 
   RingPos rp = cx.rp;
-  load_act<FMT, K>(P, cx, rp, pro, x);
+  if (nt == 0) {  // nothing to compute: only the RMSNorm-weight entry to pass
+    if (pro != PRO_NONE) {
+      ent_get(cx, rp, (K * 2u + 127u) & ~127u);
+      ent_put(cx, rp);
+    }
+    cx.rp = rp;
+    return;
+  }
+  load_act<FMT, K>(P, cx, rp, pro, ll, ep_in);
   const int sl = warp % G::WT;  // this warp's K slice
   const float us0 = pow2_neg(cx.s_shift[sl * 8 + min(2 * c, M - 1)]);
   const float us1 = pow2_neg(cx.s_shift[sl * 8 + min(2 * c + 1, M - 1)]);
@@ -622,8 +785,7 @@ __device__ __forceinline__ void gemv_phase(const StepParams& P, Cx& cx, int n_ti
       cx.tot[i] = sum;
     }
     csync();
-    gemv_epilogue<FMT, EPI>(*cx.sp, cx.tot, (t0 + tile0) * 16, ntl * 16, M, cx.s_best, cx.s_bval, rb == 0,
-                            rb + nr >= rounds, tid, kCW * 32);
+    step_epi<FMT, EPI>(P, cx, cx.tot, (t0 + tile0) * 16, ntl * 16, M, rb == 0, ep_out);
     csync();
   }
   cx.rp = rp;
@@ -676,31 +838,31 @@ __device__ __forceinline__ void set_epi(const StepParams& P, Cx& cx, int mat, in
 // Attention of one layer for this CTA's unit.  The K / V rows of older keys
 // were streamed into the next ring entry by the producer; rows of this
 // forward's tokens are read here (written by the q/k/v phase).
-__device__ __forceinline__ void attn_phase(const StepParams& P, Cx& cx, int layer) {
+__device__ __forceinline__ void attn_phase(const StepParams& P, Cx& cx, int layer, unsigned ep_in, unsigned ep_out) {
   const AttnUnit u = attn_unit(P, cx.slot, cx.pad_len);
   if (!u.active) return;
   const int NS = P.n_split, G = P.n_q / P.n_kv, R = G * P.m_per;
   const int tid = cx.tid, warp = cx.warp, lane = cx.lane, nk = u.nk;
-  const StepLayer& L = P.layers[layer];
   const int slot = cx.slot;
   uint8_t* ent = const_cast<uint8_t*>(ent_get(cx, cx.rp, kv_entry_bytes(nk)));
   const uint32_t* kw = reinterpret_cast<const uint32_t*>(ent);          // [nk][64 words]
   const uint16_t* vr = reinterpret_cast<const uint16_t*>(ent + nk * 256);  // [nk][128]
-  const size_t row0 = static_cast<size_t>(u.bh) * P.max_len;
 
-  // q rows (row r = token r / G, query head h*G + r % G); this forward's K / V rows
+  // q rows (row r = token r / G, query head h*G + r % G) and this forward's K / V
+  // rows: handed-over words of the q/k/v phase
   for (int i = tid; i < R * 64; i += kCW * 32) {
     const int r = i >> 6, d2 = i & 63;
     const int mi = r / G, gi = r % G;
-    cx.aq[r * 64 + d2] = __ldcg(reinterpret_cast<const unsigned*>(
-        P.q + (static_cast<size_t>(u.b * P.m_per + mi) * P.n_q + u.h * G + gi) * 128) + d2);
+    ll_get<1>(P.ll_q + (static_cast<size_t>(u.b * P.m_per + mi) * P.n_q + u.h * G + gi) * 64 + d2, ep_in,
+              cx.aq + r * 64 + d2, cx.err);
   }
-  for (int i = tid; i < nk * 32; i += kCW * 32) {
-    const int j = i >> 5, c16 = i & 15, isv = (i >> 4) & 1;
+  for (int i = tid; i < nk * 128; i += kCW * 32) {
+    const int j = i >> 7, isv = (i >> 6) & 1, w = i & 63;
     const int ps = u.pos(u.ka + j);
     if (ps < slot) continue;
-    const uint16_t* src = (isv ? L.v_cache : L.k_cache) + (row0 + ps) * 128 + c16 * 8;
-    *reinterpret_cast<uint4*>(ent + (isv ? nk * 256 : 0) + j * 256 + c16 * 16) = __ldcg(reinterpret_cast<const uint4*>(src));
+    const int m = u.b * P.m_per + (ps - slot);
+    ll_get<1>(P.ll_kv + (static_cast<size_t>(m) * P.n_kv + u.h) * 128 + isv * 64 + w, ep_in,
+              reinterpret_cast<uint32_t*>(ent + (isv ? nk * 256 : 0) + j * 256) + w, cx.err);
   }
   csync();
 
@@ -778,18 +940,24 @@ __device__ __forceinline__ void attn_phase(const StepParams& P, Cx& cx, int laye
   csync();
   if (*cx.s_flag) {  // last split of this head: sum the partials in split order, round once
     __threadfence();
-    for (int o = tid; o < R * 128; o += kCW * 32) {
-      const int r = o >> 7, d = o & 127;
-      float a = 0.f;
+    for (int o2 = tid; o2 < R * 64; o2 += kCW * 32) {
+      const int r = o2 >> 6, o = r * 128 + (o2 & 63) * 2;  // outputs o, o + 1
+      float a0 = 0.f, a1 = 0.f;
       for (int q0 = 0; q0 < NS; q0 += 8) {  // 8 loads in flight, summed in split order
-        float v[8];
+        float2 v[8];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) v[q] = q0 + q < NS ? __ldcg(part + static_cast<size_t>(q0 + q) * R * 128 + o) : 0.f;
+        for (int q = 0; q < 8; ++q)
+          v[q] = q0 + q < NS ? __ldcg(reinterpret_cast<const float2*>(part + static_cast<size_t>(q0 + q) * R * 128 + o))
+                             : make_float2(0.f, 0.f);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) a += v[q];
+        for (int q = 0; q < 8; ++q) {
+          a0 += v[q].x;
+          a1 += v[q].y;
+        }
       }
       const int mi = r / G, gi = r % G;
-      P.attn[(static_cast<size_t>(u.b * P.m_per + mi) * P.n_q + u.h * G + gi) * 128 + d] = f_to_bf16_bits(a);
+      ll_put(P.ll_attn + (static_cast<size_t>(u.b * P.m_per + mi) * P.n_q + u.h * G + gi) * 64 + (o2 & 63),
+             pack_bf2(a0, a1), ep_out);
     }
   }
 }
@@ -861,7 +1029,10 @@ __device__ void lm_finish(const StepParams& P, Cx& cx, bool has_rows) {
     if (tid == 0 && P.mode == SB_MODE_DECODE) P.ctrl[SB_CTRL_SLOT] += 1;
   }
   // every CTA has passed its last wait: reset the counters for the next launch
-  for (int i = tid; i < kSyncWords; i += kCW * 32) P.sync[i] = 0u;
+  // and advance the sequence number (new epochs for the handed-over words)
+  const unsigned seq = P.sync[kSyncSeq];
+  csync();
+  for (int i = tid; i < kSyncWords; i += kCW * 32) P.sync[i] = i == kSyncSeq ? seq + 1u : 0u;
 }
 
 template <int FMT, int KH, int KI>
@@ -975,31 +1146,37 @@ __global__ void __launch_bounds__(kThreads, 1) k_step(const __grid_constant__ St
     rc[m * P.rc_rows + r] =
         f_to_bf16_bits(bf(u16_to_f(P.embed[static_cast<size_t>(id) * P.hidden + rc_row0 + r]) * P.emb_mult));
   }
-  unsigned* gcount = P.sync + kSyncGrid;
 
+  // Phases hand their outputs over as epoch-tagged words: a phase polls its
+  // input words instead of waiting at a grid barrier.
+  const unsigned seq = P.sync[kSyncSeq];
   for (int l = 0; l < P.n_layers; ++l) {
     // q/k/v: RMSNorm (layer 0: embedding x12) -> RoPE, cache rows at ctrl[SLOT] + token
     if (tid == 0) set_epi(P, cx, 0, l, rope, rc);
-    gemv_phase<FMT, KH, EPI_QKV>(P, cx, P.n_tiles[0], l == 0 ? PRO_EMBED : PRO_RMSNORM, P.resid);
-    grid_sync(cx, gcount);
-    attn_phase(P, cx, l);
-    grid_sync(cx, gcount);
+    gemv_phase<FMT, KH, EPI_QKV>(P, cx, P.n_tiles[0], l == 0 ? PRO_EMBED : PRO_RMSNORM, P.ll_h,
+                                 l == 0 ? 0u : ll_epoch(seq, l - 1, LL_H_DOWN), ll_epoch(seq, l, LL_QKV));
+    attn_phase(P, cx, l, ll_epoch(seq, l, LL_QKV), ll_epoch(seq, l, LL_ATTN));
+    csync();
     // o -> residual
     if (tid == 0) set_epi(P, cx, 1, l, rope, rc);
-    gemv_phase<FMT, KH, EPI_RESID>(P, cx, P.n_tiles[1], PRO_NONE, P.attn);
-    grid_sync(cx, gcount);
+    gemv_phase<FMT, KH, EPI_RESID>(P, cx, P.n_tiles[1], PRO_NONE, P.ll_attn, ll_epoch(seq, l, LL_ATTN),
+                                   ll_epoch(seq, l, LL_H_O));
+    csync();
     // gate/up: RMSNorm -> SiLU(gate) * up
     if (tid == 0) set_epi(P, cx, 2, l, rope, rc);
-    gemv_phase<FMT, KH, EPI_SWIGLU>(P, cx, P.n_tiles[2], PRO_RMSNORM, P.resid);
-    grid_sync(cx, gcount);
+    gemv_phase<FMT, KH, EPI_SWIGLU>(P, cx, P.n_tiles[2], PRO_RMSNORM, P.ll_h, ll_epoch(seq, l, LL_H_O),
+                                    ll_epoch(seq, l, LL_ACT));
+    csync();
     // down -> residual
     if (tid == 0) set_epi(P, cx, 3, l, rope, rc);
-    gemv_phase<FMT, KI, EPI_RESID>(P, cx, P.n_tiles[3], PRO_NONE, P.act);
-    grid_sync(cx, gcount);
+    gemv_phase<FMT, KI, EPI_RESID>(P, cx, P.n_tiles[3], PRO_NONE, P.ll_act, ll_epoch(seq, l, LL_ACT),
+                                   ll_epoch(seq, l, LL_H_DOWN));
+    csync();
   }
   // final norm -> lm_head -> argmax
   if (tid == 0) set_epi(P, cx, 4, 0, rope, rc);
-  gemv_phase<FMT, KH, EPI_ARGMAX>(P, cx, P.n_tiles[4], PRO_RMSNORM, P.resid);
+  gemv_phase<FMT, KH, EPI_ARGMAX>(P, cx, P.n_tiles[4], PRO_RMSNORM, P.ll_h, ll_epoch(seq, P.n_layers - 1, LL_H_DOWN),
+                                  0u);
   int t0, nt;
   tile_range(P.n_tiles[4], t0, nt);
   lm_finish(P, cx, nt > 0);
@@ -1046,13 +1223,18 @@ static bool dims_supported(int hidden, int inter) {
 
 static int split_for(int max_len) { return (max_len + kStepKeys - 1) / kStepKeys; }
 
+// words of the handed-over activations per token
+static size_t ll_words(const SbModel* md) {
+  return static_cast<size_t>(md->hidden) / 2 + md->n_q * 64 * 2 + md->n_kv * 128 + md->inter / 2;
+}
+
 size_t step_ws_bytes(const SbModel* md, int tokens) {
   if (tokens < 1 || tokens > 8) return 0;
   const size_t rows = static_cast<size_t>(tokens) * md->n_q;  // batch * n_kv * R
   const size_t stats = rows * kStepMaxSplit * sizeof(float2);
   const size_t part = rows * kStepMaxSplit * 128 * 4;
   const size_t am = static_cast<size_t>(256) * tokens * 8;
-  return kSyncWords * 4 + stats + part + am;
+  return kSyncWords * 4 + stats + part + am + static_cast<size_t>(tokens) * ll_words(md) * 8;
 }
 
 bool step_plan(const SbModel* md, const SbState* st, StepPlan& pl, const char** why) {
@@ -1187,6 +1369,13 @@ int step_launch(const SbModel* md, const SbState* st, int step, void* ws, const 
   P.attn_part = reinterpret_cast<float*>(b + kSyncWords * 4 + rows * kStepMaxSplit * sizeof(float2));
   P.am_val = reinterpret_cast<float*>(b + kSyncWords * 4 + rows * kStepMaxSplit * (sizeof(float2) + 512));
   P.am_idx = reinterpret_cast<int*>(reinterpret_cast<char*>(P.am_val) + static_cast<size_t>(256) * P.M * 4);
+  unsigned long long* ll = reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(P.am_idx) +
+                                                                 static_cast<size_t>(256) * P.M * 4);
+  P.ll_h = ll;
+  P.ll_q = P.ll_h + static_cast<size_t>(P.M) * md->hidden / 2;
+  P.ll_kv = P.ll_q + static_cast<size_t>(P.M) * md->n_q * 64;
+  P.ll_attn = P.ll_kv + static_cast<size_t>(P.M) * md->n_kv * 128;
+  P.ll_act = P.ll_attn + static_cast<size_t>(P.M) * md->n_q * 64;
   P.n_split = pl.n_split;
   P.ring_bytes = pl.ring_bytes;
   P.rounds_per_batch = pl.rounds_per_batch;

@@ -51,6 +51,13 @@ struct StepParams {
   // scratch (state workspace): counters, attention statistics and partial
   // outputs, argmax partials
   unsigned* sync;
+  // activations handed between CTAs as 8-byte words {2 bf16, epoch}: a
+  // reader polls the words themselves (no barrier between the phases)
+  unsigned long long* ll_h;     // residual stream [M][hidden/2]
+  unsigned long long* ll_q;     // q rows [M][n_q*64]
+  unsigned long long* ll_kv;    // this forward's k and v rows [M][n_kv][2][64]
+  unsigned long long* ll_attn;  // attention output [M][n_q*64]
+  unsigned long long* ll_act;   // SwiGLU output [M][inter/2]
   float2* attn_stats;  // [B*n_kv][n_split][R]
   float* attn_part;    // [B*n_kv][n_split][R][128]
   float* am_val;       // [grid][M]
@@ -64,10 +71,12 @@ struct StepParams {
   StepLayer layers[kStepMaxLayers];
 };
 
-// sync[] words: grid barrier count, argmax arrivals, then per (stream, KV
-// head) the statistics counter and the combine counter.
+// sync[] words: grid barrier count, argmax arrivals, the launch sequence
+// number (epochs of the handed-over words), then per (stream, KV head) the
+// statistics counter and the combine counter.
 constexpr int kSyncGrid = 0;
 constexpr int kSyncArgmax = 1;
+constexpr int kSyncSeq = 2;
 constexpr int kSyncStats = 64;
 constexpr int kSyncCombine = 64 + 1024;
 constexpr int kSyncWords = 64 + 2048;

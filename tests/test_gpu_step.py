@@ -109,9 +109,10 @@ def test_fused_step_serves_b1_and_refuses_large_batches():
 
 
 def test_fused_step_wait_expiry_reports_error_and_recovers():
-    """A grid barrier that can never complete (its counter pushed out of
-    reach) expires after its time bound: the step records SB_CTRL_ERR = 4,
-    ends, resets its counters, and the next forward is correct again."""
+    """A wait that can never complete (the attention-statistics counter of
+    stream 0 / KV head 0 pushed out of reach) expires after its time bound:
+    the step records SB_CTRL_ERR = 4, ends, resets its counters, and the
+    next forward is correct again."""
     eng = _engine(SMALL, "bf16", 160, 1)
     st = eng.new_state(1, 1)
     off = int(eng.lib.sb_decode_step_scratch_offset(C.byref(eng.cmodel), 1))
@@ -119,11 +120,12 @@ def test_fused_step_wait_expiry_reports_error_and_recovers():
     ids = torch.tensor([5], device=DEV)
     ref = _run(eng, st, "ops", ids, 50, 50)
     ws = st.workspace.view(torch.int32)
-    ws[off // 4] = -1000  # count - target stays at -1000: the first barrier never completes
+    stats_word = off // 4 + 64  # the first per-(stream, KV head) statistics counter
+    ws[stats_word] = -1000  # count - target stays below zero: the first attention wait never completes
     torch.cuda.synchronize()
     bad = _run(eng, st, "fused", ids, 50, 50)
     assert bad[2] == 4
-    assert int(ws[off // 4]) == 0, "counters not reset after the failed forward"
+    assert int(ws[stats_word]) == 0, "counters not reset after the failed forward"
     good = _run(eng, st, "fused", ids, 50, 50)
     assert good[2] == 0
     assert float((good[0] - ref[0]).abs().max()) <= 1e-2 * float(ref[0].abs().max())
