@@ -210,7 +210,9 @@ int sb_lm_head_argmax_static(const SbModel* model, const SbState* state, int32_t
  * layer q/k/v (RMSNorm prologue, RoPE at positions 0..T-1, K/V written to
  * cache slots 0..T-1 of streams 0..batch-1), causal attention over each
  * stream's keys [0, prompt_len[b]), o + residual, gate/up (RMSNorm, SwiGLU),
- * down + residual.  hidden [batch*T, hidden] bf16 holds the input embeddings
+ * down + residual.  Rows of padding positions (>= prompt_len[b]) are not
+ * computed where a whole 128-row token tile or 8-position query block is
+ * padding; their hidden rows and cache slots hold unspecified values.  hidden [batch*T, hidden] bf16 holds the input embeddings
  * times the embedding multiplier on entry and the last layer's output rows on
  * exit (the caller applies the final norm / lm_head to the rows it needs).
  * T must be a multiple of 8 and <= max_len (pad the prompts; prompt_len

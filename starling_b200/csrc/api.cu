@@ -609,6 +609,9 @@ extern "C" int sb_prefill(const SbModel* md, uint16_t* hidden, int32_t batch, in
       p.sin_tab = md->rope_sin;
       p.rope_max = md->rope_max_pos;
       p.ctrl = ws.ctrl;
+      p.row_len = prompt_len;  // token tiles entirely in padding are skipped
+      p.row_T = T;
+      p.row_b0 = b0;
       SB_TRY(run_linear(L.qkv, p, ws.tc, tcb, false, s));
     }
     // causal attention over the right-padded prompts: query blocks of kPrefillQBlock tokens
@@ -637,12 +640,18 @@ extern "C" int sb_prefill(const SbModel* md, uint16_t* hidden, int32_t batch, in
     for (int b0 = 0; b0 < batch; b0 += spb) {
       const int nb = batch - b0 < spb ? batch - b0 : spb;
       const size_t r0 = static_cast<size_t>(b0) * T;
+      auto padding = [&](GemvParams& g) {
+        g.row_len = prompt_len;
+        g.row_T = T;
+        g.row_b0 = b0;
+      };
       GemvParams p = base_params(L.o, nb * T);
       p.pro = PRO_NONE;
       p.x = attn + r0 * NQ;
       p.epi = EPI_RESID;
       p.y = hidden + r0 * H;
       p.res_mult = md->res_mult;
+      padding(p);
       SB_TRY(run_linear(L.o, p, ws.tc, tcb, false, s));
       p = base_params(L.gate_up, nb * T);
       p.pro = PRO_RMSNORM;
@@ -651,6 +660,7 @@ extern "C" int sb_prefill(const SbModel* md, uint16_t* hidden, int32_t batch, in
       p.eps = md->eps;
       p.epi = EPI_SWIGLU;
       p.y = act;
+      padding(p);
       SB_TRY(run_linear(L.gate_up, p, ws.tc, tcb, false, s));
       p = base_params(L.down, nb * T);
       p.pro = PRO_NONE;
@@ -658,6 +668,7 @@ extern "C" int sb_prefill(const SbModel* md, uint16_t* hidden, int32_t batch, in
       p.epi = EPI_RESID;
       p.y = hidden + r0 * H;
       p.res_mult = md->res_mult;
+      padding(p);
       SB_TRY(run_linear(L.down, p, ws.tc, tcb, false, s));
     }
   }

@@ -163,6 +163,18 @@ __global__ void __launch_bounds__(256, 2)
   int kv_len = slot + p.m_per;
   kv_len = kv_len > p.max_len ? p.max_len : kv_len;
   const int plen = p.prompt_len ? p.prompt_len[b] : kv_len;
+  if (p.qblocks > 1 && split == 1 && slot >= plen) {
+    // prefill: every query of this block is a prompt's padding; its rows are
+    // never used (later layers see them only through row-local operations)
+    pdl_wait();
+    pdl_launch();
+    for (int i = tid; i < R * 64; i += blockDim.x) {
+      const int r = i >> 6, mi = r / G, gi = r % G;
+      const size_t t = static_cast<size_t>(zb) * p.m_per + mi;
+      *reinterpret_cast<uint32_t*>(p.out + t * p.n_q * 128 + (kvh * G + gi) * 128 + (i & 63) * 2) = 0u;
+    }
+    return;
+  }
   const int n1 = plen < kv_len ? plen : kv_len;     // prompt part [0, n1)
   const int g0 = plen < pad_len ? pad_len : n1;     // generated part [g0, kv_len)
   const int n2 = kv_len > g0 ? kv_len - g0 : 0;

@@ -223,7 +223,8 @@ __global__ void __launch_bounds__(kPrepThreads) k_tc_prep(const __grid_constant_
     }
   pdl_wait();
   pdl_launch();
-  if (m >= p.m) {
+  const bool pad_row = m < p.m && p.row_len && (m % p.row_T) >= p.row_len[p.row_b0 + m / p.row_T];
+  if (m >= p.m || pad_row) {  // past the tokens, or a prompt's padding: zero operand rows
     for (int c = tid; c < n16 * CPE; c += kPrepThreads) {
       *reinterpret_cast<uint4*>(xt + off(ml, c)) = make_uint4(0, 0, 0, 0);
       if (FMT == SB_FMT_FP8) *reinterpret_cast<uint4*>(xt + off(mp + ml, c)) = make_uint4(0, 0, 0, 0);
@@ -345,9 +346,28 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
   const int q = S > 1 ? static_cast<int>(cg::this_cluster().block_rank()) : 0;
   const int cid = blockIdx.x / S, ncl = gridDim.x / S;
   const int kb0 = q * a.kb / S, kb1 = (q + 1) * a.kb / S, nk = kb1 - kb0;
-  // work items (weight tile, token tile), token tiles inner so that the CTAs
-  // working at the same time share weight tiles (L2 hits)
-  const int items = a.tiles * a.mtiles;
+  // token tiles that hold at least one real row (prefill of right-padded
+  // prompts: tiles entirely in padding are skipped by every role alike)
+  int* s_live = reinterpret_cast<int*>(smem + L.live);
+  if (tid == 0) {
+    int n = 0;
+    for (int tt = 0; tt < a.mtiles && tt < 64; ++tt) {
+      bool real = !p.row_len;
+      const int r0 = tt * a.mp, r1 = min(r0 + a.mp, M);
+      for (int r = r0; r < r1 && !real;) {  // one check per stream overlapping the tile
+        const int b = r / p.row_T, pos = r % p.row_T;
+        if (pos < p.row_len[p.row_b0 + b]) real = true;
+        r = (b + 1) * p.row_T;
+      }
+      if (real) s_live[1 + n++] = tt;
+    }
+    s_live[0] = n;
+  }
+  __syncthreads();
+  const int nlive = s_live[0];
+  // work items (weight tile, live token tile), token tiles inner so that the
+  // CTAs working at the same time share weight tiles (L2 hits)
+  const int items = a.tiles * nlive;
   const int my_tiles = cid < items ? (items - cid + ncl - 1) / ncl : 0;
   const uint32_t a_bytes = 16384u, b_bytes = static_cast<uint32_t>(a.np) * 128u;
   // CTAs start their K blocks at different offsets so that they do not all read
@@ -384,11 +404,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
       const int total = my_tiles * nk;
       auto kb_of = [&](int it) { return kb0 + (it % nk + rot) % nk; };
       auto a_src = [&](int it) {
-        const int t = (cid + (it / nk) * ncl) / a.mtiles;
+        const int t = (cid + (it / nk) * ncl) / nlive;
         return a.wt + (static_cast<size_t>(t) * a.kb + kb_of(it)) * 16384;
       };
       auto b_src = [&](int it) {
-        const int tt = (cid + (it / nk) * ncl) % a.mtiles;
+        const int tt = s_live[1 + (cid + (it / nk) * ncl) % nlive];
         return a.xq + (static_cast<size_t>(tt) * a.kb + kb_of(it)) * b_bytes;
       };
       const int pre = total < a.stages ? total : a.stages;
@@ -469,7 +489,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
     const int rp = tc_rows_per_rank(S);
     for (int tc = 0; tc < my_tiles; ++tc) {
       const int item = cid + tc * ncl, buf = tc & 1;
-      const int t = item / a.mtiles, tok0 = (item % a.mtiles) * a.mp;
+      const int t = item / nlive, tok0 = s_live[1 + item % nlive] * a.mp;
       const int Mt = M - tok0 < a.mp ? M - tok0 : a.mp;  // tokens of this tile
       if (FMT == SB_FMT_FP8) {
         epi_sync();  // every warp is done with the previous tile's scales
@@ -582,6 +602,7 @@ bool tc_plan(int fmt, int n, int k, int m, TcPlan& pl) {
   pl.mtiles = (m + pl.mp - 1) / pl.mp;
   pl.np = fmt == SB_FMT_FP8 ? 2 * pl.mp : pl.mp;
   if (pl.np < 16 || pl.np > 256) return false;
+  if (pl.mtiles > 64) return false;  // the GEMM keeps a list of at most 64 token tiles
   pl.tiles = (n + 127) / 128;
   pl.kb = k * eb / 128;
   if (pl.mtiles > 1) {  // many token tiles (prefill): persistent over (weight tile, token tile)

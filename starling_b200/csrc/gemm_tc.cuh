@@ -28,7 +28,7 @@ struct TcPlan {
 
 // Shared-memory layout, computed identically on the host and in the kernel.
 struct TcLayout {
-  size_t stage_bytes, part, out, bars, tmem, flag, best, bval, shift, wbv, wbi, total;
+  size_t stage_bytes, part, out, bars, tmem, flag, best, bval, shift, wbv, wbi, live, total;
 };
 __host__ __device__ inline int tc_rows_per_rank(int split) {
   const int rp = (128 + split - 1) / split;
@@ -56,7 +56,8 @@ __host__ __device__ inline TcLayout tc_layout(int np, int stages, int m, int spl
   L.shift = L.bval + 128 * 4;
   L.wbv = L.shift + 128 * 4;                    // [warps][128] running argmax value
   L.wbi = L.wbv + (kTcEpiWarps + 2) * 128 * 4;  // [warps][128] running argmax index
-  L.total = L.wbi + (kTcEpiWarps + 2) * 128 * 4;
+  L.live = L.wbi + (kTcEpiWarps + 2) * 128 * 4;  // [1 + 64] token tiles holding a real row (prefill)
+  L.total = L.live + 65 * 4;
   return L;
 }
 

@@ -64,6 +64,11 @@ struct GemvParams {
   const uint16_t* rope_cache;  // EPI_QKV: [m][cos 64 | sin 64] at each token's position
   uint16_t* resid_cache;       // EPI_RESID: [m][rc_stride] rows rc_row0.. of y, kept in step with y
   int rc_stride, rc_row0;
+  // prefill of right-padded prompts (tensor-core GEMM): token m is stream
+  // row_b0 + m / row_T at position m % row_T, padding when that position is
+  // >= row_len[stream]; null: no padding
+  const int32_t* row_len;
+  int row_T, row_b0;
 };
 
 template <int FMT>

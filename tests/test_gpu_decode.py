@@ -322,3 +322,29 @@ def test_native_prefill_matches_eager(fmt, B, T):
         a, r = kv_nat[:, :, b, :, :n], kv_eag[:, :, b, :, :n]
         assert (a - r).abs().max() <= 2 ** -5 * r.abs().max(), f"{fmt} stream {b}: cache rows differ"
     assert (h_nat - h_eag).abs().max() <= 2 ** -5 * h_eag.abs().max()
+
+
+@pytest.mark.parametrize("fmt", ["fp8", "bf16"])
+def test_native_prefill_skips_padding_tiles(fmt):
+    """Prompts of 400 / 150 / 200 positions padded to T = 400: whole 128-row
+    token tiles and 8-position query blocks lie in the padding and are skipped;
+    the valid cache rows and the last hidden rows still match the eager
+    prefill."""
+    d = gr.TINY_DIMS
+    w = gr.make_weights(d, seed=6, std=0.05, norm_jitter=0.1)
+    B, T = 3, 400
+    g = torch.Generator().manual_seed(17)
+    emb = torch.randn(B, T, d.hidden, generator=g).to(torch.bfloat16)
+    pl = torch.tensor([400, 150, 200])
+    eng = GraniteEngine(d, w, fmt, max_cache_len=512, max_batch=B)
+    h_nat = eng.prefill(emb.cuda(), pl, native=True).float().cpu()
+    kv_nat = eng.kv.float().cpu()
+    eng.kv.zero_()
+    h_eag = eng.prefill(emb.cuda(), pl, native=False).float().cpu()
+    kv_eag = eng.kv.float().cpu()
+    for b in range(B):
+        n = int(pl[b])
+        a, r = kv_nat[:, :, b, :, :n], kv_eag[:, :, b, :, :n]
+        assert (a - r).abs().max() <= 2 ** -5 * r.abs().max(), f"{fmt} stream {b}: cache rows differ"
+    assert torch.isfinite(h_nat).all()
+    assert (h_nat - h_eag).abs().max() <= 2 ** -5 * h_eag.abs().max()
