@@ -54,6 +54,16 @@ typedef void* sb_stream_t; /* a cudaStream_t */
  * [16 bytes] (eb = bytes per element), i.e. every 128-row x 128-byte block is
  * contiguous in the no-swizzle K-major canonical layout of tcgen05.mma;
  * rows >= n are zero.  NULL: those token counts use the mma.sync GEMV.
+ *
+ * w_bs (optional, nvfp4 only): the block-scaled tensor-core copy used for 1..8
+ * token rows (tcgen05.mma kind::mxf4nvf4): per (128-row tile, 256-element K
+ * block) 18432 bytes = 16384 bytes of e2m1 codes (two per byte, lower K index
+ * in the low nibble) laid out like w_tc (byte (row, kbyte) at rg*1024 +
+ * kc*128 + r*16 + b), then the block scales as four 512-byte chunks, chunk j
+ * covering K elements 64j..64j+63 of the block, byte (r % 32)*16 + (r / 32)*4
+ * + i for tile row r and 16-element block i of the chunk.  Same packed row
+ * order and tensor scale as w; rows >= n are zero.  K must be a multiple of
+ * 256.  NULL: 1..8 rows use the mma.sync GEMV.
  */
 typedef struct SbLinear {
   int32_t fmt;
@@ -65,6 +75,7 @@ typedef struct SbLinear {
   float global_scale; /* nvfp4 per-tensor scale, else 1 */
   int32_t _pad;
   const void* w_tc;
+  const void* w_bs;
 } SbLinear;
 
 /* One decoder layer.  qkv rows are [q heads | k heads | v heads] with the
@@ -141,6 +152,21 @@ int sb_version(void);
 uint64_t sb_launch_count(void);
 /* scratch bytes an SbState needs for (model, batch*m tokens) */
 size_t sb_workspace_bytes(const SbModel* model, int32_t tokens);
+
+/* Which kernel serves NVFP4 linears of 1..8 token rows whose SbLinear has a
+ * w_bs copy (process-wide; no counterpart in the reference, whose NVFP4 path
+ * is eager torch).  SB_NVFP4_AUTO (default, or from
+ * STARLING_B200_NVFP4=auto|block_scaled|mma_sync at first use): the
+ * block-scaled tcgen05 kernel where it measured faster on B200 -- matrices of
+ * >= 256 row tiles (lm_head) at any row count and 8-row forwards of <= 16-tile
+ * matrices -- else the mma.sync GEMV; SB_NVFP4_BLOCK_SCALED: the block-scaled
+ * kernel for every shape it serves; SB_NVFP4_MMA_SYNC: always the GEMV.
+ * Decided when a launch is issued (a captured graph keeps the kernels it
+ * recorded).  Returns the previous mode, or SB_ERR_ARG. */
+#define SB_NVFP4_AUTO 0
+#define SB_NVFP4_BLOCK_SCALED 1
+#define SB_NVFP4_MMA_SYNC 2
+int32_t sb_set_nvfp4_path(int32_t mode);
 
 /* ---- fused decode step ---------------------------------------------------
  * One full forward of state->m new tokens per stream through every layer,

@@ -20,6 +20,7 @@ SB_CTRL_SLOT, SB_CTRL_PADLEN, SB_CTRL_ACCEPT, SB_CTRL_ERR, SB_CTRL_WORDS = 0, 1,
 SB_MODE_DECODE, SB_MODE_VERIFY, SB_MODE_FIRST = 0, 1, 2
 SB_OP_QKV, SB_OP_ATTN, SB_OP_O, SB_OP_GATE_UP, SB_OP_DOWN, SB_OP_LM_HEAD = range(6)
 SB_STEP_PER_OP, SB_STEP_FUSED = 1, 2
+SB_NVFP4_AUTO, SB_NVFP4_BLOCK_SCALED, SB_NVFP4_MMA_SYNC = 0, 1, 2
 
 vp = C.c_void_p
 
@@ -28,7 +29,7 @@ class SbLinear(C.Structure):
     _fields_ = [
         ("fmt", C.c_int32), ("n", C.c_int32), ("k", C.c_int32), ("n_pad", C.c_int32),
         ("w", vp), ("scale", vp), ("global_scale", C.c_float), ("_pad", C.c_int32),
-        ("w_tc", vp),
+        ("w_tc", vp), ("w_bs", vp),
     ]
 
 
@@ -68,7 +69,7 @@ EXPORTS = [
     "sb_residual_scale", "sb_rope", "sb_argmax_bf16", "sb_attention", "sb_decode_op",
     "sb_lm_head_argmax_static", "sb_linear_ex", "sb_linear_workspace_bytes", "sb_launch_count",
     "sb_prefill", "sb_prefill_workspace_bytes", "sb_prefill_block_rows", "sb_decode_step_ex",
-    "sb_decode_step_fused_ok", "sb_decode_step_scratch_offset",
+    "sb_decode_step_fused_ok", "sb_decode_step_scratch_offset", "sb_set_nvfp4_path",
 ]
 
 
@@ -92,6 +93,8 @@ def load() -> C.CDLL:
     lib = C.CDLL(str(LIB_PATH))
     lib.sb_last_error.restype = C.c_char_p
     lib.sb_launch_count.restype = C.c_uint64
+    lib.sb_set_nvfp4_path.restype = C.c_int32
+    lib.sb_set_nvfp4_path.argtypes = [C.c_int32]
     lib.sb_prefill_workspace_bytes.restype = C.c_size_t
     lib.sb_prefill_workspace_bytes.argtypes = [C.POINTER(SbModel), C.c_int32, C.c_int32]
     lib.sb_prefill_block_rows.restype = C.c_int32

@@ -18,6 +18,7 @@
 #include <cstring>
 
 #include "attention.cuh"
+#include "gemm_bs.cuh"
 #include "gemm_tc.cuh"
 #include "gemv.cuh"
 #include "glue.cuh"
@@ -123,8 +124,60 @@ static int run_gemv(GemvParams& p, int fmt, bool pdl, cudaStream_t s) {
   return 0;
 }
 
+// NVFP4 1..8-row path (sb_set_nvfp4_path); -1 = not yet read from
+// STARLING_B200_NVFP4.
+static std::atomic<int> g_nvfp4_path{-1};
+static int nvfp4_path() {
+  int v = g_nvfp4_path.load(std::memory_order_relaxed);
+  if (v < 0) {
+    const char* e = getenv("STARLING_B200_NVFP4");
+    v = SB_NVFP4_AUTO;
+    if (e && strcmp(e, "mma_sync") == 0) v = SB_NVFP4_MMA_SYNC;
+    if (e && strcmp(e, "block_scaled") == 0) v = SB_NVFP4_BLOCK_SCALED;
+    int expect = -1;
+    g_nvfp4_path.compare_exchange_strong(expect, v);
+    v = g_nvfp4_path.load(std::memory_order_relaxed);
+  }
+  return v;
+}
+
+// Whether the block-scaled kernel serves (l, m).  In auto mode it takes the
+// shapes where it measured faster than the mma.sync GEMV on B200 (graphed
+// launches, weights streamed from HBM): its fixed cost per launch (TMEM
+// allocation, building the activation terms, ~100 ns per tcgen05 instruction)
+// is paid back over hundreds of tiles (lm_head: 34.5 vs 42.4 us at 1 row,
+// 52 vs 131 us at 8) and by 8-row forwards over few tiles (down 18.5 vs
+// 22.6 us, o 8.5 vs 9.6 us), not by the 1-row layer projections.
+static bool bs_serves(const SbLinear& l, int m, BsPlan& bp) {
+  if (l.fmt != SB_FMT_NVFP4 || !l.w_bs || m > kBsMaxRows) return false;
+  const int mode = nvfp4_path();
+  if (mode == SB_NVFP4_MMA_SYNC || !bs_plan(l.n, l.k, m, bp)) return false;
+  if (mode == SB_NVFP4_BLOCK_SCALED) return true;
+  return bp.tiles >= 256 || (m >= 8 && bp.tiles <= 16);
+}
+
+int32_t sb_set_nvfp4_path(int32_t mode) {
+  if (mode < SB_NVFP4_AUTO || mode > SB_NVFP4_MMA_SYNC) return fail(SB_ERR_ARG, "sb_set_nvfp4_path: mode %d", mode);
+  const int prev = nvfp4_path();
+  g_nvfp4_path.store(mode, std::memory_order_relaxed);
+  return prev;
+}
+
+// 1..8 token rows: the block-scaled tcgen05 kernel where bs_serves, else the
+// GEMV kernels.
+static int run_small(const SbLinear& l, GemvParams& p, bool pdl, cudaStream_t s) {
+  BsPlan bp;
+  if (bs_serves(l, p.m, bp)) {
+    const int rc = bs_launch(p, l.w_bs, bp, pdl, s);
+    if (rc != 0) return fail(rc, "block-scaled gemm launch (n=%d k=%d m=%d): %s", p.n, p.k, p.m,
+                             rc < 1000 ? cudaGetErrorString((cudaError_t)rc) : "config");
+    return 0;
+  }
+  return run_gemv(p, l.fmt, pdl, s);
+}
+
 // One linear: the tcgen05 GEMM when it serves (l, p.m) and operand scratch is
-// given, else the GEMV kernels.
+// given, else run_small.
 static int run_linear(const SbLinear& l, GemvParams& p, void* tc_scratch, size_t tc_bytes, bool pdl, cudaStream_t s) {
   TcPlan pl;
   if (tc_scratch && tc_plan_for(l, p.m, pl)) {
@@ -135,7 +188,7 @@ static int run_linear(const SbLinear& l, GemvParams& p, void* tc_scratch, size_t
                              rc < 1000 ? cudaGetErrorString((cudaError_t)rc) : "config");
     return 0;
   }
-  return run_gemv(p, l.fmt, pdl, s);
+  return run_small(l, p, pdl, s);
 }
 
 // CTAs per (stream, KV head): enough (stream, head) groups fill the GPU on
@@ -175,7 +228,10 @@ static LmWork lm_work(const SbModel* md, int tokens, void* base) {
   LmWork w;
   DecPlan pl;
   TcPlan tp;
-  if (tokens <= 8 && dec_plan_for(l.fmt, l.n_pad / 16, l.k, tokens, pl)) {
+  BsPlan bp;
+  if (bs_serves(l, tokens, bp)) {
+    w.n_ctas = bp.n_ctas;
+  } else if (tokens <= 8 && dec_plan_for(l.fmt, l.n_pad / 16, l.k, tokens, pl)) {
     w.n_ctas = pl.n_ctas;
   } else if (tc_plan_for(l, tokens, tp)) {
     w.n_ctas = tp.n_ctas;
@@ -499,7 +555,7 @@ int sb_linear_ex(const SbLinear* lin, const uint16_t* x, uint16_t* y, int32_t m,
   p.x = x;
   p.epi = EPI_STORE;
   p.y = y;
-  return run_gemv(p, lin->fmt, use_pdl != 0, s);
+  return run_small(*lin, p, use_pdl != 0, s);
 }
 
 // ---- native prefill -------------------------------------------------------------

@@ -119,10 +119,13 @@ class EngineState:
 class GraniteEngine:
     def __init__(self, dims, weights: dict, fmt: str = "bf16", max_cache_len: int = 640,
                  max_batch: int = 1, device="cuda", rope_max_pos: Optional[int] = None,
-                 tensor_cores: bool = True):
+                 tensor_cores: bool = True, block_scaled: bool = True):
         """tensor_cores: also keep the tcgen05 tile copy of every fp8 / bf16
         weight, which serves 9..128 token rows (batched decode, verify,
-        prefill); it doubles the weight memory of those formats."""
+        prefill); it doubles the weight memory of those formats.
+        block_scaled: also keep the block-scaled tcgen05 copy of every NVFP4
+        weight (same bytes as the packed weight), which the library uses for
+        1..8 token rows where it is faster (sb_set_nvfp4_path)."""
         self.lib = _lib.load()
         self.dims = d = GraniteDims.coerce(dims)
         if d.head_dim != 128:
@@ -140,7 +143,8 @@ class GraniteEngine:
         self.final_norm = W("norm.weight").contiguous()
         head_w = weights.get("lm_head.weight", None)
         tc = bool(tensor_cores)
-        self.lm_head = pack_matrix(self.embed if head_w is None else W("lm_head.weight"), fmt, tc=tc)
+        bs = bool(block_scaled)
+        self.lm_head = pack_matrix(self.embed if head_w is None else W("lm_head.weight"), fmt, tc=tc, bs=bs)
         self.layers = []
         for i in range(d.layers):
             p = f"layers.{i}."
@@ -148,10 +152,10 @@ class GraniteEngine:
                 in_norm=W(p + "input_layernorm.weight").contiguous(),
                 post_norm=W(p + "post_attention_layernorm.weight").contiguous(),
                 qkv=pack_qkv(W(p + "self_attn.q_proj.weight"), W(p + "self_attn.k_proj.weight"),
-                             W(p + "self_attn.v_proj.weight"), d.n_q, d.n_kv, fmt, tc=tc),
-                o=pack_matrix(W(p + "self_attn.o_proj.weight"), fmt, tc=tc),
-                gate_up=pack_gate_up(W(p + "mlp.gate_proj.weight"), W(p + "mlp.up_proj.weight"), fmt, tc=tc),
-                down=pack_matrix(W(p + "mlp.down_proj.weight"), fmt, tc=tc),
+                             W(p + "self_attn.v_proj.weight"), d.n_q, d.n_kv, fmt, tc=tc, bs=bs),
+                o=pack_matrix(W(p + "self_attn.o_proj.weight"), fmt, tc=tc, bs=bs),
+                gate_up=pack_gate_up(W(p + "mlp.gate_proj.weight"), W(p + "mlp.up_proj.weight"), fmt, tc=tc, bs=bs),
+                down=pack_matrix(W(p + "mlp.down_proj.weight"), fmt, tc=tc, bs=bs),
             )
             self.layers.append(L)
         # static KV cache: [layer][k|v][batch][n_kv][max_len][128] (StaticLayer layout per layer)

@@ -52,6 +52,7 @@ class PackedLinear:
     global_scale: float = 1.0
     row_perm: Optional[torch.Tensor] = None  # packed row r holds logical row row_perm[r]
     w_tc: Optional[torch.Tensor] = None  # uint8 tensor-core tile copy (fp8 / bf16)
+    w_bs: Optional[torch.Tensor] = None  # uint8 block-scaled tensor-core copy (nvfp4)
 
     def c_struct(self) -> SbLinear:
         s = SbLinear()
@@ -61,6 +62,7 @@ class PackedLinear:
         s.scale = self.scale.data_ptr() if self.scale is not None else None
         s.global_scale = float(self.global_scale)
         s.w_tc = self.w_tc.data_ptr() if self.w_tc is not None else None
+        s.w_bs = self.w_bs.data_ptr() if self.w_bs is not None else None
         return s
 
     @property
@@ -112,10 +114,44 @@ def tc_untile(t: torch.Tensor, n: int, kbytes: int) -> torch.Tensor:
     return v.reshape(n_pad, kbytes)[:n]
 
 
-def pack_matrix(w: torch.Tensor, fmt: str, tc: bool = False) -> PackedLinear:
+def bs_tiles(codes: torch.Tensor, sb: torch.Tensor) -> torch.Tensor:
+    """NVFP4 codes ``[n, k]`` (4-bit values in uint8) and block scales
+    ``[n, k/16]`` (e4m3 bytes) -> the block-scaled tensor-core copy
+    (``SbLinear.w_bs``): per (128-row tile, 256-element K block) the codes, two
+    per byte (lower K index in the low nibble), in the tile layout of
+    :func:`tc_tiles`, then four 512-byte scale chunks (chunk ``j`` = K elements
+    ``64j..64j+63``), byte ``(r % 32)*16 + (r // 32)*4 + i`` for tile row ``r``
+    and 16-element block ``i`` of the chunk."""
+    n, k = codes.shape
+    if k % 256:
+        raise ValueError(f"K={k} must be a multiple of 256 for the block-scaled copy")
+    n_pad = (n + 127) // 128 * 128
+    if n_pad != n:
+        codes = torch.cat([codes, torch.zeros(n_pad - n, k, dtype=torch.uint8, device=codes.device)])
+        sb = torch.cat([sb, torch.zeros(n_pad - n, k // 16, dtype=torch.uint8, device=sb.device)])
+    T, KB = n_pad // 128, k // 256
+    packed = (codes[:, 0::2] | (codes[:, 1::2] << 4)).contiguous()  # [n_pad, k/2]
+    ct = packed.reshape(T, 16, 8, KB, 8, 16).permute(0, 3, 1, 4, 2, 5).reshape(T, KB, 16384)
+    st = sb.reshape(T, 4, 32, KB, 4, 4).permute(0, 3, 4, 2, 1, 5).reshape(T, KB, 2048)
+    return torch.cat([ct, st], dim=2).contiguous().view(-1)
+
+
+def bs_untile(t: torch.Tensor, n: int, k: int):
+    """Inverse of :func:`bs_tiles` (layout check) -> (codes [n, k], scales [n, k/16])."""
+    n_pad = (n + 127) // 128 * 128
+    T, KB = n_pad // 128, k // 256
+    v = t.view(T, KB, 18432)
+    packed = v[:, :, :16384].reshape(T, KB, 16, 8, 8, 16).permute(0, 2, 4, 1, 3, 5).reshape(n_pad, k // 2)
+    codes = torch.stack([packed & 15, packed >> 4], dim=2).reshape(n_pad, k)
+    sb = v[:, :, 16384:].reshape(T, KB, 4, 32, 4, 4).permute(0, 4, 3, 1, 2, 5).reshape(n_pad, k // 16)
+    return codes[:n], sb[:n]
+
+
+def pack_matrix(w: torch.Tensor, fmt: str, tc: bool = False, bs: bool = False) -> PackedLinear:
     """Quantise (if needed) and pack a logical weight [N, K] (bf16 or fp32).
 
-    tc: also build the tensor-core tile copy (fp8 / bf16 only)."""
+    tc: also build the tensor-core tile copy (fp8 / bf16 only).
+    bs: also build the block-scaled tensor-core copy (nvfp4, K % 256 == 0)."""
     n, k = w.shape
     kge = KGROUP_ELEMS[fmt]
     if k % 64:
@@ -144,6 +180,7 @@ def pack_matrix(w: torch.Tensor, fmt: str, tc: bool = False) -> PackedLinear:
         packed = _frag_order(q, kge).contiguous()
         return PackedLinear(fmt, n, k, n_pad, packed, s.contiguous(), w_tc=w_tc)
     codes, sb, g = parts
+    w_bs = bs_tiles(codes, sb) if bs and k % 256 == 0 else None
     w_tc = None
     if tc:  # code x block scale as bf16 (<= 6 significant bits: exact); the tensor scale stays apart
         cb = quant.e2m1_to_f32(codes).view(n, k // 16, 16) * quant.e4m3_to_f32(sb)[:, :, None]
@@ -155,7 +192,7 @@ def pack_matrix(w: torch.Tensor, fmt: str, tc: bool = False) -> PackedLinear:
     packed = (e[:, 0] | (e[:, 1] << 4)).contiguous()
     T, KG = n_pad // 16, k // 64
     sv = sb.reshape(T, 2, 8, KG, 4).permute(0, 3, 2, 4, 1).contiguous().view(-1)
-    return PackedLinear(fmt, n, k, n_pad, packed, sv, g, w_tc=w_tc)
+    return PackedLinear(fmt, n, k, n_pad, packed, sv, g, w_tc=w_tc, w_bs=w_bs)
 
 
 def rope_pair_perm(n_heads: int, head_dim: int = 128) -> torch.Tensor:
@@ -175,18 +212,18 @@ def gate_up_perm(inter: int) -> torch.Tensor:
     return torch.stack([torch.arange(inter), torch.arange(inter) + inter], dim=1).reshape(-1)
 
 
-def pack_qkv(wq, wk, wv, n_q, n_kv, fmt, head_dim=128, tc: bool = False) -> PackedLinear:
+def pack_qkv(wq, wk, wv, n_q, n_kv, fmt, head_dim=128, tc: bool = False, bs: bool = False) -> PackedLinear:
     perm = qkv_perm(n_q, n_kv, head_dim).to(wq.device)
     w = torch.cat([wq, wk, wv], dim=0)[perm]
-    p = pack_matrix(w, fmt, tc=tc)
+    p = pack_matrix(w, fmt, tc=tc, bs=bs)
     p.row_perm = perm
     return p
 
 
-def pack_gate_up(wg, wu, fmt, tc: bool = False) -> PackedLinear:
+def pack_gate_up(wg, wu, fmt, tc: bool = False, bs: bool = False) -> PackedLinear:
     perm = gate_up_perm(wg.shape[0]).to(wg.device)
     w = torch.cat([wg, wu], dim=0)[perm]
-    p = pack_matrix(w, fmt, tc=tc)
+    p = pack_matrix(w, fmt, tc=tc, bs=bs)
     p.row_perm = perm
     return p
 

@@ -54,7 +54,7 @@ def test_struct_layout_matches_header(tmp_path):
         "int main(void){\n"
         'printf("SbLinear %zu\\nSbLayer %zu\\nSbModel %zu\\nSbState %zu\\n", sizeof(SbLinear), sizeof(SbLayer),'
         " sizeof(SbModel), sizeof(SbState));\n"
-        "P(SbLinear, w) P(SbLinear, global_scale) P(SbLinear, w_tc) P(SbLayer, qkv) P(SbLayer, k_cache) P(SbModel, eps)"
+        "P(SbLinear, w) P(SbLinear, global_scale) P(SbLinear, w_tc) P(SbLinear, w_bs) P(SbLayer, qkv) P(SbLayer, k_cache) P(SbModel, eps)"
         " P(SbModel, embed) P(SbModel, lm_head) P(SbModel, layers) P(SbState, eos_id) P(SbState, ids)"
         " P(SbState, workspace_bytes)\nreturn 0;}\n"
     )

@@ -195,8 +195,22 @@ def test_verify_logits_match_oracle(golden):
     assert acc == j
 
 
-@pytest.mark.parametrize("fmt", ["fp8", "int8", "nvfp4"])
+@pytest.mark.parametrize("fmt", ["fp8", "int8", "nvfp4", "nvfp4-block-scaled"])
 def test_quantized_teacher_forced(golden, fmt):
+    """Teacher-forced decode steps vs the oracle model.  nvfp4-block-scaled:
+    every projection and the lm_head on the block-scaled tcgen05 kernel
+    (embedding / RMSNorm prologues, RoPE + cache, residual, SwiGLU and argmax
+    epilogues)."""
+    forced = fmt.endswith("block-scaled")
+    fmt = fmt.split("-")[0]
+    prev = _lib.load().sb_set_nvfp4_path(_lib.SB_NVFP4_BLOCK_SCALED if forced else _lib.SB_NVFP4_AUTO)
+    try:
+        _teacher_forced(golden, fmt)
+    finally:
+        _lib.load().sb_set_nvfp4_path(prev)
+
+
+def _teacher_forced(golden, fmt):
     d, w, g = golden
     emb = g["inputs_embeds"]
     eng = GraniteEngine(d, w, fmt, max_cache_len=96, max_batch=1)

@@ -143,6 +143,99 @@ def test_linear_tensor_cores_bf16_copy(fmt, n, k, m):
     _close_bf16(y.cpu(), ref)
 
 
+def _linear(p, x, pdl=0):
+    m = x.shape[0]
+    y = torch.empty(m, p.n, dtype=BF16, device="cuda")
+    check(lib.sb_linear(C.byref(p.c_struct()), ptr(x), ptr(y), m, pdl, S()), "sb_linear")
+    return y
+
+
+def _bs(w):
+    p = _to_dev(pack.pack_matrix(w, "nvfp4", bs=True))
+    p.w_bs = p.w_bs.cuda()
+    return p
+
+
+@pytest.fixture
+def block_scaled():
+    """Every NVFP4 linear of 1..8 rows with a w_bs copy on the block-scaled
+    kernel (not only the shapes the automatic choice gives it)."""
+    prev = lib.sb_set_nvfp4_path(_lib.SB_NVFP4_BLOCK_SCALED)
+    yield
+    lib.sb_set_nvfp4_path(prev)
+
+
+@pytest.mark.parametrize("n,k,m", [(3072, 2048, 1), (2048, 8192, 1), (2048, 2048, 1), (16384, 2048, 1),
+                                   (20000, 256, 2), (1000, 2048, 3), (2048, 2048, 8), (2048, 8192, 8),
+                                   (512, 1024, 5), (200, 256, 4)])
+def test_linear_block_scaled_nvfp4(block_scaled, n, k, m):
+    """NVFP4 at 1..8 token rows on the block-scaled tcgen05 kernel
+    (kind::mxf4nvf4: the weight's codes and e4m3 block scales as they are, the
+    activation as eight e2m1 terms) vs the fp32 reference over the exactly
+    dequantised weight: same bar as the GEMV (one bf16 rounding step).  Shapes
+    cover K split over clusters of 2..8 CTAs, one and several tiles per
+    persistent CTA, partial tiles and N = 8..64."""
+    w = _w(n, k, seed=n + k + m)
+    x = torch.randn(m, k, generator=torch.Generator().manual_seed(8)).to(BF16)
+    y = _linear(_bs(w), x.cuda())
+    ref = (x.float() @ _oracle_dense(w, "nvfp4").T).to(BF16)
+    _close_bf16(y.cpu(), ref)
+
+
+def test_linear_block_scaled_wide_range_rows(block_scaled):
+    """Activation terms: rows spanning many binades, an all-zero row and a row
+    near 1e-20 still match the fp32 reference."""
+    n, k, m = 512, 1024, 6
+    w = _w(n, k, seed=5)
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(m, k, generator=g) * torch.exp2(torch.randint(-12, 6, (m, k), generator=g).float())
+    x[3] = 0
+    x[5] *= 1e-20
+    x = x.to(BF16)
+    y = _linear(_bs(w), x.cuda()).cpu()
+    ref = (x.float() @ _oracle_dense(w, "nvfp4").T).to(BF16)
+    assert torch.all(y[3] == 0)
+    _close_bf16(y, ref)
+
+
+def test_linear_block_scaled_runs_deterministic_and_agrees_with_gemv(block_scaled):
+    """The block-scaled kernel is the one that runs (kernel names from the
+    profiler), repeats bit for bit with and without programmatic dependent
+    launch, and agrees with the mma.sync GEMV over the same packed weight."""
+    w = _w(3072, 2048, seed=21)
+    x = torch.randn(1, 2048, device="cuda").to(BF16)
+    p = _bs(w)
+    with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CUDA]) as prof:
+        y0 = _linear(p, x, 0)
+        torch.cuda.synchronize()
+    names = [e.name for e in prof.events()]
+    assert any("k_bs_gemm" in s for s in names), names[:10]
+    y1 = _linear(p, x, 1)
+    y2 = _linear(p, x, 0)
+    assert torch.equal(y0, y1) and torch.equal(y0, y2)
+    yg = _linear(_to_dev(pack.pack_matrix(w, "nvfp4")), x)  # no w_bs: the mma.sync GEMV
+    _close_bf16(y0.cpu(), yg.cpu())
+
+
+def test_nvfp4_path_switch():
+    """sb_set_nvfp4_path returns the previous mode and rejects unknown ones;
+    in automatic mode a 1-row layer projection stays on the GEMV and the
+    lm_head-sized matrix takes the block-scaled kernel."""
+    prev = lib.sb_set_nvfp4_path(_lib.SB_NVFP4_AUTO)
+    try:
+        assert lib.sb_set_nvfp4_path(_lib.SB_NVFP4_AUTO) == _lib.SB_NVFP4_AUTO
+        assert lib.sb_set_nvfp4_path(7) not in (0, 1, 2)
+        x = torch.randn(1, 256, device="cuda").to(BF16)
+        for n, want in ((2048, False), (40000, True)):
+            p = _bs(_w(n, 256, seed=n))
+            with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CUDA]) as prof:
+                _linear(p, x)
+                torch.cuda.synchronize()
+            assert any("k_bs_gemm" in e.name for e in prof.events()) == want, n
+    finally:
+        lib.sb_set_nvfp4_path(prev)
+
+
 def test_linear_tensor_cores_wide_range_rows():
     """fp8 activation split: rows spanning many binades (and an all-zero row)
     still match the fp32 reference."""

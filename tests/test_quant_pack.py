@@ -152,3 +152,38 @@ def test_tensor_core_tile_layout(fmt):
         want = int(rows[row, kb_]) if row < n else 0
         assert int(t[off]) == want
     assert torch.equal(pack.tc_untile(t, n, kbytes), rows)
+
+
+def test_block_scaled_copy_layout():
+    """w_bs (nvfp4): per (tile, 256-element K block) 16384 bytes of codes, two
+    per byte (lower K index in the low nibble) at rg*1024 + kc*128 + r*16 + b,
+    then four 512-byte scale chunks, byte (r % 32)*16 + (r // 32)*4 + i for
+    chunk j (K elements 64j..64j+63) and 16-element block i; padded rows zero;
+    codes and scales are the oracle's quantisation."""
+    n, k = 200, 512
+    w = _w(n, k, seed=13)
+    p = pack.pack_matrix(w, "nvfp4", bs=True)
+    assert p.w_bs is not None and p.w_bs.numel() == 2 * (k // 256) * 18432
+    codes, sb, _ = qr.quantize("nvfp4", w.float().numpy())
+    codes = torch.from_numpy(np.asarray(codes, dtype=np.uint8).reshape(n, k))
+    sb = torch.from_numpy(np.asarray(sb, dtype=np.uint8).reshape(n, k // 16))
+    t = p.w_bs
+    KB = k // 256
+    g = torch.Generator().manual_seed(1)
+    for _ in range(500):
+        row = int(torch.randint(0, 256, (1,), generator=g))
+        e = int(torch.randint(0, k, (1,), generator=g))
+        tile, rr = divmod(row, 128)
+        rg, r = divmod(rr, 8)
+        kb, ke = divmod(e, 256)
+        kc, b = divmod(ke // 2, 16)
+        blk = (tile * KB + kb) * 18432
+        byte = int(t[blk + rg * 1024 + kc * 128 + r * 16 + b])
+        want = int(codes[row, e]) if row < n else 0
+        assert (byte >> (4 * (e & 1))) & 15 == want
+        j, i = divmod((ke % 256) // 16, 4)
+        s = int(t[blk + 16384 + j * 512 + (rr % 32) * 16 + (rr // 32) * 4 + i])
+        assert s == (int(sb[row, kb * 16 + j * 4 + i]) if row < n else 0)
+    c2, s2 = pack.bs_untile(t, n, k)
+    assert torch.equal(c2, codes) and torch.equal(s2, sb)
+    assert pack.pack_matrix(w[:, :448], "nvfp4", bs=True).w_bs is None  # K % 256 != 0: no copy
