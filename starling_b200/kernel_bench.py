@@ -152,8 +152,11 @@ def cmd_attention(a) -> None:
 
 def cmd_linear(a) -> None:
     lib = _lib.load()
+    lib.sb_set_nvfp4_path({"auto": _lib.SB_NVFP4_AUTO, "block_scaled": _lib.SB_NVFP4_BLOCK_SCALED,
+                           "mma_sync": _lib.SB_NVFP4_MMA_SYNC}[a.nvfp4_path])
     w = (torch.randn(a.n, a.k, device="cuda") * 0.02).to(torch.bfloat16)
-    copies = [pack.pack_matrix(w, a.fmt, tc=True) for _ in range(4)]  # rotate: 4 copies > L2 at large n
+    # rotate: 4 copies > L2 at large n
+    copies = [pack.pack_matrix(w, a.fmt, tc=True, bs=a.fmt == "nvfp4") for _ in range(4)]
     cs = [p.c_struct() for p in copies]
     x = torch.randn(a.m, a.k, device="cuda").to(torch.bfloat16)
     y = torch.empty(a.m, a.n, dtype=torch.bfloat16, device="cuda")
@@ -166,7 +169,7 @@ def cmd_linear(a) -> None:
 
     us = _graph_time(run) / a.reps
     nbytes = copies[0].nbytes
-    path = "tcgen05" if need else "gemv"
+    path = "tcgen05" if need else ("nvfp4 " + a.nvfp4_path if a.fmt == "nvfp4" else "gemv")
     print(f"linear {a.fmt} n={a.n} k={a.k} m={a.m} ({path}): {us:.2f} us per launch; weight bytes "
           f"{nbytes / 1e6:.2f} MB -> {nbytes / us / 1e3:.0f} GB/s")
 
@@ -190,6 +193,8 @@ def main(argv=None) -> None:
     p.add_argument("--k", type=int, default=2048)
     p.add_argument("--m", type=int, default=48)
     p.add_argument("--reps", type=int, default=20)
+    p.add_argument("--nvfp4-path", choices=["auto", "block_scaled", "mma_sync"], default="auto",
+                   help="kernel for 1..8-row NVFP4 launches (sb_set_nvfp4_path)")
     a = ap.parse_args(argv)
     torch.set_grad_enabled(False)
     {"ops": cmd_ops, "step": cmd_step, "attention": cmd_attention, "linear": cmd_linear}[a.cmd](a)
