@@ -11,7 +11,7 @@
 // the canonical no-swizzle K-major layout of tcgen05 (8-row x 16-byte core
 // matrices; K chunks 128 B apart, 8-row groups 1024 B apart), so one bulk
 // copy (cp.async.bulk, no tensor map) stages it.  The activations are
-// prepared once per launch by k_tc_prep into the same layout:
+// prepared once per launch (k_tc_prep_cta / k_tc_prep_warp) into the same layout:
 //  * bf16 weights (kind::f16): the bf16 rows themselves (after the prologue);
 //  * fp8 weights (kind::f8f6f4, e4m3 x e4m3): each row is scaled by a power
 //    of two 2^s (max |x| 2^s in [128, 256)) and split into two e4m3 terms,
@@ -95,17 +95,137 @@ struct TcArgs {
 };
 
 // ---- B operand: prologue + layout ------------------------------------------------
+// Many rows (prefill, token tiles of 128): one warp per (padded) token row,
+// kPrepRows rows per CTA: every reduction is a warp shuffle (no block barrier),
+// every lane works at any K, and the rows keep the SMs busy.  Lane l takes
+// the 16-element chunks l, l + 32, ... of the row; the row is read in up to
+// three passes (RMSNorm statistics; the maximum for the fp8 scale; the
+// output), the later ones from L1.  Rows >= m and padding rows of right-padded
+// prompts are written as zeros.
+constexpr int kPrepRows = 8;
+constexpr int kPrepThreads = kPrepRows * 32;
+constexpr int kPrepMaxK = 16384;
+
+template <int FMT>
+__global__ void __launch_bounds__(kPrepThreads) k_tc_prep_warp(const __grid_constant__ GemvParams p, uint8_t* xq,
+                                                                int32_t* xshift, int mp, int np, int rows) {
+  const int lane = threadIdx.x & 31;
+  const int m = blockIdx.x * kPrepRows + (threadIdx.x >> 5);  // token (padded to whole token tiles)
+  const int K = p.k, n16 = K / 16;
+  const size_t kb_bytes = static_cast<size_t>(np) * 128;
+  constexpr int CPE = tc_bf16_operand(FMT) ? 2 : 1;  // 16-byte output chunks per 16 elements and term
+  if (p.pro != PRO_NONE && m < p.m)  // RMSNorm weights are constant: warm L1 before the dependency wait
+    for (int c16 = lane; c16 < n16; c16 += 32) asm volatile("prefetch.global.L1 [%0];" ::"l"(p.norm_w + c16 * 16));
+  pdl_wait();
+  pdl_launch();
+  if (m >= rows) return;
+  // token tile m / mp holds rows mp * tile .. of the operand, each tile [kb][np/8][8][8][16 B]
+  uint8_t* xt = xq + static_cast<size_t>(m / mp) * (K * (tc_bf16_operand(FMT) ? 2 : 1) / 128) * kb_bytes;
+  const int ml = m % mp;  // row of the token within its tile
+  auto off = [&](int n, int c) -> size_t {  // 16-byte chunk c (along K bytes) of B-operand row n
+    return static_cast<size_t>(c >> 3) * kb_bytes + static_cast<size_t>(n >> 3) * 1024 + (c & 7) * 128 + (n & 7) * 16;
+  };
+  const bool pad_row = m < p.m && p.row_len && (m % p.row_T) >= p.row_len[p.row_b0 + m / p.row_T];
+  if (m >= p.m || pad_row) {  // past the tokens, or a prompt's padding: zero operand rows
+    for (int c = lane; c < n16 * CPE; c += 32) {
+      *reinterpret_cast<uint4*>(xt + off(ml, c)) = make_uint4(0, 0, 0, 0);
+      if (FMT == SB_FMT_FP8) *reinterpret_cast<uint4*>(xt + off(mp + ml, c)) = make_uint4(0, 0, 0, 0);
+    }
+    if (FMT == SB_FMT_FP8 && lane == 0) xshift[m] = 0;
+    return;
+  }
+  const bool embed = p.pro == PRO_EMBED;
+  const uint16_t* src;
+  if (embed) {
+    int64_t id = p.ids[m];
+    id = id < 0 ? 0 : (id >= p.embed_rows ? p.embed_rows - 1 : id);  // never read outside the table
+    src = p.embed + static_cast<size_t>(id) * K;
+  } else {
+    src = p.x + static_cast<size_t>(m) * K;
+  }
+  // the 16 input values of chunk c16 (embedding rows: embed_tokens(ids) * 12, llm_mega.py:514)
+  auto load16 = [&](int c16, float* f) {
+    unpack8(*reinterpret_cast<const uint4*>(src + c16 * 16), f);
+    unpack8(*reinterpret_cast<const uint4*>(src + c16 * 16 + 8), f + 8);
+    if (embed)
+#pragma unroll
+      for (int e = 0; e < 16; ++e) f[e] = bf(f[e] * p.emb_mult);
+  };
+  float rstd = 0.f;
+  if (p.pro != PRO_NONE) {  // RMSNorm statistics (modeling_granite.py:192-197)
+    float ss = 0.f;
+    for (int c16 = lane; c16 < n16; c16 += 32) {
+      float f[16];
+      load16(c16, f);
+      if (embed && p.hidden_out) {  // the residual stream of layer 0
+        uint4* ho = reinterpret_cast<uint4*>(p.hidden_out + static_cast<size_t>(m) * K + c16 * 16);
+        ho[0] = pack8(f);
+        ho[1] = pack8(f + 8);
+      }
+#pragma unroll
+      for (int e = 0; e < 16; ++e) ss += f[e] * f[e];
+    }
+    ss = warp_sum(ss);
+    rstd = 1.f / sqrtf(ss / static_cast<float>(K) + p.eps);
+  }
+  // prologue output of chunk c16: weight * bf16(x * rstd), or the input
+  auto values16 = [&](int c16, float* f) {
+    load16(c16, f);
+    if (p.pro != PRO_NONE) {
+      float wn[16];
+      unpack8(__ldg(reinterpret_cast<const uint4*>(p.norm_w + c16 * 16)), wn);
+      unpack8(__ldg(reinterpret_cast<const uint4*>(p.norm_w + c16 * 16 + 8)), wn + 8);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) f[e] = bf(wn[e] * bf(f[e] * rstd));
+    }
+  };
+  if constexpr (tc_bf16_operand(FMT)) {
+    for (int c16 = lane; c16 < n16; c16 += 32) {
+      float f[16];
+      values16(c16, f);
+      *reinterpret_cast<uint4*>(xt + off(ml, 2 * c16)) = pack8(f);
+      *reinterpret_cast<uint4*>(xt + off(ml, 2 * c16 + 1)) = pack8(f + 8);
+    }
+  } else {
+    float am = 0.f;
+    for (int c16 = lane; c16 < n16; c16 += 32) {
+      float f[16];
+      values16(c16, f);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) am = fmaxf(am, fabsf(f[e]));
+    }
+    am = warp_max(am);
+    int e2 = 0;
+    if (am > 0.f) frexpf(am, &e2);
+    const int shift = 8 - e2;  // max |x| 2^shift in [128, 256)
+    if (lane == 0) xshift[m] = shift;
+    for (int c16 = lane; c16 < n16; c16 += 32) {
+      float f[16];
+      values16(c16, f);
+      uint8_t q0[16], q1[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const float v = ldexpf(f[e], shift);  // exact
+        const float t0 = e4m3_round(v, q0[e]);
+        e4m3_round((v - t0) * 16.f, q1[e]);  // exact residual
+      }
+      *reinterpret_cast<uint4*>(xt + off(ml, c16)) = *reinterpret_cast<const uint4*>(q0);
+      *reinterpret_cast<uint4*>(xt + off(mp + ml, c16)) = *reinterpret_cast<const uint4*>(q1);
+    }
+  }
+}
+
 // One CTA per (padded) token row; the row is read once into registers (16
 // consecutive elements per thread and chunk), then RMSNorm statistics, the
 // power-of-two scale and the e4m3 split are all computed from registers.
 // Rows >= m are written as zeros.
-constexpr int kPrepThreads = 256;
+constexpr int kPrepCtaThreads = 256;
 constexpr int kPrepChunks = 4;  // 16-element chunks per thread: K <= 16384
 
 template <int FMT>
-__global__ void __launch_bounds__(kPrepThreads) k_tc_prep(const __grid_constant__ GemvParams p, uint8_t* xq,
+__global__ void __launch_bounds__(kPrepCtaThreads) k_tc_prep_cta(const __grid_constant__ GemvParams p, uint8_t* xq,
                                                            int32_t* xshift, int mp, int np) {
-  __shared__ float s_red[kPrepThreads / 32];
+  __shared__ float s_red[kPrepCtaThreads / 32];
   const int m = blockIdx.x, tid = threadIdx.x, K = p.k;  // m: token (padded to whole token tiles)
   const int n16 = K / 16;
   const size_t kb_bytes = static_cast<size_t>(np) * 128;
@@ -120,7 +240,7 @@ __global__ void __launch_bounds__(kPrepThreads) k_tc_prep(const __grid_constant_
   if (p.pro != PRO_NONE && m < p.m)
 #pragma unroll
     for (int j = 0; j < kPrepChunks; ++j) {
-      const int c16 = tid + j * kPrepThreads;
+      const int c16 = tid + j * kPrepCtaThreads;
       if (c16 < n16) {
         nw[j][0] = __ldg(reinterpret_cast<const uint4*>(p.norm_w + c16 * 16));
         nw[j][1] = __ldg(reinterpret_cast<const uint4*>(p.norm_w + c16 * 16 + 8));
@@ -130,7 +250,7 @@ __global__ void __launch_bounds__(kPrepThreads) k_tc_prep(const __grid_constant_
   pdl_launch();
   const bool pad_row = m < p.m && p.row_len && (m % p.row_T) >= p.row_len[p.row_b0 + m / p.row_T];
   if (m >= p.m || pad_row) {  // past the tokens, or a prompt's padding: zero operand rows
-    for (int c = tid; c < n16 * CPE; c += kPrepThreads) {
+    for (int c = tid; c < n16 * CPE; c += kPrepCtaThreads) {
       *reinterpret_cast<uint4*>(xt + off(ml, c)) = make_uint4(0, 0, 0, 0);
       if (FMT == SB_FMT_FP8) *reinterpret_cast<uint4*>(xt + off(mp + ml, c)) = make_uint4(0, 0, 0, 0);
     }
@@ -149,7 +269,7 @@ __global__ void __launch_bounds__(kPrepThreads) k_tc_prep(const __grid_constant_
   float f[kPrepChunks][16];
 #pragma unroll
   for (int j = 0; j < kPrepChunks; ++j) {
-    const int c16 = tid + j * kPrepThreads;
+    const int c16 = tid + j * kPrepCtaThreads;
     if (c16 < n16) {
       unpack8(*reinterpret_cast<const uint4*>(src + c16 * 16), f[j]);
       unpack8(*reinterpret_cast<const uint4*>(src + c16 * 16 + 8), f[j] + 8);
@@ -168,14 +288,14 @@ __global__ void __launch_bounds__(kPrepThreads) k_tc_prep(const __grid_constant_
     float ss = 0.f;
 #pragma unroll
     for (int j = 0; j < kPrepChunks; ++j)
-      if (tid + j * kPrepThreads < n16)
+      if (tid + j * kPrepCtaThreads < n16)
 #pragma unroll
         for (int e = 0; e < 16; ++e) ss += f[j][e] * f[j][e];
     ss = block_sum256(ss, s_red);
     const float rstd = 1.f / sqrtf(ss / static_cast<float>(K) + p.eps);
 #pragma unroll
     for (int j = 0; j < kPrepChunks; ++j) {
-      const int c16 = tid + j * kPrepThreads;
+      const int c16 = tid + j * kPrepCtaThreads;
       if (c16 < n16) {
         float wn[16];
         unpack8(nw[j][0], wn);
@@ -188,7 +308,7 @@ __global__ void __launch_bounds__(kPrepThreads) k_tc_prep(const __grid_constant_
   if constexpr (tc_bf16_operand(FMT)) {
 #pragma unroll
     for (int j = 0; j < kPrepChunks; ++j) {
-      const int c16 = tid + j * kPrepThreads;
+      const int c16 = tid + j * kPrepCtaThreads;
       if (c16 < n16) {
         *reinterpret_cast<uint4*>(xt + off(ml, 2 * c16)) = pack8(f[j]);
         *reinterpret_cast<uint4*>(xt + off(ml, 2 * c16 + 1)) = pack8(f[j] + 8);
@@ -198,7 +318,7 @@ __global__ void __launch_bounds__(kPrepThreads) k_tc_prep(const __grid_constant_
     float am = 0.f;
 #pragma unroll
     for (int j = 0; j < kPrepChunks; ++j)
-      if (tid + j * kPrepThreads < n16)
+      if (tid + j * kPrepCtaThreads < n16)
 #pragma unroll
         for (int e = 0; e < 16; ++e) am = fmaxf(am, fabsf(f[j][e]));
     am = block_max256(am, s_red);
@@ -208,7 +328,7 @@ __global__ void __launch_bounds__(kPrepThreads) k_tc_prep(const __grid_constant_
     if (tid == 0) xshift[m] = shift;
 #pragma unroll
     for (int j = 0; j < kPrepChunks; ++j) {
-      const int c16 = tid + j * kPrepThreads;
+      const int c16 = tid + j * kPrepCtaThreads;
       if (c16 < n16) {
         uint8_t q0[16], q1[16];
 #pragma unroll
@@ -502,7 +622,7 @@ size_t tc_operand_bytes(int fmt, int k, int m) {
 bool tc_plan(int fmt, int n, int k, int m, TcPlan& pl) {
   if (!tc_format(fmt) || m < 1 || n < 1) return false;
   const int eb = elem_bytes(fmt);
-  if ((k * eb) % 128 != 0 || k > 16 * kPrepThreads * kPrepChunks) return false;
+  if ((k * eb) % 128 != 0 || k > kPrepMaxK || k > 16 * kPrepCtaThreads * kPrepChunks) return false;
   pl.mp = tile_rows(fmt, m);
   pl.mtiles = (m + pl.mp - 1) / pl.mp;
   pl.np = fmt == SB_FMT_FP8 ? 2 * pl.mp : pl.mp;
@@ -574,13 +694,16 @@ static int tc_launch_t(const GemvParams& p0, const void* w_tc, void* operand, co
   at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(pl.mp * pl.mtiles);
-  cfg.blockDim = dim3(kPrepThreads);
+  const int rows = pl.mp * pl.mtiles;
+  const bool per_warp = pl.mtiles > 1;
+  cfg.gridDim = dim3(per_warp ? (rows + kPrepRows - 1) / kPrepRows : rows);
+  cfg.blockDim = dim3(per_warp ? kPrepThreads : kPrepCtaThreads);
   cfg.stream = stream;
   cfg.attrs = at;
   cfg.numAttrs = pdl ? 1 : 0;
   note_launch();
-  cudaError_t e = cudaLaunchKernelEx(&cfg, k_tc_prep<FMT>, p, xq, xshift, pl.mp, pl.np);
+  cudaError_t e = per_warp ? cudaLaunchKernelEx(&cfg, k_tc_prep_warp<FMT>, p, xq, xshift, pl.mp, pl.np, rows)
+                           : cudaLaunchKernelEx(&cfg, k_tc_prep_cta<FMT>, p, xq, xshift, pl.mp, pl.np);
   if (e != cudaSuccess) return e;
 
   TcArgs a;
