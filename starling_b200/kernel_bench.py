@@ -7,6 +7,7 @@ ncu summaries under profiles/ are captured on).
     python -m starling_b200.kernel_bench linear --fmt fp8 --n 16384 --k 2048 --m 48
     python -m starling_b200.kernel_bench step --workload b48 --layers 4   # one eager step in NVTX range "step"
     python -m starling_b200.kernel_bench step --workload b1 --path fused  # the one-launch fused step
+    python -m starling_b200.kernel_bench prefill --layers 40       # one native prefill of the b48 prompts
 
 Workloads (same as bench.py): b48 = 48 streams, FP8 weights, prompts
 U[300,900]; b1 = one stream, NVFP4 weights, 320 prompt positions.  Weights are
@@ -150,6 +151,31 @@ def cmd_attention(a) -> None:
           f"-> {nbytes / us / 1e3:.0f} GB/s; err={int(st.ctrl[_lib.SB_CTRL_ERR])}")
 
 
+def cmd_prefill(a) -> None:
+    """One native prefill of the b48 workload (48 prompts U[300,900], FP8), the
+    timed call inside NVTX range "prefill"."""
+    B, fmt, max_len = WORKLOADS["b48"]
+    dev = torch.device("cuda")
+    d = GraniteDims(layers=a.layers)
+    w = syn.make_weights(d, seed=0, device=dev)
+    eng = GraniteEngine(d, w, fmt, max_cache_len=max_len, max_batch=B, device=dev)
+    del w
+    torch.cuda.empty_cache()
+    inp = syn.batched_inputs(d.hidden, batch=B, seed=0)
+    emb = inp.inputs_embeds.to(dev)
+    eng.prefill(emb, inp.prompt_lengths)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("prefill")
+    e0.record()
+    eng.prefill(emb, inp.prompt_lengths)
+    e1.record()
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    print(f"prefill b48 ({B} prompts, padded to {inp.T}, {int(inp.prompt_lengths.sum())} positions), "
+          f"{a.layers} layers: {e0.elapsed_time(e1):.1f} ms")
+
+
 def cmd_linear(a) -> None:
     lib = _lib.load()
     lib.sb_set_nvfp4_path({"auto": _lib.SB_NVFP4_AUTO, "block_scaled": _lib.SB_NVFP4_BLOCK_SCALED,
@@ -187,6 +213,8 @@ def main(argv=None) -> None:
     p = sub.add_parser("attention")
     p.add_argument("--batch", type=int, default=48)
     p.add_argument("--reps", type=int, default=20)
+    p = sub.add_parser("prefill")
+    p.add_argument("--layers", type=int, default=40)
     p = sub.add_parser("linear")
     p.add_argument("--fmt", default="fp8")
     p.add_argument("--n", type=int, default=16384)
@@ -197,7 +225,7 @@ def main(argv=None) -> None:
                    help="kernel for 1..8-row NVFP4 launches (sb_set_nvfp4_path)")
     a = ap.parse_args(argv)
     torch.set_grad_enabled(False)
-    {"ops": cmd_ops, "step": cmd_step, "attention": cmd_attention, "linear": cmd_linear}[a.cmd](a)
+    {"ops": cmd_ops, "step": cmd_step, "attention": cmd_attention, "linear": cmd_linear, "prefill": cmd_prefill}[a.cmd](a)
 
 
 if __name__ == "__main__":
