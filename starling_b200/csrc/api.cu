@@ -562,6 +562,18 @@ int sb_linear_ex(const SbLinear* lin, const uint16_t* x, uint16_t* y, int32_t m,
 // Query tokens per attention CTA (R = n_q / n_kv * 8 query rows <= 64) and the
 // projection rows per launch (whole streams).
 static const int kPrefillQBlock = 8;
+
+// STARLING_B200_PREFILL_ATTN=two_pass runs the prefill's attention on the
+// two-pass prefill kernel (attention_pf.cu); otherwise the decode kernel with
+// query blocks of kPrefillQBlock positions.
+static bool use_prefill_attn() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("STARLING_B200_PREFILL_ATTN");
+    v = (e && strcmp(e, "two_pass") == 0) ? 1 : 0;
+  }
+  return v == 1;
+}
 static const int kPrefillBlockRows = 8192;
 
 static int prefill_streams_per_block(int B, int T) {
@@ -689,7 +701,8 @@ extern "C" int sb_prefill(const SbModel* md, uint16_t* hidden, int32_t batch, in
     a.chunk_cap = attn_key_capacity(T, 1);
     a.slots = 2;
     a.cache_rows = static_cast<long long>(md->max_batch) * md->n_kv * md->max_len;
-    const int rc = attn_launch(a, batch, false, s);
+    const int rc = use_prefill_attn() && attn_prefill_ok(md->n_q, md->n_kv) ? attn_prefill_launch(a, batch, T, s)
+                                                                           : attn_launch(a, batch, false, s);
     if (rc == SB_ERR_CONFIG) return fail(rc, "sb_prefill: no attention configuration for T=%d", T);
     if (rc != 0) return fail(rc, "sb_prefill: attention launch: %s", cudaGetErrorString((cudaError_t)rc));
     // per block of streams: o (+ residual), gate/up (RMSNorm, SwiGLU), down (+ residual)

@@ -25,5 +25,11 @@ int attn_tile_keys(int split);
 int attn_key_capacity(int max_len, int split);
 size_t attn_smem_bytes(int R, int chunk_cap, int slots, int tk);
 int attn_launch(const AttnParams& p, int batch, bool pdl, cudaStream_t stream);
+// Prefill (attention_pf.cu): causal attention of T prompt positions per stream
+// (queries p.q / p.out rows b * T + pos, keys cache slots 0..pos), 128 query
+// rows per CTA; uses p.q, k_cache, v_cache, out, n_q, n_kv, max_len,
+// attn_mult, prompt_len.
+bool attn_prefill_ok(int n_q, int n_kv);
+int attn_prefill_launch(const AttnParams& p, int batch, int T, cudaStream_t stream);
 
 }  // namespace sb
