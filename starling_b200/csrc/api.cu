@@ -563,14 +563,14 @@ int sb_linear_ex(const SbLinear* lin, const uint16_t* x, uint16_t* y, int32_t m,
 // projection rows per launch (whole streams).
 static const int kPrefillQBlock = 8;
 
-// STARLING_B200_PREFILL_ATTN=two_pass runs the prefill's attention on the
-// two-pass prefill kernel (attention_pf.cu); otherwise the decode kernel with
-// query blocks of kPrefillQBlock positions.
+// The prefill's attention runs on the two-pass prefill kernel
+// (attention_pf.cu); STARLING_B200_PREFILL_ATTN=blocks8 runs it on the decode
+// kernel with query blocks of kPrefillQBlock positions instead (A/B runs).
 static bool use_prefill_attn() {
   static int v = -1;
   if (v < 0) {
     const char* e = getenv("STARLING_B200_PREFILL_ATTN");
-    v = (e && strcmp(e, "two_pass") == 0) ? 1 : 0;
+    v = (e && strcmp(e, "blocks8") == 0) ? 0 : 1;
   }
   return v == 1;
 }
