@@ -78,9 +78,34 @@ __device__ __forceinline__ float block_max256(float v, float* s_red) {
   return t;
 }
 
-__device__ __forceinline__ float e4m3_round(float v, uint8_t& q) {
-  q = __nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3);
-  return __half2float(__half(__nv_cvt_fp8_to_halfraw(q, __NV_E4M3)));
+// 16 activation values -> the two e4m3 terms of the fp8 operand, x 2^shift =
+// t0 + t1 / 16 with t0 = e4m3(x 2^shift), t1 = e4m3(16 (x 2^shift - t0)), both
+// round-to-nearest saturating, bytes in element order.  The power-of-two
+// scaling and both subtractions are exact; the conversions go two at a time.
+__device__ __forceinline__ void e4m3_split16(const float* f, int shift, uint4& w0, uint4& w1) {
+  const bool fast = shift >= -126 && shift <= 126;  // 2^shift is a normal float
+  const float s2 = fast ? __int_as_float((shift + 127) << 23) : 0.f;
+  uint32_t a[4], b[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float v[4], r[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) v[e] = fast ? f[4 * i + e] * s2 : ldexpf(f[4 * i + e], shift);
+    const uint32_t p0 = __nv_cvt_float2_to_fp8x2(make_float2(v[0], v[1]), __NV_SATFINITE, __NV_E4M3);
+    const uint32_t p1 = __nv_cvt_float2_to_fp8x2(make_float2(v[2], v[3]), __NV_SATFINITE, __NV_E4M3);
+    const float2 d0 = __half22float2(__half2(__nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(p0), __NV_E4M3)));
+    const float2 d1 = __half22float2(__half2(__nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(p1), __NV_E4M3)));
+    r[0] = (v[0] - d0.x) * 16.f;
+    r[1] = (v[1] - d0.y) * 16.f;
+    r[2] = (v[2] - d1.x) * 16.f;
+    r[3] = (v[3] - d1.y) * 16.f;
+    const uint32_t p2 = __nv_cvt_float2_to_fp8x2(make_float2(r[0], r[1]), __NV_SATFINITE, __NV_E4M3);
+    const uint32_t p3 = __nv_cvt_float2_to_fp8x2(make_float2(r[2], r[3]), __NV_SATFINITE, __NV_E4M3);
+    a[i] = (p0 & 0xFFFFu) | (p1 << 16);
+    b[i] = (p2 & 0xFFFFu) | (p3 << 16);
+  }
+  w0 = make_uint4(a[0], a[1], a[2], a[3]);
+  w1 = make_uint4(b[0], b[1], b[2], b[3]);
 }
 
 }  // namespace
@@ -202,15 +227,10 @@ __global__ void __launch_bounds__(kPrepThreads) k_tc_prep_warp(const __grid_cons
     for (int c16 = lane; c16 < n16; c16 += 32) {
       float f[16];
       values16(c16, f);
-      uint8_t q0[16], q1[16];
-#pragma unroll
-      for (int e = 0; e < 16; ++e) {
-        const float v = ldexpf(f[e], shift);  // exact
-        const float t0 = e4m3_round(v, q0[e]);
-        e4m3_round((v - t0) * 16.f, q1[e]);  // exact residual
-      }
-      *reinterpret_cast<uint4*>(xt + off(ml, c16)) = *reinterpret_cast<const uint4*>(q0);
-      *reinterpret_cast<uint4*>(xt + off(mp + ml, c16)) = *reinterpret_cast<const uint4*>(q1);
+      uint4 w0, w1;
+      e4m3_split16(f, shift, w0, w1);
+      *reinterpret_cast<uint4*>(xt + off(ml, c16)) = w0;
+      *reinterpret_cast<uint4*>(xt + off(mp + ml, c16)) = w1;
     }
   }
 }
@@ -330,15 +350,10 @@ __global__ void __launch_bounds__(kPrepCtaThreads) k_tc_prep_cta(const __grid_co
     for (int j = 0; j < kPrepChunks; ++j) {
       const int c16 = tid + j * kPrepCtaThreads;
       if (c16 < n16) {
-        uint8_t q0[16], q1[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const float v = ldexpf(f[j][e], shift);  // exact
-          const float t0 = e4m3_round(v, q0[e]);
-          e4m3_round((v - t0) * 16.f, q1[e]);  // exact residual
-        }
-        *reinterpret_cast<uint4*>(xt + off(ml, c16)) = *reinterpret_cast<const uint4*>(q0);
-        *reinterpret_cast<uint4*>(xt + off(mp + ml, c16)) = *reinterpret_cast<const uint4*>(q1);
+        uint4 w0, w1;
+        e4m3_split16(f[j], shift, w0, w1);
+        *reinterpret_cast<uint4*>(xt + off(ml, c16)) = w0;
+        *reinterpret_cast<uint4*>(xt + off(mp + ml, c16)) = w1;
       }
     }
   }
