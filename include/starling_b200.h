@@ -158,8 +158,8 @@ size_t sb_workspace_bytes(const SbModel* model, int32_t tokens);
  * is eager torch).  SB_NVFP4_AUTO (default, or from
  * STARLING_B200_NVFP4=auto|block_scaled|mma_sync at first use): the
  * block-scaled tcgen05 kernel where it measured faster on B200 -- matrices of
- * >= 256 row tiles (lm_head) at any row count and 8-row forwards of <= 16-tile
- * matrices -- else the mma.sync GEMV; SB_NVFP4_BLOCK_SCALED: the block-scaled
+ * >= 256 row tiles (lm_head) at any row count and every 8-row forward -- else
+ * the mma.sync GEMV; SB_NVFP4_BLOCK_SCALED: the block-scaled
  * kernel for every shape it serves; SB_NVFP4_MMA_SYNC: always the GEMV.
  * Decided when a launch is issued (a captured graph keeps the kernels it
  * recorded).  Returns the previous mode, or SB_ERR_ARG. */

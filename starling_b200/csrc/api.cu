@@ -145,15 +145,16 @@ static int nvfp4_path() {
 // shapes where it measured faster than the mma.sync GEMV on B200 (graphed
 // launches, weights streamed from HBM): its fixed cost per launch (TMEM
 // allocation, building the activation terms, ~100 ns per tcgen05 instruction)
-// is paid back over hundreds of tiles (lm_head: 34.5 vs 42.4 us at 1 row,
-// 52 vs 131 us at 8) and by 8-row forwards over few tiles (down 18.5 vs
-// 22.6 us, o 8.5 vs 9.6 us), not by the 1-row layer projections.
+// is paid back over hundreds of tiles (lm_head: 24.7 vs 42.5 us at 1 row,
+// 52 vs 131 us at 8) and by every 8-row forward (q/k/v 9.0 vs 10.8, o 8.5 vs
+// 9.7, gate/up 18.9 vs 25.2, down 18.5 vs 22.6 us), not by the 1-row layer
+// projections (gate/up 9.7 vs 9.3, q/k/v 7.3 vs 4.3 us).
 static bool bs_serves(const SbLinear& l, int m, BsPlan& bp) {
   if (l.fmt != SB_FMT_NVFP4 || !l.w_bs || m > kBsMaxRows) return false;
   const int mode = nvfp4_path();
   if (mode == SB_NVFP4_MMA_SYNC || !bs_plan(l.n, l.k, m, bp)) return false;
   if (mode == SB_NVFP4_BLOCK_SCALED) return true;
-  return bp.tiles >= 256 || (m >= 8 && bp.tiles <= 16);
+  return bp.tiles >= 256 || m >= 8;
 }
 
 int32_t sb_set_nvfp4_path(int32_t mode) {

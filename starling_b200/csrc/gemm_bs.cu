@@ -60,10 +60,12 @@
 //
 // Measured on B200 (graphed launches, weights from HBM): each tcgen05.mma of
 // N = 8 costs about as much as a wide one (~100 ns of issue per instruction,
-// ~40 ns per tcgen05.cp), so a CTA streams ~30 GB/s and the fixed cost of a
-// launch (TMEM allocation, the activation terms) is ~3 us; the kernel wins
-// over the mma.sync GEMV where hundreds of tiles amortise that (lm_head) and
-// on 8-row forwards, and the host picks it for those shapes only (api.cu).
+// ~40 ns per tcgen05.cp) while the tensor pipe stays ~1 % busy, so a CTA
+// streams ~30 GB/s; plans therefore put two CTAs (two issuing threads) on an
+// SM where shared memory and TMEM allow.  With the fixed cost of a launch
+// (TMEM allocation, the activation terms, ~3 us) the kernel beats the mma.sync
+// GEMV on the lm_head (hundreds of tiles) and on 8-row forwards, and the host
+// picks it for those shapes (api.cu).
 #include <cooperative_groups.h>
 
 #include "gemm_bs.cuh"
@@ -495,30 +497,46 @@ static const int kSMs = 148;
 static const size_t kBsSmemOne = 220 * 1024;  // one CTA per SM (persistent over tiles)
 static const size_t kBsSmemTwo = 110 * 1024;  // two CTAs per SM (clusters splitting K)
 
-bool bs_plan(int n, int k, int m, BsPlan& pl) {
-  if (m < 1 || m > kBsMaxRows || n < 1 || k < 256 || k % 256 != 0) return false;
+// STARLING_B200_BS_CTAS_PER_SM=1 keeps one CTA per SM (A/B runs)
+static int bs_ctas_per_sm_max() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("STARLING_B200_BS_CTAS_PER_SM");
+    v = (e && atoi(e) == 1) ? 1 : 2;
+  }
+  return v;
+}
+
+// Plan for per_sm CTAs per SM (1: up to 220 KB of shared memory and 512 TMEM
+// columns each; 2: half of both).  Two CTAs per SM run two MMA-issuing threads
+// per SM, which is what bounds this kernel (tcgen05 issue latency, not the
+// tensor pipe): lm_head at 1 row 34.4 -> 24.7 us, gate/up at 8 rows 26.1 ->
+// 18.9 us on B200.
+static bool bs_plan_for(int n, int k, int m, int per_sm, BsPlan& pl) {
   pl.m = m;
   pl.ncol = kBsTerms * m;
   pl.tiles = (n + 127) / 128;
   pl.kb = k / 256;
-  if (pl.tiles * 4 >= kSMs * 3) {  // enough tiles: persistent, no K split
+  const int slots = kSMs * per_sm;
+  if (pl.tiles * 4 >= slots * 3) {  // enough tiles: persistent, no K split
     pl.split = 1;
-    pl.n_ctas = pl.tiles < kSMs ? pl.tiles : kSMs;
+    pl.n_ctas = pl.tiles < slots ? pl.tiles : slots;
   } else {
-    int s = kSMs / pl.tiles;
+    int s = slots / pl.tiles;
     if (s > 8) s = 8;
     if (s > pl.kb) s = pl.kb;
     if (s < 1) s = 1;
     pl.split = s;
     pl.n_ctas = pl.tiles * s;
   }
+  const bool two = pl.split > 1 || per_sm > 1;  // two CTAs per SM
   pl.kbc = (pl.kb + pl.split - 1) / pl.split;
   const int acc = 2 * pl.ncol;
   pl.sf_col = (acc + 31) / 32 * 32;
   // TMEM: accumulators, then 16 scale columns per ring stage (A) and per K
-  // block (B); two CTAs per SM (split > 1) keep to 256 columns each
-  const int tmem_max = pl.split > 1 ? 256 : 512;
-  const size_t budget = pl.split > 1 ? kBsSmemTwo : kBsSmemOne;
+  // block (B)
+  const int tmem_max = two ? 256 : 512;
+  const size_t budget = two ? kBsSmemTwo : kBsSmemOne;
   int max_st = pl.split > 1 ? pl.kbc : 12;  // a split CTA has at most kbc blocks: all in flight at once
   if (max_st > 12) max_st = 12;
   pl.stages = 0;
@@ -532,6 +550,12 @@ bool bs_plan(int n, int k, int m, BsPlan& pl) {
   while (pl.tmem_cols < pl.sf_col + 16 * (pl.stages + pl.kbc)) pl.tmem_cols *= 2;
   pl.smem = bs_layout(pl.ncol, pl.kbc, pl.stages, m, pl.split).total;
   return true;
+}
+
+bool bs_plan(int n, int k, int m, BsPlan& pl) {
+  if (m < 1 || m > kBsMaxRows || n < 1 || k < 256 || k % 256 != 0) return false;
+  if (bs_ctas_per_sm_max() >= 2 && bs_plan_for(n, k, m, 2, pl)) return true;
+  return bs_plan_for(n, k, m, 1, pl);
 }
 
 template <int EPI>
