@@ -37,7 +37,8 @@
 //    activation scaling and run the fused row-owned epilogue (tc_epi.cuh).
 // With many tiles (lm_head, gate/up) each CTA is persistent over tiles and the
 // epilogue of one tile overlaps the MMAs of the next (double-buffered
-// accumulator).  With few tiles a cluster of `split` (<= 4) CTAs shares a
+// accumulator; with one token tile and hundreds of weight tiles, two CTAs of
+// <= 110 KB per SM).  With few tiles a cluster of `split` (<= 4) CTAs shares a
 // tile, each taking a contiguous K range; every CTA pushes its partial rows
 // to the rank that finishes them (distributed shared memory), which sums them
 // in rank order (deterministic) and runs the epilogue on 128/split rows.
@@ -361,7 +362,7 @@ __global__ void __launch_bounds__(kPrepCtaThreads) k_tc_prep_cta(const __grid_co
 
 // ---- the GEMM ----------------------------------------------------------------------
 template <int FMT, int EPI>
-__global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant__ GemvParams p, const __grid_constant__ TcArgs a) {
+__global__ void __launch_bounds__(kTcThreads, 2) k_tc_gemm(const __grid_constant__ GemvParams p, const __grid_constant__ TcArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int M = p.m;
@@ -634,28 +635,51 @@ size_t tc_operand_bytes(int fmt, int k, int m) {
   return static_cast<size_t>(mtiles) * np * k * elem_bytes(fmt) + static_cast<size_t>(mtiles) * mp * 4;
 }
 
-bool tc_plan(int fmt, int n, int k, int m, TcPlan& pl) {
-  if (!tc_format(fmt) || m < 1 || n < 1) return false;
+// STARLING_B200_TC_CTAS_PER_SM=1 keeps one GEMM CTA per SM for decode /
+// verify launches (A/B runs)
+static int tc_ctas_per_sm_max() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("STARLING_B200_TC_CTAS_PER_SM");
+    v = (e && atoi(e) == 1) ? 1 : 2;
+  }
+  return v;
+}
+
+static const size_t kTcSmemTwo = 110 * 1024;  // two CTAs per SM
+
+// Plan for per_sm CTAs per SM.  Two CTAs per SM (decode / verify: one token
+// tile, many weight tiles) halve the ring and the TMEM of each but run two
+// MMA-issuing threads per SM, which is what bounds the streaming of a CTA at
+// these shapes (four MMAs per stage, issue latency rather than tensor-pipe
+// time).
+static bool tc_plan_for(int fmt, int n, int k, int m, int per_sm, TcPlan& pl) {
   const int eb = elem_bytes(fmt);
-  if ((k * eb) % 128 != 0 || k > kPrepMaxK || k > 16 * kPrepCtaThreads * kPrepChunks) return false;
   pl.mp = tile_rows(fmt, m);
   pl.mtiles = (m + pl.mp - 1) / pl.mp;
   pl.np = fmt == SB_FMT_FP8 ? 2 * pl.mp : pl.mp;
   if (pl.np < 16 || pl.np > 256) return false;
   if (pl.mtiles > 64) return false;  // the GEMM keeps a list of at most 64 token tiles
+  if (per_sm > 1 && pl.mtiles > 1) return false;
   pl.tiles = (n + 127) / 128;
   pl.kb = k * eb / 128;
+  const int slots = kSMs * per_sm;
+  // measured at 48 rows: two CTAs per SM pay off for persistent plans over
+  // hundreds of tiles (lm_head 88.8 -> 73.1 us) but not with K split over
+  // clusters of 8 (q/k/v 14.9 -> 16.9, o 9.7 -> 10.5 us; gate/up, down even)
+  if (per_sm > 1 && pl.tiles * 4 < slots * 3) return false;
   if (pl.mtiles > 1) {  // many token tiles (prefill): persistent over (weight tile, token tile)
     pl.split = 1;
     const int items = pl.tiles * pl.mtiles;
     pl.n_ctas = items < kSMs ? items : kSMs;
-  } else if (pl.tiles * 4 >= kSMs * 3) {  // enough tiles: persistent, no K split
+  } else if (pl.tiles * 4 >= slots * 3) {  // enough tiles: persistent, no K split
     pl.split = 1;
-    pl.n_ctas = pl.tiles < kSMs ? pl.tiles : kSMs;
+    pl.n_ctas = pl.tiles < slots ? pl.tiles : slots;
   } else {
-    // clusters of more than 4 CTAs of ~200 KiB do not all fit at once
-    int s = kSMs / pl.tiles;
-    if (s > 4) s = 4;
+    // one CTA per SM: clusters of more than 4 CTAs of ~200 KiB do not all fit at once
+    int s = slots / pl.tiles;
+    const int smax = per_sm > 1 ? 8 : 4;
+    if (s > smax) s = smax;
     if (s > pl.kb) s = pl.kb;
     if (s < 1) s = 1;
     pl.split = s;
@@ -663,16 +687,26 @@ bool tc_plan(int fmt, int n, int k, int m, TcPlan& pl) {
   }
   pl.ncols = 32;
   while (pl.ncols < 2 * pl.np) pl.ncols *= 2;  // two accumulator buffers
+  if (per_sm > 1 && pl.ncols > 256) return false;
+  const size_t budget = per_sm > 1 ? kTcSmemTwo : kTcSmem;
   pl.stages = 0;
   const int ml = m < pl.mp ? m : pl.mp;  // token rows of one tile
   for (int st = 8; st >= 2; --st)
-    if (tc_layout(pl.np, st, ml, pl.split).total <= kTcSmem) {
+    if (tc_layout(pl.np, st, ml, pl.split).total <= budget) {
       pl.stages = st;
       break;
     }
   if (!pl.stages) return false;
   pl.smem = tc_layout(pl.np, pl.stages, ml, pl.split).total;
   return true;
+}
+
+bool tc_plan(int fmt, int n, int k, int m, TcPlan& pl) {
+  if (!tc_format(fmt) || m < 1 || n < 1) return false;
+  const int eb = elem_bytes(fmt);
+  if ((k * eb) % 128 != 0 || k > kPrepMaxK || k > 16 * kPrepCtaThreads * kPrepChunks) return false;
+  if (tc_ctas_per_sm_max() >= 2 && tc_plan_for(fmt, n, k, m, 2, pl)) return true;
+  return tc_plan_for(fmt, n, k, m, 1, pl);
 }
 
 template <int FMT, int EPI>
