@@ -362,3 +362,43 @@ def test_native_prefill_skips_padding_tiles(fmt):
         assert (a - r).abs().max() <= 2 ** -5 * r.abs().max(), f"{fmt} stream {b}: cache rows differ"
     assert torch.isfinite(h_nat).all()
     assert (h_nat - h_eag).abs().max() <= 2 ** -5 * h_eag.abs().max()
+
+
+@pytest.mark.parametrize("fmt,B", [("fp8", 16), ("nvfp4", 1), ("nvfp4", 8)])
+def test_lm_head_argmax_full_vocab(fmt, B):
+    """The lm_head over the full 100352-row vocabulary with the fused argmax:
+    at 16 rows the tensor-core GEMM on 296 persistent CTAs (two per SM), at 1
+    and 8 rows (NVFP4) the block-scaled kernel.  Every CTA's partial best
+    meets in one token per row, which must be the first maximum of the bf16
+    logits the same launch wrote (torch's argmax rule); the logits must match
+    bf16(bf16(RMSNorm(h) W^T) / 8) over the dequantised weight."""
+    import ctypes as C
+
+    from starling_b200 import quant
+    from starling_b200.engine import GraniteDims
+
+    V, H = 100352, 512
+    d = GraniteDims(hidden=H, n_q=4, n_kv=2, inter=1024, vocab=V, layers=1)
+    g = torch.Generator(device="cuda").manual_seed(11)
+    w = {}
+    for name, shape in [("embed_tokens.weight", (V, H)), ("norm.weight", (H,)),
+                        ("layers.0.input_layernorm.weight", (H,)), ("layers.0.post_attention_layernorm.weight", (H,)),
+                        ("layers.0.self_attn.q_proj.weight", (512, H)), ("layers.0.self_attn.k_proj.weight", (256, H)),
+                        ("layers.0.self_attn.v_proj.weight", (256, H)), ("layers.0.self_attn.o_proj.weight", (H, 512)),
+                        ("layers.0.mlp.gate_proj.weight", (1024, H)), ("layers.0.mlp.up_proj.weight", (1024, H)),
+                        ("layers.0.mlp.down_proj.weight", (H, 1024))]:
+        w[name] = (torch.randn(shape, generator=g, device="cuda") * (0.05 if len(shape) == 2 else 1.0)).to(torch.bfloat16)
+    eng = GraniteEngine(d, w, fmt, max_cache_len=64, max_batch=B)
+    st = eng.new_state(B, 1, _lib.SB_MODE_FIRST, out_steps=1)
+    st.hidden.copy_(torch.randn(B, H, generator=torch.Generator(device="cuda").manual_seed(4), device="cuda"))
+    _lib.check(eng.lib.sb_lm_head_argmax(C.byref(eng.cmodel), C.byref(st.c), 0, _lib.current_stream()),
+               "sb_lm_head_argmax")
+    torch.cuda.synchronize()
+    logits = st.logits[:B].float()
+    assert torch.equal(st.out_ids[:B], logits.argmax(-1))
+    h = st.hidden[:B].float()
+    xn = (h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + d.eps)).to(torch.bfloat16).float()
+    xn = (w["norm.weight"].float() * xn).to(torch.bfloat16).float()
+    wd = quant.dequantize(fmt, quant.quantize(fmt, w["embed_tokens.weight"]))
+    ref = ((xn @ wd.T).to(torch.bfloat16).float() / d.logits_scaling).to(torch.bfloat16).float()
+    assert (logits - ref).abs().max() <= 2.0 ** -6 * ref.abs().max()

@@ -236,6 +236,21 @@ def test_nvfp4_path_switch():
         lib.sb_set_nvfp4_path(prev)
 
 
+def test_linear_tensor_cores_many_tiles_two_ctas_per_sm():
+    """A matrix of hundreds of 128-row tiles at 48 rows: the persistent plan
+    with two CTAs per SM (296 CTAs, half the ring and TMEM each), fp8 and
+    bf16, vs the fp32 reference."""
+    for fmt in ("fp8", "bf16"):
+        n, k, m = 90000, 256, 48
+        w = _w(n, k, seed=17)
+        x = torch.randn(m, k, generator=torch.Generator().manual_seed(9)).to(BF16)
+        p = _to_dev(pack.pack_matrix(w, fmt, tc=True))
+        p.w_tc = p.w_tc.cuda()
+        y = _linear_tc(p, x.cuda())
+        ref = (x.float() @ _oracle_dense(w, fmt).T).to(BF16)
+        _close_bf16(y.cpu(), ref)
+
+
 def test_linear_tensor_cores_wide_range_rows():
     """fp8 activation split: rows spanning many binades (and an all-zero row)
     still match the fp32 reference."""
