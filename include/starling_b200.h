@@ -162,7 +162,8 @@ size_t sb_workspace_bytes(const SbModel* model, int32_t tokens);
  * the mma.sync GEMV; SB_NVFP4_BLOCK_SCALED: the block-scaled
  * kernel for every shape it serves; SB_NVFP4_MMA_SYNC: always the GEMV.
  * Decided when a launch is issued (a captured graph keeps the kernels it
- * recorded).  Returns the previous mode, or SB_ERR_ARG. */
+ * recorded); workspaces from sb_workspace_bytes fit every choice.  Returns the
+ * previous mode, or SB_ERR_ARG. */
 #define SB_NVFP4_AUTO 0
 #define SB_NVFP4_BLOCK_SCALED 1
 #define SB_NVFP4_MMA_SYNC 2

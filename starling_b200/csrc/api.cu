@@ -230,17 +230,28 @@ static LmWork lm_work(const SbModel* md, int tokens, void* base) {
   DecPlan pl;
   TcPlan tp;
   BsPlan bp;
+  const GemvCfg c = gemv_pick(l.fmt, l.n_pad, l.k, tokens);
+  const int gemv_ctas = gemv_grid(c, l.n_pad / 16) / c.ck;
+  const bool dec = tokens <= 8 && dec_plan_for(l.fmt, l.n_pad / 16, l.k, tokens, pl);
+  const bool tc = tc_plan_for(l, tokens, tp);
   if (bs_serves(l, tokens, bp)) {
     w.n_ctas = bp.n_ctas;
-  } else if (tokens <= 8 && dec_plan_for(l.fmt, l.n_pad / 16, l.k, tokens, pl)) {
+  } else if (dec) {
     w.n_ctas = pl.n_ctas;
-  } else if (tc_plan_for(l, tokens, tp)) {
+  } else if (tc) {
     w.n_ctas = tp.n_ctas;
   } else {
-    const GemvCfg c = gemv_pick(l.fmt, l.n_pad, l.k, tokens);
-    w.n_ctas = gemv_grid(c, l.n_pad / 16) / c.ck;
+    w.n_ctas = gemv_ctas;
   }
-  const size_t pv = static_cast<size_t>(w.n_ctas) * tokens * 4;
+  // the partials are sized for the largest grid any kernel choice could use
+  // (sb_set_nvfp4_path may change the choice after a state was sized)
+  int n_max = gemv_ctas;
+  if (dec && pl.n_ctas > n_max) n_max = pl.n_ctas;
+  if (tc && tp.n_ctas > n_max) n_max = tp.n_ctas;
+  BsPlan bq;
+  if (l.fmt == SB_FMT_NVFP4 && l.w_bs && bs_plan(l.n, l.k, tokens, bq) && bq.n_ctas > n_max) n_max = bq.n_ctas;
+  if (w.n_ctas > n_max) n_max = w.n_ctas;
+  const size_t pv = static_cast<size_t>(n_max) * tokens * 4;
   char* b = static_cast<char*>(base);
   w.counter = reinterpret_cast<int*>(b);
   w.val = reinterpret_cast<float*>(b + 256);

@@ -8,6 +8,7 @@ ncu summaries under profiles/ are captured on).
     python -m starling_b200.kernel_bench step --workload b48 --layers 4   # one eager step in NVTX range "step"
     python -m starling_b200.kernel_bench step --workload b1 --path fused  # the one-launch fused step
     python -m starling_b200.kernel_bench prefill --layers 40       # one native prefill of the b48 prompts
+    python -m starling_b200.kernel_bench verify --layers 40        # one 8-token verify forward, B=1, NVFP4
 
 Workloads (same as bench.py): b48 = 48 streams, FP8 weights, prompts
 U[300,900]; b1 = one stream, NVFP4 weights, 320 prompt positions.  Weights are
@@ -176,6 +177,45 @@ def cmd_prefill(a) -> None:
           f"{a.layers} layers: {e0.elapsed_time(e1):.1f} ms")
 
 
+def cmd_verify(a) -> None:
+    """One graphed verify forward of 8 draft tokens at B = 1 (NVFP4, cache of
+    600 positions: the speculative-verify workload) on each NVFP4 kernel
+    choice, and its per-op times."""
+    dev = torch.device("cuda")
+    d = GraniteDims(layers=a.layers)
+    w = syn.make_weights(d, seed=0, device=dev)
+    eng = GraniteEngine(d, w, "nvfp4", max_cache_len=640, max_batch=1, device=dev)
+    del w
+    torch.cuda.empty_cache()
+    eng.kv.normal_(generator=torch.Generator(device="cuda").manual_seed(1))
+    st = eng.new_state(1, 8, _lib.SB_MODE_VERIFY, out_steps=1)
+    st.ids.copy_(torch.randint(0, d.vocab, (8,), generator=torch.Generator().manual_seed(2)).to(dev))
+    lib = eng.lib
+    prev = lib.sb_set_nvfp4_path(_lib.SB_NVFP4_AUTO)
+    try:
+        for name, path in (("auto", _lib.SB_NVFP4_AUTO), ("mma_sync", _lib.SB_NVFP4_MMA_SYNC)):
+            lib.sb_set_nvfp4_path(path)
+            ops = []
+            for op, opname in enumerate(OPS):
+                def run(op=op):
+                    for layer in range(d.layers):
+                        check(lib.sb_decode_op(C.byref(eng.cmodel), C.byref(st.c), layer, op, 0,
+                                               _lib.current_stream()))
+                st.set_slot(600, pad_len=600)
+                ops.append(f"{opname} {_graph_time(run) / d.layers:.2f}")
+            st.set_slot(600, pad_len=600)
+            lm = _graph_time(lambda: check(lib.sb_decode_op(C.byref(eng.cmodel), C.byref(st.c), 0,
+                                                            _lib.SB_OP_LM_HEAD, 0, _lib.current_stream())))
+            eng.step_path = "ops"
+            st.set_slot(600, pad_len=600)
+            full = _graph_time(lambda: eng.decode_step(st, 0))
+            eng.step_path = "auto"
+            print(f"verify 8 tokens, cache 600, {d.layers} layers, NVFP4 {name}: forward {full:.1f} us "
+                  f"(per launch: {', '.join(ops)}, lm_head {lm:.2f} us)")
+    finally:
+        lib.sb_set_nvfp4_path(prev)
+
+
 def cmd_linear(a) -> None:
     lib = _lib.load()
     lib.sb_set_nvfp4_path({"auto": _lib.SB_NVFP4_AUTO, "block_scaled": _lib.SB_NVFP4_BLOCK_SCALED,
@@ -213,6 +253,8 @@ def main(argv=None) -> None:
     p = sub.add_parser("attention")
     p.add_argument("--batch", type=int, default=48)
     p.add_argument("--reps", type=int, default=20)
+    p = sub.add_parser("verify")
+    p.add_argument("--layers", type=int, default=40)
     p = sub.add_parser("prefill")
     p.add_argument("--layers", type=int, default=40)
     p = sub.add_parser("linear")
@@ -225,7 +267,8 @@ def main(argv=None) -> None:
                    help="kernel for 1..8-row NVFP4 launches (sb_set_nvfp4_path)")
     a = ap.parse_args(argv)
     torch.set_grad_enabled(False)
-    {"ops": cmd_ops, "step": cmd_step, "attention": cmd_attention, "linear": cmd_linear, "prefill": cmd_prefill}[a.cmd](a)
+    {"ops": cmd_ops, "step": cmd_step, "attention": cmd_attention, "linear": cmd_linear, "prefill": cmd_prefill,
+     "verify": cmd_verify}[a.cmd](a)
 
 
 if __name__ == "__main__":
