@@ -65,7 +65,7 @@ struct PfArgs {
   float attn_mult;
 };
 
-__global__ void __launch_bounds__(kPfThreads, 1) k_attn_prefill(const __grid_constant__ PfArgs a) {
+__global__ void __launch_bounds__(kPfThreads, 2) k_attn_prefill(const __grid_constant__ PfArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint16_t* qs = reinterpret_cast<uint16_t*>(smem);  // [128][136]
   uint16_t* ksm = qs + kPfRows * kPfStride;           // [2][64][136]
@@ -121,10 +121,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_attn_prefill(const __grid_con
   const int wkt = wlast / kPfKeys + 1;
   cp_wait_all();
   __syncthreads();
-  uint32_t qf[8][4];
-#pragma unroll
-  for (int ks = 0; ks < 8; ++ks)
-    ldsm4(s32(qs + (r0 + (lane & 7) + 8 * ((lane >> 3) & 1)) * kPfStride + ks * 16 + 8 * (lane >> 4)), qf[ks]);
+  // this warp's Q rows, read again from shared memory at every k-step (keeps
+  // the registers of two CTAs per SM)
+  const uint32_t qaddr = s32(qs + (r0 + (lane & 7) + 8 * ((lane >> 3) & 1)) * kPfStride + 8 * (lane >> 4));
 
   float sacc[8][4];
   // rounded, masked scores of key tile kt (K in kbuf) -> sacc
@@ -134,14 +133,18 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_attn_prefill(const __grid_con
 #pragma unroll
       for (int j = 0; j < 4; ++j) sacc[nt][j] = 0.f;
 #pragma unroll
-    for (int ks = 0; ks < 8; ks += 2)
+    for (int ks = 0; ks < 8; ks += 2) {
+      uint32_t qa[4], qb2[4];
+      ldsm4(qaddr + ks * 32, qa);
+      ldsm4(qaddr + (ks + 1) * 32, qb2);
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt) {
         uint32_t bfr[4];  // B fragments of k-steps ks and ks + 1 for keys 8 nt ..
         ldsm4(s32(kbuf + (nt * 8 + (lane & 7)) * kPfStride + ks * 16 + 8 * (lane >> 3)), bfr);
-        mma_bf16(sacc[nt], qf[ks], bfr[0], bfr[1]);
-        mma_bf16(sacc[nt], qf[ks + 1], bfr[2], bfr[3]);
+        mma_bf16(sacc[nt], qa, bfr[0], bfr[1]);
+        mma_bf16(sacc[nt], qb2, bfr[2], bfr[3]);
       }
+    }
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
