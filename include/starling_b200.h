@@ -222,9 +222,11 @@ int sb_lm_head_argmax(const SbModel* model, const SbState* state, int32_t step, 
 /* sb_lm_head_argmax for callers that cannot allocate device memory (no
  * device allocator of their own, or cudaMalloc forbidden because it
  * synchronises the device).  No counterpart in the reference.  Same inputs
- * and outputs as sb_lm_head_argmax; state->workspace is ignored: the scratch
- * is a fixed 256 KiB device array inside the library (held on every GPU that
- * loads it until exit).  Calls whose scratch would exceed it return
+ * and outputs as sb_lm_head_argmax; state->workspace is ignored and may be
+ * NULL: the scratch is a fixed 256 KiB device array inside the library (held
+ * on every GPU that loads it until exit).  Only the lm_head launch's own
+ * scratch must fit (its argmax partials, plus its activation operand when the
+ * lm_head runs on the tensor-core GEMM); calls where it would not return
  * SB_ERR_CONFIG.  The first call on a device looks up the array's device
  * address; make that first call before any stream capture.  Calls share the
  * array: calls that overlap on the GPU race. */

@@ -28,6 +28,8 @@ weight: ``y = bf16(x.float() @ W_deq.T)``.
 from __future__ import annotations
 
 import math
+import os
+from concurrent.futures import ThreadPoolExecutor
 from dataclasses import dataclass, field
 from typing import Optional
 
@@ -194,14 +196,27 @@ def repeat_kv(x: torch.Tensor, n_rep: int) -> torch.Tensor:
 # model
 # --------------------------------------------------------------------------- #
 class OracleModel:
-    def __init__(self, d: Dims, weights: dict, fmt: str = "bf16"):
+    """The decoder's weights as the oracle uses them.  Quantised formats are
+    quantised and dequantised here (numpy); with ``workers`` > 1 the layers are
+    built on a thread pool (numpy releases the GIL inside its array
+    operations; each layer is independent, so the result is the same)."""
+
+    def __init__(self, d: Dims, weights: dict, fmt: str = "bf16", workers: Optional[int] = None):
         self.d = d
         self.fmt = fmt
         self.embed = weights["embed_tokens.weight"]
         self.final_norm = weights["norm.weight"]
-        self.layers = [make_layer(d, weights, i, fmt) for i in range(d.layers)]
-        # lm_head is tied to the embedding (BASELINE: tied lm_head).
-        self.lm_head = Linear(self.embed, fmt)
+        if workers is None:
+            workers = min(os.cpu_count() or 1, 16) if fmt != "bf16" and d.layers > 2 else 1
+        if workers > 1:
+            with ThreadPoolExecutor(workers) as ex:
+                head = ex.submit(Linear, self.embed, fmt)
+                self.layers = list(ex.map(lambda i: make_layer(d, weights, i, fmt), range(d.layers)))
+                self.lm_head = head.result()
+        else:
+            self.layers = [make_layer(d, weights, i, fmt) for i in range(d.layers)]
+            # lm_head is tied to the embedding.
+            self.lm_head = Linear(self.embed, fmt)
 
 
 class OracleCache:

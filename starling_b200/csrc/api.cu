@@ -202,7 +202,9 @@ static int attn_split(int groups, int max_len) {
   return s < 1 ? 1 : (s > 8 ? 8 : s);
 }
 
-static int check_state(const SbModel* md, const SbState* st) {
+// need_workspace = false: the caller supplies the scratch itself
+// (sb_lm_head_argmax_static), so state->workspace may be NULL.
+static int check_state(const SbModel* md, const SbState* st, bool need_workspace = true) {
   if (!md || !st) return fail(SB_ERR_ARG, "null model/state");
   if (st->batch < 1 || st->m < 1 || st->batch * st->m > 64)
     return fail(SB_ERR_ARG, "batch*m must be in [1, 64] (batch=%d m=%d)", st->batch, st->m);
@@ -210,7 +212,7 @@ static int check_state(const SbModel* md, const SbState* st) {
   if (md->head_dim != 128) return fail(SB_ERR_ARG, "head_dim must be 128");
   if (md->n_q % md->n_kv != 0 || (md->n_q / md->n_kv) * st->m > 64)
     return fail(SB_ERR_ARG, "query rows per KV head (n_q/n_kv * m) must be <= 64");
-  if (!st->ids || !st->ctrl || !st->hidden || !st->q || !st->attn || !st->act || !st->workspace)
+  if (!st->ids || !st->ctrl || !st->hidden || !st->q || !st->attn || !st->act || (need_workspace && !st->workspace))
     return fail(SB_ERR_ARG, "state buffer missing");
   if (st->mode < SB_MODE_DECODE || st->mode > SB_MODE_FIRST) return fail(SB_ERR_ARG, "bad mode");
   return 0;
@@ -224,7 +226,11 @@ struct LmWork {
   size_t bytes;
 };
 
-static LmWork lm_work(const SbModel* md, int tokens, void* base) {
+// exact = false: the partials are sized for the largest grid any kernel choice
+// could use, so a workspace sized once stays valid when sb_set_nvfp4_path
+// changes the choice later; exact = true: for the launch about to be issued
+// only (scratch sized per call).
+static LmWork lm_work(const SbModel* md, int tokens, void* base, bool exact = false) {
   const SbLinear& l = md->lm_head;
   LmWork w;
   DecPlan pl;
@@ -243,13 +249,12 @@ static LmWork lm_work(const SbModel* md, int tokens, void* base) {
   } else {
     w.n_ctas = gemv_ctas;
   }
-  // the partials are sized for the largest grid any kernel choice could use
-  // (sb_set_nvfp4_path may change the choice after a state was sized)
   int n_max = gemv_ctas;
   if (dec && pl.n_ctas > n_max) n_max = pl.n_ctas;
   if (tc && tp.n_ctas > n_max) n_max = tp.n_ctas;
   BsPlan bq;
   if (l.fmt == SB_FMT_NVFP4 && l.w_bs && bs_plan(l.n, l.k, tokens, bq) && bq.n_ctas > n_max) n_max = bq.n_ctas;
+  if (exact) n_max = w.n_ctas;
   if (w.n_ctas > n_max) n_max = w.n_ctas;
   const size_t pv = static_cast<size_t>(n_max) * tokens * 4;
   char* b = static_cast<char*>(base);
@@ -312,9 +317,26 @@ static int run_norm(const SbModel* md, const SbState* st, const uint16_t* x, boo
   return 0;
 }
 
-static int launch_lm_head(const SbModel* md, const SbState* st, int step, cudaStream_t s) {
+// Scratch of the lm_head launch alone: [argmax partials | 256-byte aligned
+// tensor-core operand of the lm_head (only when the lm_head takes that path)].
+struct LmLayout {
+  size_t tc_off, tc_bytes, total;
+};
+static LmLayout lm_layout(const SbModel* md, int tokens) {
+  LmLayout w;
+  const size_t lm = lm_work(md, tokens, nullptr, true).bytes;
+  w.tc_off = (lm + 255) & ~size_t(255);
+  w.tc_bytes = tc_scratch_need(md->lm_head, tokens);
+  w.total = w.tc_bytes ? w.tc_off + w.tc_bytes : lm;
+  return w;
+}
+
+// lm_only: the state's workspace holds only lm_layout() (argmax partials,
+// then the lm_head's own tensor-core operand) instead of the step's whole
+// ws_layout().
+static int launch_lm_head(const SbModel* md, const SbState* st, int step, cudaStream_t s, bool lm_only = false) {
   const int T = st->batch * st->m;
-  LmWork w = lm_work(md, T, st->workspace);
+  LmWork w = lm_work(md, T, st->workspace, lm_only);
   if (w.bytes > st->workspace_bytes) return fail(SB_ERR_ARG, "workspace too small (%zu < %zu)", st->workspace_bytes, w.bytes);
   GemvParams p = base_params(md->lm_head, T);
   p.pro = PRO_RMSNORM;
@@ -323,7 +345,15 @@ static int launch_lm_head(const SbModel* md, const SbState* st, int step, cudaSt
   p.eps = md->eps;
   size_t tcb = 0;
   void* tcs = nullptr;
-  SB_TRY(tc_scratch_of(md, st, tcs, tcb));
+  if (lm_only) {
+    const LmLayout lw = lm_layout(md, T);
+    if (st->workspace_bytes < lw.total)
+      return fail(SB_ERR_ARG, "workspace too small (%zu < %zu)", st->workspace_bytes, lw.total);
+    tcs = lw.tc_bytes ? static_cast<char*>(st->workspace) + lw.tc_off : nullptr;
+    tcb = lw.tc_bytes;
+  } else {
+    SB_TRY(tc_scratch_of(md, st, tcs, tcb));
+  }
   TcPlan tp;
   const bool tc = tcs && tc_plan_for(md->lm_head, T, tp);
   if (T > kFusedNormMaxRows && !tc) {
@@ -618,6 +648,16 @@ static PrefillWs prefill_ws(const SbModel* md, int B, int T, void* base) {
   return w;
 }
 
+// A prefill block of `rows` token rows runs each projection on the tcgen05
+// GEMM (tile copy present and the shape served), else on the GEMV kernels,
+// which compute every fused epilogue (RoPE + cache write, SwiGLU, residual)
+// for up to 64 rows in one launch (one row chunk per CTA).
+static const int kPrefillGemvMaxRows = 64;
+static bool prefill_rows_served(const SbLinear& l, int rows) {
+  TcPlan pl;
+  return rows <= kPrefillGemvMaxRows || tc_plan_for(l, rows, pl);
+}
+
 static int check_prefill(const SbModel* md, int B, int T) {
   if (!md || !md->layers || md->n_layers < 1) return fail(SB_ERR_ARG, "sb_prefill: no model");
   if (B < 1 || B > md->max_batch) return fail(SB_ERR_ARG, "sb_prefill: batch %d outside [1, %d]", B, md->max_batch);
@@ -633,11 +673,10 @@ static int check_prefill(const SbModel* md, int B, int T) {
     const SbLayer& L = md->layers[l];
     const SbLinear* lins[4] = {&L.qkv, &L.o, &L.gate_up, &L.down};
     for (const SbLinear* x : lins) {
-      TcPlan pl;
       if (!lin_ok(*x)) return fail(SB_ERR_ARG, "sb_prefill: layer %d: bad packed linear", l);
-      if (!tc_plan_for(*x, rows, pl) || (tail && !tc_plan_for(*x, tail, pl)))
-        return fail(SB_ERR_CONFIG, "sb_prefill: layer %d: the tensor-core GEMM does not serve blocks of %d / %d "
-                    "rows (no tile copy, or too few rows for this format)", l, rows, tail);
+      if (!prefill_rows_served(*x, rows) || (tail && !prefill_rows_served(*x, tail)))
+        return fail(SB_ERR_CONFIG, "sb_prefill: layer %d: blocks of %d / %d rows need the tensor-core tile copy "
+                    "of every projection (more than %d rows)", l, rows, tail, kPrefillGemvMaxRows);
     }
   }
   return 0;
@@ -816,47 +855,50 @@ int sb_attention(const SbModel* md, const SbState* st, int32_t layer, sb_stream_
 // only this C ABI and owns no device allocator, or a latency-critical serving
 // loop that forbids cudaMalloc because it synchronises the whole device and
 // may fail once another framework has reserved the HBM pool.  This variant of
-// sb_lm_head_argmax keeps its argmax partials and completion counter in a
-// fixed file-scope device array instead of state->workspace.  The array is
-// kStaticLmScratchBytes (256 KiB) and lives on every GPU that loads this
-// library until the process exits.  Calls whose partials would not fit are
-// rejected.  All calls share the array, so two calls that overlap on the GPU
-// (different streams, or two processes' kernels interleaved through one
-// context) race: serialise them.
+// sb_lm_head_argmax keeps the lm_head launch's scratch (argmax partials,
+// completion counter and, on the tensor-core path, the lm_head's activation
+// operand) in a fixed file-scope device array instead of state->workspace,
+// which may be NULL.  The array is kStaticLmScratchBytes (256 KiB) and lives
+// on every GPU that loads this library until the process exits.  Calls whose
+// lm_head scratch would not fit are rejected.  All calls share the array, so
+// two calls that overlap on the GPU (different streams, or two processes'
+// kernels interleaved through one context) race: serialise them.
 // ---------------------------------------------------------------------------
 namespace {
 constexpr size_t kStaticLmScratchBytes = 256 * 1024;
 __device__ __align__(256) unsigned char g_lm_scratch[kStaticLmScratchBytes];
 constexpr int kMaxDevices = 64;
-void* g_lm_scratch_addr[kMaxDevices] = {};  // device address of g_lm_scratch per device
+// device address of g_lm_scratch per device, looked up once per device
+std::atomic<void*> g_lm_scratch_addr[kMaxDevices] = {};
 }  // namespace
 
 extern "C" int sb_lm_head_argmax_static(const SbModel* md, const SbState* st, int32_t step, sb_stream_t stream) {
-  SB_TRY(check_state(md, st));
+  SB_TRY(check_state(md, st, false));
   if (!lin_ok(md->lm_head)) return fail(SB_ERR_ARG, "bad lm_head");
+  const int T = st->batch * st->m;
+  const size_t need = lm_layout(md, T).total;
+  if (need > kStaticLmScratchBytes)
+    return fail(SB_ERR_CONFIG,
+                "sb_lm_head_argmax_static: %d token rows need %zu lm_head scratch bytes, more than the fixed %zu; "
+                "use sb_lm_head_argmax with a caller workspace",
+                T, need, kStaticLmScratchBytes);
   int dev = 0;
   SB_TRY(cudaGetDevice(&dev));
   if (dev < 0 || dev >= kMaxDevices) return fail(SB_ERR_ARG, "device index %d out of range", dev);
   // one-time set-up per device (this device is current): host code must use
-  // the symbol's device address, never &g_lm_scratch, which is a host stand-in
-  if (!g_lm_scratch_addr[dev]) {
-    void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_lm_scratch);
+  // the symbol's device address, never &g_lm_scratch, which is a host stand-in.
+  // Two threads racing here both store the same address.
+  void* base = g_lm_scratch_addr[dev].load(std::memory_order_acquire);
+  if (!base) {
+    const cudaError_t e = cudaGetSymbolAddress(&base, g_lm_scratch);
     if (e != cudaSuccess) return fail(e, "cudaGetSymbolAddress(g_lm_scratch): %s", cudaGetErrorString(e));
-    g_lm_scratch_addr[dev] = p;
+    g_lm_scratch_addr[dev].store(base, std::memory_order_release);
   }
-  const int T = st->batch * st->m;
-  const size_t need = ws_layout(md, T).total;
-  if (need > kStaticLmScratchBytes)
-    return fail(SB_ERR_CONFIG,
-                "sb_lm_head_argmax_static: %d token rows need %zu scratch bytes, more than the fixed %zu; "
-                "use sb_lm_head_argmax with a caller workspace",
-                T, need, kStaticLmScratchBytes);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   // the completion counter (first 256 bytes) must start at zero on every call
-  SB_TRY(cudaMemsetAsync(g_lm_scratch_addr[dev], 0, 256, s));
+  SB_TRY(cudaMemsetAsync(base, 0, 256, s));
   SbState local = *st;
-  local.workspace = g_lm_scratch_addr[dev];
+  local.workspace = base;
   local.workspace_bytes = kStaticLmScratchBytes;
-  return launch_op(md, &local, 0, SB_OP_LM_HEAD, step, s);
+  return launch_lm_head(md, &local, step, s, true);
 }

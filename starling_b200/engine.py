@@ -1,5 +1,5 @@
 """GraniteEngine: packed weights, static KV cache and device state for the
-native decode path, plus the (torch) prefill that fills the cache.
+native decode path, plus the prefill that fills the cache (``sb_prefill``).
 
 The decode / verify forward itself is one C-ABI call per step
 (``sb_decode_step``) issuing the fused sm_100a kernels; everything it reads
@@ -14,7 +14,6 @@ from dataclasses import dataclass, fields
 from typing import Optional
 
 import torch
-import torch.nn.functional as F
 
 from . import _lib
 from ._lib import SB_CTRL_PADLEN, SB_CTRL_SLOT, SB_CTRL_WORDS, SbLayer, SbModel, SbState, check, ptr
@@ -237,7 +236,7 @@ class GraniteEngine:
             out = out[self._inverse_perm(p)]
         return out
 
-    # ---- prefill (torch on the GPU, the reference's eager semantics) -------- #
+    # ---- single linears and prefill --------------------------------------- #
     def linear(self, x: torch.Tensor, p: PackedLinear) -> torch.Tensor:
         """y = x W^T through the native dequant-GEMV (any number of rows; fp32
         accumulation over the exactly dequantised weight).  Output columns in
@@ -265,35 +264,22 @@ class GraniteEngine:
         return inv
 
     @torch.inference_mode()
-    def prefill(self, inputs_embeds: torch.Tensor, prompt_lengths: Optional[torch.Tensor] = None,
-                chunk_streams: int = 8, native: Optional[bool] = None) -> torch.Tensor:
+    def prefill(self, inputs_embeds: torch.Tensor, prompt_lengths: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Prefill over ``inputs_embeds`` (B, T, H) (before the x12 embedding
         multiplier), writing cache slots [0, T) of streams 0..B-1: the
         ``GraniteModel.forward`` with a causal (+ right-padding) mask of
-        llm_mega.py:176-202 / batched.py:222-276.  Returns the last real
-        position's hidden row per stream, before the final norm: (B, H).
-
-        native=None: the library's ``sb_prefill`` when every projection has a
-        tensor-core tile copy that serves the shape, else the eager path below
-        (torch attention and glue, projections through ``sb_linear_ex``);
-        native=True requires the former, native=False forces the latter."""
+        llm_mega.py:176-202 / batched.py:222-276, run by the library's
+        ``sb_prefill``.  Returns the last real position's hidden row per
+        stream, before the final norm: (B, H).  Raises ``StarlingError`` where
+        the library does not serve the shape (there is no other path)."""
+        d = self.dims
         B, T, _ = inputs_embeds.shape
         if T >= self.max_cache_len:
             raise ValueError(f"prompt {T} >= max_cache_len {self.max_cache_len}")
-        if native is not False:
-            out = self._prefill_native(inputs_embeds, prompt_lengths, required=native is True)
-            if out is not None:
-                return out
-        return self._prefill_eager(inputs_embeds, prompt_lengths, chunk_streams)
-
-    def _prefill_native(self, inputs_embeds, prompt_lengths, required: bool):
-        d = self.dims
-        B, T, _ = inputs_embeds.shape
         Tp = (T + 7) // 8 * 8  # sb_prefill takes whole query blocks of 8 positions
         if Tp > self.max_cache_len or B > self.max_batch:
-            if required:
-                raise ValueError(f"native prefill needs T rounded to 8 ({Tp}) <= max_cache_len and B <= max_batch")
-            return None
+            raise ValueError(f"prefill needs T rounded up to 8 ({Tp}) <= max_cache_len {self.max_cache_len} "
+                             f"and B ({B}) <= max_batch {self.max_batch}")
         dev = self.device
         hidden = torch.zeros(B, Tp, d.hidden, dtype=BF16, device=dev)
         hidden[:, :T] = inputs_embeds.to(dev, BF16) * d.emb_mult
@@ -309,67 +295,10 @@ class GraniteEngine:
         attn = torch.empty_like(q)
         act = torch.empty(rows, d.inter, dtype=BF16, device=dev)
         ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)
-        rc = self.lib.sb_prefill(m, ptr(hidden), B, Tp, ptr(pl), ptr(q), ptr(attn), ptr(act), ptr(ws), ws_bytes,
-                                 _lib.current_stream())
-        if rc == 1002 and not required:  # SB_ERR_CONFIG: a projection is not served by the tensor-core GEMM
-            return None
-        check(rc, "sb_prefill")
+        check(self.lib.sb_prefill(m, ptr(hidden), B, Tp, ptr(pl), ptr(q), ptr(attn), ptr(act), ptr(ws), ws_bytes,
+                                  _lib.current_stream()), "sb_prefill")
         last = (pl.long() - 1) if pl is not None else torch.full((B,), T - 1, device=dev)
         return hidden[torch.arange(B, device=dev), last, :].contiguous()
-
-    def _prefill_eager(self, inputs_embeds, prompt_lengths, chunk_streams):
-        d = self.dims
-        B, T, _ = inputs_embeds.shape
-        dev = self.device
-        hidden = inputs_embeds.to(dev, BF16) * d.emb_mult
-        pl = None if prompt_lengths is None else prompt_lengths.to(dev).long()
-        cos = self.rope_cos[:T].repeat(1, 2)[None, None]  # (1,1,T,128)
-        sin = self.rope_sin[:T].repeat(1, 2)[None, None]
-        kpos = torch.arange(T, device=dev)
-        valid = kpos[None, :] <= kpos[:, None]  # (T q, T k)
-        valid = valid[None].expand(B, T, T)
-        if pl is not None:
-            valid = valid & (kpos[None, None, :] < pl[:, None, None])
-        neg = torch.finfo(BF16).min
-        mask = torch.zeros(B, 1, T, T, dtype=BF16, device=dev).masked_fill_(~valid[:, None], neg)
-        G = d.n_q // d.n_kv
-        half = d.head_dim // 2
-
-        def rot(x):
-            return torch.cat((-x[..., half:], x[..., :half]), dim=-1)
-
-        for li, L in enumerate(self.layers):
-            residual = hidden
-            xf = hidden.float()
-            normed = L["in_norm"] * (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + d.eps)).to(BF16)
-            qkv = self.linear(normed, L["qkv"])
-            q, k, v = qkv.split([d.n_q * 128, d.n_kv * 128, d.n_kv * 128], dim=-1)
-            q = q.reshape(B, T, d.n_q, 128).transpose(1, 2)
-            k = k.reshape(B, T, d.n_kv, 128).transpose(1, 2)
-            v = v.reshape(B, T, d.n_kv, 128).transpose(1, 2)
-            q = q * cos + rot(q) * sin
-            k = k * cos + rot(k) * sin
-            self.kv[li, 0, :B, :, :T] = k
-            self.kv[li, 1, :B, :, :T] = v
-            outs = []
-            for b0 in range(0, B, chunk_streams):
-                b1 = min(B, b0 + chunk_streams)
-                kr = k[b0:b1].repeat_interleave(G, dim=1)
-                vr = v[b0:b1].repeat_interleave(G, dim=1)
-                sc = torch.matmul(q[b0:b1], kr.transpose(2, 3)) * d.attn_mult + mask[b0:b1]
-                pr = F.softmax(sc, dim=-1, dtype=torch.float32).to(BF16)
-                outs.append(torch.matmul(pr, vr))
-            ao = torch.cat(outs).transpose(1, 2).reshape(B, T, d.n_q * 128)
-            hidden = residual + self.linear(ao, L["o"]) * d.res_mult
-            residual = hidden
-            xf = hidden.float()
-            normed = L["post_norm"] * (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + d.eps)).to(BF16)
-            gu = self.linear(normed, L["gate_up"])
-            act = F.silu(gu[..., : d.inter]) * gu[..., d.inter:]
-            hidden = residual + self.linear(act, L["down"]) * d.res_mult
-        if pl is None:
-            return hidden[:, -1, :].contiguous()
-        return hidden[torch.arange(B, device=dev), pl - 1, :].contiguous()
 
     def load_cache_from(self, k_list, v_list, batch_index: int = 0) -> None:
         """Copy externally computed K/V (per layer (n_kv, S, 128) or (B, n_kv, S, 128)) into slots [0, S)."""

@@ -312,56 +312,63 @@ def test_batched_tensor_cores_teacher_forced(golden, fmt):
                 assert ((got_r - ref_r).abs() <= bound).all(), f"layer {li} {'kv'[kv]} row differs"
 
 
-@pytest.mark.parametrize("fmt,B,T", [("bf16", 3, 24), ("fp8", 5, 40), ("nvfp4", 6, 29), ("int8", 2, 70)])
-def test_native_prefill_matches_eager(fmt, B, T):
-    """sb_prefill (every projection on the tcgen05 GEMM with its fused
-    epilogue, attention by query blocks) against the eager prefill (torch
-    attention and glue, the reference's op sequence): K/V cache rows of the
-    valid prompt positions and the returned last hidden rows, right-padded
-    batches, T not a multiple of 8 for some cases."""
+def _prefill_vs_oracle(d, w, fmt, emb, pl, max_len):
+    """sb_prefill + first-token lm_head on the GPU against the oracle's
+    prefill (GraniteModel.forward over the right-padded prompts): K/V cache
+    rows of every valid prompt position, the first-token logits and ids."""
+    B = emb.shape[0]
+    eng = GraniteEngine(d, w, fmt, max_cache_len=max_len, max_batch=B)
+    last = eng.prefill(emb.cuda(), pl)
+    st = eng.new_state(B, 1, _lib.SB_MODE_FIRST, out_steps=1)
+    st.hidden.copy_(last)
+    eng.lm_head_argmax(st)
+    torch.cuda.synchronize()
+    kv_nat = eng.kv.float().cpu()
+    odec = gr.OracleDecoder(gr.OracleModel(d, w, fmt=fmt), max_len, B=B)
+    ref_ids = odec.prefill(emb, pl)
+    for b in range(B):
+        n = int(pl[b])
+        for li in range(d.layers):
+            for kv, ref_c in ((0, odec.cache.k[li]), (1, odec.cache.v[li])):
+                got_r, ref_r = kv_nat[li, kv, b, :, :n], ref_c[b, :, :n].float()
+                assert (got_r - ref_r).abs().max() <= 2 ** -5 * ref_r.abs().max(), \
+                    f"{fmt} stream {b} layer {li} {'kv'[kv]}: cache rows differ"
+        ref = odec.last_logits[b]
+        got = st.logits[b].cpu()
+        err = (got.float() - ref.float()).abs().max()
+        assert err <= _logit_tol(ref), f"{fmt} stream {b}: first-token logits differ by {err:.4g}"
+        if _margin(ref) > _logit_tol(ref):
+            assert int(st.out_ids[b]) == int(ref_ids[b])
+
+
+@pytest.mark.parametrize("fmt,B,T", [("bf16", 3, 24), ("fp8", 5, 40), ("nvfp4", 6, 29), ("int8", 2, 70),
+                                     ("nvfp4", 1, 20), ("int8", 1, 7), ("nvfp4", 2, 33)])
+def test_native_prefill_vs_oracle(fmt, B, T):
+    """sb_prefill against the oracle for every format: right-padded batches,
+    T not a multiple of 8, and the small prompts whose projections run on the
+    GEMV kernels (NVFP4 / INT8 blocks of <= 64 rows) rather than the tcgen05
+    GEMM."""
     d = gr.TINY_DIMS
     w = gr.make_weights(d, seed=5, std=0.05, norm_jitter=0.1)
     g = torch.Generator().manual_seed(B * 100 + T)
     emb = torch.randn(B, T, d.hidden, generator=g).to(torch.bfloat16)
     pl = torch.randint(T // 2, T + 1, (B,), generator=g)
     pl[0] = T
-    eng = GraniteEngine(d, w, fmt, max_cache_len=96, max_batch=B)
-    h_nat = eng.prefill(emb.cuda(), pl, native=True).float().cpu()
-    kv_nat = eng.kv.float().cpu()
-    eng.kv.zero_()
-    h_eag = eng.prefill(emb.cuda(), pl, native=False).float().cpu()
-    kv_eag = eng.kv.float().cpu()
-    for b in range(B):
-        n = int(pl[b])
-        a, r = kv_nat[:, :, b, :, :n], kv_eag[:, :, b, :, :n]
-        assert (a - r).abs().max() <= 2 ** -5 * r.abs().max(), f"{fmt} stream {b}: cache rows differ"
-    assert (h_nat - h_eag).abs().max() <= 2 ** -5 * h_eag.abs().max()
+    _prefill_vs_oracle(d, w, fmt, emb, pl, 96)
 
 
 @pytest.mark.parametrize("fmt", ["fp8", "bf16"])
 def test_native_prefill_skips_padding_tiles(fmt):
     """Prompts of 400 / 150 / 200 positions padded to T = 400: whole 128-row
     token tiles and 8-position query blocks lie in the padding and are skipped;
-    the valid cache rows and the last hidden rows still match the eager
-    prefill."""
+    the valid cache rows and the first-token logits still match the oracle."""
     d = gr.TINY_DIMS
     w = gr.make_weights(d, seed=6, std=0.05, norm_jitter=0.1)
     B, T = 3, 400
     g = torch.Generator().manual_seed(17)
     emb = torch.randn(B, T, d.hidden, generator=g).to(torch.bfloat16)
     pl = torch.tensor([400, 150, 200])
-    eng = GraniteEngine(d, w, fmt, max_cache_len=512, max_batch=B)
-    h_nat = eng.prefill(emb.cuda(), pl, native=True).float().cpu()
-    kv_nat = eng.kv.float().cpu()
-    eng.kv.zero_()
-    h_eag = eng.prefill(emb.cuda(), pl, native=False).float().cpu()
-    kv_eag = eng.kv.float().cpu()
-    for b in range(B):
-        n = int(pl[b])
-        a, r = kv_nat[:, :, b, :, :n], kv_eag[:, :, b, :, :n]
-        assert (a - r).abs().max() <= 2 ** -5 * r.abs().max(), f"{fmt} stream {b}: cache rows differ"
-    assert torch.isfinite(h_nat).all()
-    assert (h_nat - h_eag).abs().max() <= 2 ** -5 * h_eag.abs().max()
+    _prefill_vs_oracle(d, w, fmt, emb, pl, 512)
 
 
 @pytest.mark.parametrize("fmt,B", [("fp8", 16), ("nvfp4", 1), ("nvfp4", 8)])

@@ -1,0 +1,273 @@
+"""Parity at the Granite-1B decoder's full dimensions (40 layers, hidden 2048,
+16 / 4 heads, intermediate 8192, vocabulary 100352, tied lm_head, random-init
+N(0, 0.02) weights): the native path against the CPU oracle on the workloads
+the benchmark times.
+
+* B=1 greedy decode, bf16 and NVFP4: prefill of 300 audio embeddings + 20
+  prompt ids, first-token logits, then 128 decode steps teacher-forced with the
+  oracle's greedy tokens (every step's logits compared), and the free-running
+  128-step greedy sequence of the K=8 graphed decoder (multistep.py:250-333);
+* B=48 lock-step decode, FP8, prompt lengths U[300, 900] right-padded
+  (batched.py:331-437): three teacher-forced steps of all 48 streams on the
+  tcgen05 path, from identical random caches;
+* FP8 native prefill of 4 streams with prompts U[300, 900] (batched.py:222-276);
+* one NVFP4 verify forward of 8 tokens over a 600-position cache
+  (speculative.py:598-680): logits of every row, argmaxes and accept length.
+
+Tolerance (floating point): every logit within ``RTOL * |ref| + ATOL_FRAC *
+max|ref|`` of the oracle's.  Greedy ids must be identical; a different argmax
+is accepted only where the oracle's own top-2 margin is within that tolerance
+at its top logit (a genuine near-tie), and the teacher-forced run keeps checking
+past it.
+"""
+
+import os
+
+import pytest
+import torch
+
+from oracle import granite_ref as gr
+
+pytestmark = pytest.mark.gpu
+
+if not torch.cuda.is_available():
+    pytest.skip("needs a CUDA device", allow_module_level=True)
+
+from starling_b200 import _lib  # noqa: E402
+from starling_b200.engine import GraniteEngine  # noqa: E402
+from starling_b200.multistep import MultiStepLLMMega  # noqa: E402
+
+torch.set_grad_enabled(False)
+torch.set_num_threads(min(os.cpu_count() or 1, 16))
+
+D = gr.BASELINE_DIMS
+RTOL = 1e-2
+ATOL_FRAC = 1e-2
+NO_EOS = -1
+
+
+def _tol(ref: torch.Tensor) -> torch.Tensor:
+    r = ref.float()
+    return RTOL * r.abs() + ATOL_FRAC * r.abs().max()
+
+
+def _check_logits(got: torch.Tensor, ref: torch.Tensor, what: str, stats: list) -> None:
+    g, r = got.float().cpu(), ref.float().cpu()
+    err = (g - r).abs()
+    # the smallest ATOL_FRAC this row would need (for tightening the bound)
+    need = float(((err - RTOL * r.abs()).clamp_min(0).max() / r.abs().max()))
+    stats.append(need)
+    bad = err > _tol(r)
+    assert not bad.any(), (f"{what}: {int(bad.sum())} logits outside tolerance; max err {float(err.max()):.4g}, "
+                           f"needs atol {need:.3g} x max|ref|")
+
+
+def _near_tie(ref: torch.Tensor) -> bool:
+    t = ref.float().topk(2).values
+    return float(t[0] - t[1]) <= float(_tol(ref).max())
+
+
+def _report(name: str, stats: list) -> None:
+    if stats:
+        print(f"[{name}] rows {len(stats)}: atol needed (x max|ref|) max {max(stats):.3g} "
+              f"mean {sum(stats) / len(stats):.3g}")
+
+
+_MODELS = {}
+
+
+@pytest.fixture(scope="module")
+def weights():
+    return gr.make_weights(D, seed=0, std=0.02)
+
+
+def _oracle(weights, fmt):
+    """One full-size oracle model at a time (each holds ~10 GB of fp32
+    dequantised weights for the quantised formats)."""
+    if fmt not in _MODELS:
+        _MODELS.clear()
+        _MODELS[fmt] = gr.OracleModel(D, weights, fmt=fmt)
+    return _MODELS[fmt]
+
+
+def _b1_inputs(weights):
+    """300 N(0,1) audio embeddings + the embeddings of 20 random prompt ids
+    (merged before the x12 multiplier)."""
+    g = torch.Generator().manual_seed(0)
+    audio = torch.randn(1, 300, D.hidden, generator=g).to(torch.bfloat16)
+    ids = torch.randint(0, D.vocab, (20,), generator=g)
+    return torch.cat([audio, weights["embed_tokens.weight"][ids].unsqueeze(0)], dim=1)
+
+
+@pytest.mark.parametrize("fmt", ["bf16", "nvfp4"])
+def test_b1_prefill_teacher_forced_and_greedy_128(weights, fmt):
+    emb = _b1_inputs(weights)
+    T, L, n_new = emb.shape[1], 640, 129  # first token + 128 decode steps
+    om = _oracle(weights, fmt)
+    odec = gr.OracleDecoder(om, L)
+    ref_ids, ref_logits = odec.generate(emb, n_new, NO_EOS, record_logits=True)
+    assert len(ref_ids) == n_new
+
+    eng = GraniteEngine(D, weights, fmt, max_cache_len=L, max_batch=1)
+    stats = []
+    # prefill + first token
+    st = eng.new_state(1, 1, _lib.SB_MODE_DECODE, out_steps=1)
+    last = eng.prefill(emb.cuda())
+    st.hidden.copy_(last)
+    st.set_mode(_lib.SB_MODE_FIRST)
+    eng.lm_head_argmax(st)
+    st.set_mode(_lib.SB_MODE_DECODE)
+    _check_logits(st.logits[0], ref_logits[0], f"{fmt} prefill", stats)
+    if not _near_tie(ref_logits[0]):
+        assert int(st.out_ids[0]) == ref_ids[0]
+    # 128 decode steps, each fed the oracle's greedy token of the previous step
+    ties = 0
+    for i in range(n_new - 1):
+        st.ids[0] = ref_ids[i]
+        st.set_slot(T + i, pad_len=T)
+        eng.decode_step(st, 0)
+        ref = ref_logits[i + 1]
+        _check_logits(st.logits[0], ref, f"{fmt} step {i}", stats)
+        if _near_tie(ref):
+            ties += 1
+        else:
+            assert int(st.out_ids[0]) == ref_ids[i + 1], f"{fmt} step {i}: argmax differs"
+    _report(f"b1 {fmt} teacher-forced", stats)
+
+    # the free-running K=8 graphed decoder: identical ids up to a genuine near-tie
+    dec = MultiStepLLMMega(engine=eng, steps_per_replay=8)
+    got = dec.generate(emb.cuda(), max_new_tokens=n_new, eos_token_id=NO_EOS).ids[0].tolist()
+    assert len(got) == n_new
+    for i in range(n_new):
+        if got[i] != ref_ids[i]:
+            assert _near_tie(ref_logits[i]), f"{fmt}: greedy id {i} differs ({got[i]} vs {ref_ids[i]})"
+            print(f"[b1 {fmt}] greedy sequences part at a near-tie, step {i}")
+            break
+    print(f"[b1 {fmt}] 128-step greedy: {sum(a == b for a, b in zip(got, ref_ids))}/{n_new} ids equal, "
+          f"{ties} near-ties among the teacher-forced steps")
+
+
+@pytest.mark.parametrize("fmt", ["nvfp4"])
+def test_verify_8_tokens_cache_600(weights, fmt):
+    """One verify forward: 8 token ids (last emitted + 7 drafts) at cache
+    slots 600..607 over a 600-position prefill; every row's logits, the argmax
+    per row and the accepted-prefix length (speculative.py:430-459)."""
+    g = torch.Generator().manual_seed(3)
+    emb = torch.randn(1, 600, D.hidden, generator=g).to(torch.bfloat16)
+    om = _oracle(weights, fmt)
+    odec = gr.OracleDecoder(om, 640)
+    odec.prefill(emb)
+    ids = torch.randint(0, D.vocab, (8,), generator=g)
+    ref = odec.verify(ids, 600)
+    ref_pred = ref.float().argmax(-1)
+    # make the drafts agree with the oracle for the first three positions, so
+    # the accept length is not trivially 0
+    ids[1:4] = ref_pred[0:3]
+    odec = gr.OracleDecoder(om, 640)
+    odec.prefill(emb)
+    ref = odec.verify(ids, 600)
+    ref_pred = ref.float().argmax(-1)
+    acc = 0
+    while acc < 7 and int(ref_pred[acc]) == int(ids[acc + 1]):
+        acc += 1
+
+    eng = GraniteEngine(D, {k: v for k, v in weights.items()}, fmt, max_cache_len=640, max_batch=1)
+    eng.prefill(emb.cuda())
+    st = eng.new_state(1, 8, _lib.SB_MODE_VERIFY, out_steps=1)
+    st.ids.copy_(ids.cuda())
+    st.set_slot(600, pad_len=600)
+    eng.decode_step(st, 0)
+    torch.cuda.synchronize()
+    stats = []
+    ties = [_near_tie(ref[i]) for i in range(8)]
+    for i in range(8):
+        _check_logits(st.logits[i], ref[i], f"verify row {i}", stats)
+        if not ties[i]:
+            assert int(st.out_ids[i]) == int(ref_pred[i]), f"verify row {i}: argmax differs"
+    if not any(ties[:acc + 1]):
+        assert int(st.ctrl[_lib.SB_CTRL_ACCEPT]) == acc
+    _report("verify nvfp4", stats)
+
+
+def _b48_lengths(B=48):
+    g = torch.Generator().manual_seed(0)
+    return torch.randint(300, 901, (B,), generator=g)
+
+
+def test_b48_fp8_teacher_forced_steps(weights):
+    """48 right-padded streams (prompt lengths U[300, 900], padded to the
+    longest) decode in lock step on the tcgen05 path: from identical random
+    caches (N(0,1) K/V in every stream's prompt slots), three steps of random
+    token ids; every stream's logits and argmax against the oracle, and the
+    new cache rows."""
+    fmt, B, L = "fp8", 48, 1040
+    pl = _b48_lengths(B)
+    T = int(pl.max())
+    om = _oracle(weights, fmt)
+    odec = gr.OracleDecoder(om, L, B=B)
+    g = torch.Generator().manual_seed(5)
+    for li in range(D.layers):
+        for c in (odec.cache.k[li], odec.cache.v[li]):
+            c[:, :, :T] = torch.randn(B, D.n_kv, T, D.head_dim, generator=g).to(torch.bfloat16)
+            for b in range(B):
+                c[b, :, int(pl[b]):T] = 0
+    odec.pos = T
+    eng = GraniteEngine(D, weights, fmt, max_cache_len=L, max_batch=B)
+    assert eng.layers[0]["qkv"].w_tc is not None
+    eng.load_cache_from(odec.cache.k, odec.cache.v)
+    st = eng.new_state(B, 1, _lib.SB_MODE_DECODE, out_steps=1, prompt_len=pl, rope_off=T - pl)
+    kpos = torch.arange(L)
+    stats = []
+    for i in range(3):
+        tokens = torch.randint(0, D.vocab, (B,), generator=g)
+        st.ids[:B] = tokens.cuda()
+        st.set_slot(T + i, pad_len=T)
+        eng.decode_step(st, 0)
+        valid = (kpos[None, :] < pl[:, None]) | ((kpos >= T) & (kpos <= T + i))[None, :]
+        ref = odec.step(tokens, T + i - (T - pl), valid)
+        for b in range(B):
+            _check_logits(st.logits[b], ref[b], f"b48 step {i} stream {b}", stats)
+            if not _near_tie(ref[b]):
+                assert int(st.out_ids[b]) == int(ref[b].float().argmax()), f"step {i} stream {b}: argmax differs"
+        for li in (0, D.layers - 1):
+            for kv in range(2):
+                got_r = eng.kv[li, kv, :B, :, T + i].cpu().float()
+                ref_r = (odec.cache.k if kv == 0 else odec.cache.v)[li][:, :, T + i].float()
+                bound = 2 ** -6 * ref_r.abs().amax(-1, keepdim=True) + 1e-6
+                assert ((got_r - ref_r).abs() <= bound).all(), f"step {i} layer {li} {'kv'[kv]} rows differ"
+    _report("b48 fp8 teacher-forced", stats)
+
+
+def test_fp8_prefill_4_streams(weights):
+    """The native prefill of 4 right-padded prompts (lengths U[300, 900]) on
+    the tcgen05 GEMMs and the two-pass prefill attention: every layer's cache
+    rows of the valid prompt positions and the first-token logits."""
+    fmt, B, L = "fp8", 4, 1040
+    pl = _b48_lengths(B)
+    T = int(pl.max())
+    g = torch.Generator().manual_seed(6)
+    emb = torch.randn(B, T, D.hidden, generator=g).to(torch.bfloat16)
+    emb = emb * (torch.arange(T)[None, :] < pl[:, None]).unsqueeze(-1).to(torch.bfloat16)
+    om = _oracle(weights, fmt)
+    odec = gr.OracleDecoder(om, L, B=B)
+    ref_ids = odec.prefill(emb, pl)
+    eng = GraniteEngine(D, weights, fmt, max_cache_len=L, max_batch=B)
+    last = eng.prefill(emb.cuda(), pl)
+    st = eng.new_state(B, 1, _lib.SB_MODE_FIRST, out_steps=1)
+    st.hidden.copy_(last)
+    eng.lm_head_argmax(st)
+    torch.cuda.synchronize()
+    stats = []
+    for b in range(B):
+        ref = odec.last_logits[b]
+        _check_logits(st.logits[b], ref, f"prefill stream {b}", stats)
+        if not _near_tie(ref):
+            assert int(st.out_ids[b]) == int(ref_ids[b])
+        n = int(pl[b])
+        for li in range(D.layers):
+            for kv, ref_c in ((0, odec.cache.k[li]), (1, odec.cache.v[li])):
+                got_r = eng.kv[li, kv, b, :, :n].cpu().float()
+                ref_r = ref_c[b, :, :n].float()
+                bound = 2 ** -5 * ref_r.abs().amax(-1, keepdim=True) + 1e-6
+                assert ((got_r - ref_r).abs() <= bound).all(), f"stream {b} layer {li} {'kv'[kv]}: cache rows differ"
+    _report("prefill fp8 b4", stats)

@@ -23,27 +23,41 @@ from starling_b200.engine import GraniteDims, GraniteEngine  # noqa: E402
 torch.set_grad_enabled(False)
 
 
-def _engine(vocab, fmt, tensor_cores=True):
-    d = GraniteDims(hidden=512, n_q=4, n_kv=2, inter=1024, vocab=vocab, layers=1)
+SMALL = dict(hidden=512, n_q=4, n_kv=2, inter=1024)
+# the Granite-1B decoder's lm_head dimensions (hidden 2048, 16 / 4 heads)
+FULL = dict(hidden=2048, n_q=16, n_kv=4, inter=8192)
+
+
+def _engine(vocab, fmt, tensor_cores=True, dims=SMALL):
+    d = GraniteDims(vocab=vocab, layers=1, **dims)
+    H, I, NQ, NKV = d.hidden, d.inter, d.n_q * 128, d.n_kv * 128
     g = torch.Generator(device="cuda").manual_seed(7)
     w = {}
-    for name, shape in [("embed_tokens.weight", (vocab, 512)), ("norm.weight", (512,)),
-                        ("layers.0.input_layernorm.weight", (512,)), ("layers.0.post_attention_layernorm.weight", (512,)),
-                        ("layers.0.self_attn.q_proj.weight", (512, 512)), ("layers.0.self_attn.k_proj.weight", (256, 512)),
-                        ("layers.0.self_attn.v_proj.weight", (256, 512)), ("layers.0.self_attn.o_proj.weight", (512, 512)),
-                        ("layers.0.mlp.gate_proj.weight", (1024, 512)), ("layers.0.mlp.up_proj.weight", (1024, 512)),
-                        ("layers.0.mlp.down_proj.weight", (512, 1024))]:
+    for name, shape in [("embed_tokens.weight", (vocab, H)), ("norm.weight", (H,)),
+                        ("layers.0.input_layernorm.weight", (H,)), ("layers.0.post_attention_layernorm.weight", (H,)),
+                        ("layers.0.self_attn.q_proj.weight", (NQ, H)), ("layers.0.self_attn.k_proj.weight", (NKV, H)),
+                        ("layers.0.self_attn.v_proj.weight", (NKV, H)), ("layers.0.self_attn.o_proj.weight", (H, NQ)),
+                        ("layers.0.mlp.gate_proj.weight", (I, H)), ("layers.0.mlp.up_proj.weight", (I, H)),
+                        ("layers.0.mlp.down_proj.weight", (H, I))]:
         w[name] = (torch.randn(shape, generator=g, device="cuda") * (0.05 if len(shape) == 2 else 1.0)).to(torch.bfloat16)
-    return GraniteEngine(d, w, fmt, max_cache_len=64, max_batch=8, tensor_cores=tensor_cores)
+    return GraniteEngine(d, w, fmt, max_cache_len=64, max_batch=16, tensor_cores=tensor_cores)
 
 
-@pytest.mark.parametrize("vocab,fmt,batch", [(100352, "nvfp4", 1), (2051, "bf16", 1), (100352, "fp8", 2)])
-def test_static_scratch_matches_workspace_version(vocab, fmt, batch):
-    eng = _engine(vocab, fmt)
+@pytest.mark.parametrize("vocab,fmt,batch,dims,null_ws", [
+    (100352, "nvfp4", 1, SMALL, False), (2051, "bf16", 1, SMALL, False), (100352, "fp8", 2, SMALL, False),
+    (100352, "nvfp4", 1, FULL, True), (100352, "fp8", 2, FULL, True), (100352, "fp8", 16, FULL, True),
+    (100352, "bf16", 1, FULL, True)])
+def test_static_scratch_matches_workspace_version(vocab, fmt, batch, dims, null_ws):
+    """null_ws: the state carries no workspace at all (pointer NULL, 0 bytes),
+    as a caller without a device allocator would pass it."""
+    eng = _engine(vocab, fmt, dims=dims)
     lib = eng.lib
+    H = eng.dims.hidden
     ref = eng.new_state(batch, 1, _lib.SB_MODE_FIRST, out_steps=1)
     new = eng.new_state(batch, 1, _lib.SB_MODE_FIRST, out_steps=1)
-    h = torch.randn(batch, 512, generator=torch.Generator(device="cuda").manual_seed(1), device="cuda").to(torch.bfloat16)
+    if null_ws:
+        new.c.workspace, new.c.workspace_bytes = None, 0
+    h = torch.randn(batch, H, generator=torch.Generator(device="cuda").manual_seed(1), device="cuda").to(torch.bfloat16)
     ref.hidden.copy_(h)
     new.hidden.copy_(h)
     s = _lib.current_stream()
