@@ -155,9 +155,7 @@ size_t sb_workspace_bytes(const SbModel* model, int32_t tokens);
 
 /* Which kernel serves NVFP4 linears of 1..8 token rows whose SbLinear has a
  * w_bs copy (process-wide; no counterpart in the reference, whose NVFP4 path
- * is eager torch).  SB_NVFP4_AUTO (default, or from
- * STARLING_B200_NVFP4=auto|block_scaled|mma_sync at first use): the
- * block-scaled tcgen05 kernel where it measured faster on B200 -- matrices of
+ * is eager torch).  SB_NVFP4_AUTO (default): the block-scaled tcgen05 kernel where it measured faster on B200 -- matrices of
  * >= 256 row tiles (lm_head) at any row count and every 8-row forward -- else
  * the mma.sync GEMV; SB_NVFP4_BLOCK_SCALED: the block-scaled
  * kernel for every shape it serves; SB_NVFP4_MMA_SYNC: always the GEMV.
@@ -177,19 +175,18 @@ int32_t sb_set_nvfp4_path(int32_t mode);
  * (src/starling/granite/multistep.py:157-188); with m > 1 it is the verify
  * forward SpeculativeDecoder._verify_step_fused (speculative.py:598-680) with
  * the acceptance compare of speculative.py:430-459 fused on device.
- * `step` indexes out_ids in DECODE mode.  About 5 launches per layer; with
- * the environment variable STARLING_B200_STEP=fused, forwards of up to 8
- * token rows (batch * m) that the fused step serves run as ONE cooperative
- * launch instead (weights streamed through shared memory across layers, grid
- * barriers between dependent phases; needs one weight format for every
- * projection, hidden / inter 2048 / 8192 or 512 / 1024, max_len <= 1024 and
- * batch * n_kv * ceil(max_len / 32) <= SMs). */
+ * `step` indexes out_ids in DECODE mode.  About 5 launches per layer
+ * (sb_decode_step_ex selects the one-launch fused step instead). */
 int sb_decode_step(const SbModel* model, const SbState* state, int32_t step, sb_stream_t stream);
 
 /* sb_decode_step with the kernel path chosen by the caller:
- * flags = 0 as sb_decode_step; SB_STEP_PER_OP: per-op kernels only;
- * SB_STEP_FUSED: the fused step, or SB_ERR_CONFIG where it does not serve
- * the forward.  No reference counterpart (choice between the two paths). */
+ * flags = 0 or SB_STEP_PER_OP: the per-op kernels (sb_decode_step);
+ * SB_STEP_FUSED: forwards of up to 8 token rows (batch * m) as ONE
+ * cooperative launch (weights streamed through shared memory across layers,
+ * activations handed between CTAs through flagged words; needs one weight
+ * format for every projection, hidden / inter 2048 / 8192 or 512 / 1024,
+ * max_len <= 1024 and batch * n_kv * ceil(max_len / 32) <= SMs), or
+ * SB_ERR_CONFIG where it does not serve the forward.  No reference counterpart (choice between the two paths). */
 #define SB_STEP_PER_OP 1
 #define SB_STEP_FUSED 2
 int sb_decode_step_ex(const SbModel* model, const SbState* state, int32_t step, int32_t flags, sb_stream_t stream);

@@ -117,6 +117,21 @@ def weights_checksum(w: dict) -> float:
 # --------------------------------------------------------------------------- #
 # linear layers (bf16 or dequantised)
 # --------------------------------------------------------------------------- #
+# Accumulation of the oracle's matmuls.  "bf16": what the reference runs (bf16
+# matmuls accumulated in fp32 by the BLAS, in its order).  "f64": the same ops
+# and rounding points with every matmul accumulated in float64 and rounded once
+# to bf16 -- the most accurate result at each of the reference's rounding
+# points, used by the tests to measure how far any accumulation order (the
+# BLAS's, the CUDA kernels') sits from it.
+ACCUMULATE = "bf16"
+
+
+def _matmul(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    if ACCUMULATE == "f64":
+        return torch.matmul(a.double(), b.double()).to(BF16)
+    return torch.matmul(a, b)
+
+
 class Linear:
     """``nn.Linear`` stand-in.  ``fmt == 'bf16'`` runs the bf16 matmul the
     reference runs; quantised formats run ``bf16(x.float() @ W_deq.T)``."""
@@ -133,6 +148,8 @@ class Linear:
             self.w = torch.from_numpy(quant_ref.dequantize(fmt, parts))  # fp32
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        if ACCUMULATE == "f64":  # every product and sum exact to ~2^-53, one rounding to bf16
+            return F.linear(x.double(), self.w.double()).to(BF16)
         if self.fmt == "bf16":
             return F.linear(x, self.w)
         return F.linear(x.float(), self.w).to(BF16)
@@ -270,10 +287,10 @@ def layer_forward(d: Dims, L: dict, kc: torch.Tensor, vc: torch.Tensor, hidden, 
     vc.index_copy_(2, slots, v)
     kr = repeat_kv(kc, n_q // n_kv)
     vr = repeat_kv(vc, n_q // n_kv)
-    scores = torch.matmul(q, kr.transpose(2, 3)) * d.attn_mult
+    scores = _matmul(q, kr.transpose(2, 3)) * d.attn_mult
     scores = scores + mask
     attn = F.softmax(scores, dim=-1, dtype=torch.float32).to(BF16)
-    ao = torch.matmul(attn, vr).transpose(1, 2).reshape(B, T, n_q * hd)
+    ao = _matmul(attn, vr).transpose(1, 2).reshape(B, T, n_q * hd)
     ao = L["o"](ao)
     hidden = residual_scale(residual, ao, d.res_mult)
     residual = hidden

@@ -71,29 +71,8 @@ static GemvParams base_params(const SbLinear& l, int m) {
   return p;
 }
 
-// STARLING_B200_GEMV=v1 forces the general kernel for every shape (A/B runs).
-static bool use_dec_kernel() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("STARLING_B200_GEMV");
-    v = (e && strcmp(e, "v1") == 0) ? 0 : 1;
-  }
-  return v == 1;
-}
-
 static bool dec_plan_for(int fmt, int n_tiles, int k, int m, DecPlan& pl) {
-  return use_dec_kernel() && gemv_dec_plan(fmt, n_tiles, k, m, pl);
-}
-
-// STARLING_B200_GEMM=mma_sync keeps token counts above 8 on the mma.sync GEMV
-// even when a tensor-core tile copy of the weight exists (A/B runs).
-static bool use_tc_kernel() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("STARLING_B200_GEMM");
-    v = (e && strcmp(e, "mma_sync") == 0) ? 0 : 1;
-  }
-  return v == 1;
+  return gemv_dec_plan(fmt, n_tiles, k, m, pl);
 }
 
 // The tcgen05 path serves a linear with a tile copy above 8 token rows (FP8,
@@ -102,7 +81,7 @@ static bool use_tc_kernel() {
 // compute-bound, i.e. prefill).
 static bool tc_plan_for(const SbLinear& l, int m, TcPlan& pl) {
   const int min_rows = (l.fmt == SB_FMT_NVFP4 || l.fmt == SB_FMT_INT8) ? 64 : 8;
-  return m > min_rows && l.w_tc && use_tc_kernel() && tc_plan(l.fmt, l.n, l.k, m, pl);
+  return m > min_rows && l.w_tc && tc_plan(l.fmt, l.n, l.k, m, pl);
 }
 
 static int run_gemv(GemvParams& p, int fmt, bool pdl, cudaStream_t s) {
@@ -124,22 +103,9 @@ static int run_gemv(GemvParams& p, int fmt, bool pdl, cudaStream_t s) {
   return 0;
 }
 
-// NVFP4 1..8-row path (sb_set_nvfp4_path); -1 = not yet read from
-// STARLING_B200_NVFP4.
-static std::atomic<int> g_nvfp4_path{-1};
-static int nvfp4_path() {
-  int v = g_nvfp4_path.load(std::memory_order_relaxed);
-  if (v < 0) {
-    const char* e = getenv("STARLING_B200_NVFP4");
-    v = SB_NVFP4_AUTO;
-    if (e && strcmp(e, "mma_sync") == 0) v = SB_NVFP4_MMA_SYNC;
-    if (e && strcmp(e, "block_scaled") == 0) v = SB_NVFP4_BLOCK_SCALED;
-    int expect = -1;
-    g_nvfp4_path.compare_exchange_strong(expect, v);
-    v = g_nvfp4_path.load(std::memory_order_relaxed);
-  }
-  return v;
-}
+// NVFP4 1..8-row path (sb_set_nvfp4_path)
+static std::atomic<int> g_nvfp4_path{SB_NVFP4_AUTO};
+static int nvfp4_path() { return g_nvfp4_path.load(std::memory_order_relaxed); }
 
 // Whether the block-scaled kernel serves (l, m).  In auto mode it takes the
 // shapes where it measured faster than the mma.sync GEMV on B200 (graphed
@@ -496,17 +462,6 @@ size_t sb_workspace_bytes(const SbModel* md, int32_t tokens) {
   return ws_layout(md, tokens).total;
 }
 
-// sb_decode_step's default path: the per-op kernels; STARLING_B200_STEP=fused
-// selects the fused step wherever it serves the forward.
-static bool use_step_kernel() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("STARLING_B200_STEP");
-    v = (e && strcmp(e, "fused") == 0) ? 1 : 0;
-  }
-  return v == 1;
-}
-
 size_t sb_decode_step_scratch_offset(const SbModel* md, int32_t tokens) {
   if (!md || tokens < 1) return static_cast<size_t>(-1);
   const WsLayout w = ws_layout(md, tokens);
@@ -528,9 +483,8 @@ int sb_decode_step_ex(const SbModel* md, const SbState* st, int32_t step, int32_
   if (!md->layers || md->n_layers < 1) return fail(SB_ERR_ARG, "no layers");
   if ((flags & SB_STEP_PER_OP) && (flags & SB_STEP_FUSED)) return fail(SB_ERR_ARG, "conflicting step flags");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  // flags 0: the default path (per-op kernels; the fused step where it serves
-  // the forward when STARLING_B200_STEP=fused)
-  if ((flags & SB_STEP_FUSED) || (flags == 0 && use_step_kernel())) {
+  // flags 0: the default path, the per-op kernels
+  if (flags & SB_STEP_FUSED) {
     StepPlan pl;
     const char* why = "";
     if (step_plan(md, st, pl, &why)) {
@@ -541,7 +495,7 @@ int sb_decode_step_ex(const SbModel* md, const SbState* st, int32_t step, int32_
       if (rc != 0) return fail(rc, "fused step launch: %s", rc < 1000 ? cudaGetErrorString((cudaError_t)rc) : "config");
       return 0;
     }
-    if (flags & SB_STEP_FUSED) return fail(SB_ERR_CONFIG, "the fused step does not serve this forward: %s", why);
+    return fail(SB_ERR_CONFIG, "the fused step does not serve this forward: %s", why);
   }
   for (int l = 0; l < md->n_layers; ++l)
     for (int op = SB_OP_QKV; op <= SB_OP_DOWN; ++op) SB_TRY(launch_op(md, st, l, op, step, s));
@@ -606,16 +560,8 @@ int sb_linear_ex(const SbLinear* lin, const uint16_t* x, uint16_t* y, int32_t m,
 static const int kPrefillQBlock = 8;
 
 // The prefill's attention runs on the two-pass prefill kernel
-// (attention_pf.cu); STARLING_B200_PREFILL_ATTN=blocks8 runs it on the decode
-// kernel with query blocks of kPrefillQBlock positions instead (A/B runs).
-static bool use_prefill_attn() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("STARLING_B200_PREFILL_ATTN");
-    v = (e && strcmp(e, "blocks8") == 0) ? 0 : 1;
-  }
-  return v == 1;
-}
+// (attention_pf.cu) where it serves the head grouping, else on the decode
+// kernel with query blocks of kPrefillQBlock positions.
 static const int kPrefillBlockRows = 8192;
 
 static int prefill_streams_per_block(int B, int T) {
@@ -752,7 +698,7 @@ extern "C" int sb_prefill(const SbModel* md, uint16_t* hidden, int32_t batch, in
     a.chunk_cap = attn_key_capacity(T, 1);
     a.slots = 2;
     a.cache_rows = static_cast<long long>(md->max_batch) * md->n_kv * md->max_len;
-    const int rc = use_prefill_attn() && attn_prefill_ok(md->n_q, md->n_kv) ? attn_prefill_launch(a, batch, T, s)
+    const int rc = attn_prefill_ok(md->n_q, md->n_kv) ? attn_prefill_launch(a, batch, T, s)
                                                                            : attn_launch(a, batch, false, s);
     if (rc == SB_ERR_CONFIG) return fail(rc, "sb_prefill: no attention configuration for T=%d", T);
     if (rc != 0) return fail(rc, "sb_prefill: attention launch: %s", cudaGetErrorString((cudaError_t)rc));

@@ -497,15 +497,7 @@ static const int kSMs = 148;
 static const size_t kBsSmemOne = 220 * 1024;  // one CTA per SM (persistent over tiles)
 static const size_t kBsSmemTwo = 110 * 1024;  // two CTAs per SM (clusters splitting K)
 
-// STARLING_B200_BS_CTAS_PER_SM=1 keeps one CTA per SM (A/B runs)
-static int bs_ctas_per_sm_max() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("STARLING_B200_BS_CTAS_PER_SM");
-    v = (e && atoi(e) == 1) ? 1 : 2;
-  }
-  return v;
-}
+static int bs_ctas_per_sm_max() { return 2; }
 
 // Plan for per_sm CTAs per SM (1: up to 220 KB of shared memory and 512 TMEM
 // columns each; 2: half of both).  Two CTAs per SM run two MMA-issuing threads

@@ -635,16 +635,7 @@ size_t tc_operand_bytes(int fmt, int k, int m) {
   return static_cast<size_t>(mtiles) * np * k * elem_bytes(fmt) + static_cast<size_t>(mtiles) * mp * 4;
 }
 
-// STARLING_B200_TC_CTAS_PER_SM=1 keeps one GEMM CTA per SM for decode /
-// verify launches (A/B runs)
-static int tc_ctas_per_sm_max() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("STARLING_B200_TC_CTAS_PER_SM");
-    v = (e && atoi(e) == 1) ? 1 : 2;
-  }
-  return v;
-}
+static int tc_ctas_per_sm_max() { return 2; }
 
 static const size_t kTcSmemTwo = 110 * 1024;  // two CTAs per SM
 

@@ -1202,19 +1202,11 @@ static DevInfo dev_info() {
   return info[dev];
 }
 
-// Weight bytes one CTA keeps in flight at most.  Deeper queues do not raise
-// the stream's bandwidth (the step consumes far below it between grid
-// barriers) but add their queueing delay to the step's latency-critical
-// activation reads.  STARLING_B200_STEP_INFLIGHT=<bytes> overrides (A/B runs).
-static int inflight_cap() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("STARLING_B200_STEP_INFLIGHT");
-    v = e ? atoi(e) : 48 * 1024;
-    if (v < 40 * 1024) v = 40 * 1024;  // >= one entry
-  }
-  return v;
-}
+// Weight bytes one CTA keeps in flight at most (>= one 40 KiB entry).  Deeper
+// queues do not raise the stream's bandwidth (the step consumes far below it
+// between grid barriers) but add their queueing delay to the step's
+// latency-critical activation reads.
+static int inflight_cap() { return 48 * 1024; }
 
 // (hidden, inter) shapes with a compiled kernel
 static bool dims_supported(int hidden, int inter) {

@@ -203,8 +203,8 @@ class GraniteEngine:
         return EngineState(self, batch, m, mode, **kw)
 
     # ---- native calls ----------------------------------------------------- #
-    # decode-step kernel path: "auto" (the library's default: per-op kernels,
-    # or the fused one-launch step with STARLING_B200_STEP=fused), "fused"
+    # decode-step kernel path: "auto" (the library's default: per-op kernels),
+    # "fused"
     # (required), "prefer_fused" (fused where it serves the forward) or "ops"
     step_path = "auto"
 

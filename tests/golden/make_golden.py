@@ -1,9 +1,9 @@
 """Generate golden vectors by running the reference decoders on CPU.
 
-Run in a container that has the reference checkout (read-only) at
-``/root/reference`` (override with ``STARLING_REF``):
+Run where a checkout of the reference (sims1253/starling) is available,
+with ``STARLING_REF`` naming its root directory:
 
-    python tests/golden/make_golden.py
+    STARLING_REF=<reference checkout> python tests/golden/make_golden.py
 
 It imports the reference's own ``LLMMega``, ``FusedLLMMega``,
 ``BatchedLLMMega`` and ``SpeculativeDecoder`` (src/starling/granite/*.py),
@@ -27,7 +27,9 @@ import torch
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parent.parent
 sys.path.insert(0, str(REPO))
-REF = Path(os.environ.get("STARLING_REF", "/root/reference")) / "src"
+if not os.environ.get("STARLING_REF"):
+    raise SystemExit("set STARLING_REF to the root of a reference checkout (it holds src/starling/)")
+REF = Path(os.environ["STARLING_REF"]) / "src"
 sys.path.insert(0, str(REF))
 
 torch.cuda.synchronize = lambda *a, **k: None  # called unconditionally by the reference

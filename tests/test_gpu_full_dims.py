@@ -42,7 +42,8 @@ torch.set_num_threads(min(os.cpu_count() or 1, 16))
 
 D = gr.BASELINE_DIMS
 RTOL = 1e-2
-ATOL_FRAC = 1e-2
+ATOL_FRAC = 2.0 ** -5  # 4 bf16 steps of the largest logit
+REL_L2 = 1e-2
 NO_EOS = -1
 
 
@@ -51,26 +52,39 @@ def _tol(ref: torch.Tensor) -> torch.Tensor:
     return RTOL * r.abs() + ATOL_FRAC * r.abs().max()
 
 
-def _check_logits(got: torch.Tensor, ref: torch.Tensor, what: str, stats: list) -> None:
-    g, r = got.float().cpu(), ref.float().cpu()
-    err = (g - r).abs()
-    # the smallest ATOL_FRAC this row would need (for tightening the bound)
-    need = float(((err - RTOL * r.abs()).clamp_min(0).max() / r.abs().max()))
-    stats.append(need)
-    bad = err > _tol(r)
-    assert not bad.any(), (f"{what}: {int(bad.sum())} logits outside tolerance; max err {float(err.max()):.4g}, "
-                           f"needs atol {need:.3g} x max|ref|")
+class LogitStats:
+    """Per-row comparison of logits against the oracle: every element within
+    ``RTOL |ref| + ATOL_FRAC max|ref|`` and the relative L2 error within
+    ``REL_L2``.  Rows are collected and checked at the end, so a failure
+    reports the whole run."""
+
+    def __init__(self, name: str):
+        self.name = name
+        self.rows = []  # (what, max|e| / max|ref|, ||e|| / ||ref||, elements outside)
+
+    def add(self, got: torch.Tensor, ref: torch.Tensor, what: str) -> None:
+        g, r = got.float().cpu(), ref.float().cpu()
+        e = (g - r).abs()
+        self.rows.append((what, float(e.max() / r.abs().max()), float(e.norm() / r.norm()),
+                          int((e > _tol(r)).sum())))
+
+    def report(self) -> str:
+        fr = [x[1] for x in self.rows]
+        l2 = [x[2] for x in self.rows]
+        s = (f"[{self.name}] {len(self.rows)} rows: max|err|/max|ref| max {max(fr):.3g} mean "
+             f"{sum(fr) / len(fr):.3g}; rel L2 max {max(l2):.3g} mean {sum(l2) / len(l2):.3g}")
+        print(s)
+        return s
+
+    def check(self) -> None:
+        s = self.report()
+        bad = [x for x in self.rows if x[3] or x[2] > REL_L2]
+        assert not bad, f"{s}; {len(bad)} rows outside tolerance, first: {bad[:3]}"
 
 
 def _near_tie(ref: torch.Tensor) -> bool:
     t = ref.float().topk(2).values
     return float(t[0] - t[1]) <= float(_tol(ref).max())
-
-
-def _report(name: str, stats: list) -> None:
-    if stats:
-        print(f"[{name}] rows {len(stats)}: atol needed (x max|ref|) max {max(stats):.3g} "
-              f"mean {sum(stats) / len(stats):.3g}")
 
 
 _MODELS = {}
@@ -99,6 +113,58 @@ def _b1_inputs(weights):
     return torch.cat([audio, weights["embed_tokens.weight"][ids].unsqueeze(0)], dim=1)
 
 
+def test_accumulation_noise_floor_b1_bf16(weights):
+    """How far any accumulation order sits from the exact one.  The oracle is
+    run twice on the B=1 workload (prefill + 3 teacher-forced decode steps,
+    bf16 weights): as the reference runs it (bf16 matmuls accumulated by the
+    CPU BLAS) and with every matmul accumulated in float64 and rounded once to
+    bf16 at the same rounding points.  The native path must be no further from
+    the float64 run than the BLAS-accumulated oracle is, within a factor of 2
+    (or one bf16 step of the largest logit): its kernels lose no precision
+    beyond their accumulation order."""
+    emb = _b1_inputs(weights)
+    T, L = emb.shape[1], 640
+    om = _oracle(weights, "bf16")
+    runs = {}
+    for acc in ("bf16", "f64"):
+        gr.ACCUMULATE = acc
+        try:
+            odec = gr.OracleDecoder(om, L)
+            odec.prefill(emb)
+            rows = [odec.last_logits[0].clone()]
+            ids = [int(rows[0].float().argmax())]
+            for i in range(3):
+                valid = (torch.arange(L) <= T + i).view(1, -1)
+                tok = runs["bf16"][1][i] if "bf16" in runs else ids[-1]
+                rows.append(odec.step(torch.tensor([tok]), torch.tensor([T + i]), valid)[0].clone())
+                ids.append(int(rows[-1].float().argmax()))
+        finally:
+            gr.ACCUMULATE = "bf16"
+        runs[acc] = (rows, ids)
+    eng = GraniteEngine(D, weights, "bf16", max_cache_len=L, max_batch=1)
+    st = eng.new_state(1, 1, _lib.SB_MODE_DECODE, out_steps=1)
+    st.hidden.copy_(eng.prefill(emb.cuda()))
+    st.set_mode(_lib.SB_MODE_FIRST)
+    eng.lm_head_argmax(st)
+    st.set_mode(_lib.SB_MODE_DECODE)
+    native = [st.logits[0].cpu().clone()]
+    for i in range(3):
+        st.ids[0] = runs["bf16"][1][i]
+        st.set_slot(T + i, pad_len=T)
+        eng.decode_step(st, 0)
+        native.append(st.logits[0].cpu().clone())
+    exact = runs["f64"][0]
+    blas, gpu = LogitStats("oracle (BLAS order) vs float64"), LogitStats("native vs float64")
+    for i in range(4):
+        blas.add(runs["bf16"][0][i], exact[i], f"row {i}")
+        gpu.add(native[i], exact[i], f"row {i}")
+    blas.report()
+    gpu.report()
+    for (w, fb, lb, _), (_, fg, lg, _) in zip(blas.rows, gpu.rows):
+        assert fg <= max(2 * fb, 2.0 ** -7), f"{w}: native max err {fg:.3g} vs the BLAS order's {fb:.3g}"
+        assert lg <= max(2 * lb, 2.0 ** -9), f"{w}: native rel L2 {lg:.3g} vs the BLAS order's {lb:.3g}"
+
+
 @pytest.mark.parametrize("fmt", ["bf16", "nvfp4"])
 def test_b1_prefill_teacher_forced_and_greedy_128(weights, fmt):
     emb = _b1_inputs(weights)
@@ -109,7 +175,7 @@ def test_b1_prefill_teacher_forced_and_greedy_128(weights, fmt):
     assert len(ref_ids) == n_new
 
     eng = GraniteEngine(D, weights, fmt, max_cache_len=L, max_batch=1)
-    stats = []
+    stats = LogitStats(f"b1 {fmt} teacher-forced")
     # prefill + first token
     st = eng.new_state(1, 1, _lib.SB_MODE_DECODE, out_steps=1)
     last = eng.prefill(emb.cuda())
@@ -117,22 +183,21 @@ def test_b1_prefill_teacher_forced_and_greedy_128(weights, fmt):
     st.set_mode(_lib.SB_MODE_FIRST)
     eng.lm_head_argmax(st)
     st.set_mode(_lib.SB_MODE_DECODE)
-    _check_logits(st.logits[0], ref_logits[0], f"{fmt} prefill", stats)
+    stats.add(st.logits[0], ref_logits[0], f"{fmt} prefill")
     if not _near_tie(ref_logits[0]):
         assert int(st.out_ids[0]) == ref_ids[0]
     # 128 decode steps, each fed the oracle's greedy token of the previous step
-    ties = 0
+    ties, wrong = 0, []
     for i in range(n_new - 1):
         st.ids[0] = ref_ids[i]
         st.set_slot(T + i, pad_len=T)
         eng.decode_step(st, 0)
         ref = ref_logits[i + 1]
-        _check_logits(st.logits[0], ref, f"{fmt} step {i}", stats)
+        stats.add(st.logits[0], ref, f"{fmt} step {i}")
         if _near_tie(ref):
             ties += 1
-        else:
-            assert int(st.out_ids[0]) == ref_ids[i + 1], f"{fmt} step {i}: argmax differs"
-    _report(f"b1 {fmt} teacher-forced", stats)
+        elif int(st.out_ids[0]) != ref_ids[i + 1]:
+            wrong.append(i)
 
     # the free-running K=8 graphed decoder: identical ids up to a genuine near-tie
     dec = MultiStepLLMMega(engine=eng, steps_per_replay=8)
@@ -145,6 +210,8 @@ def test_b1_prefill_teacher_forced_and_greedy_128(weights, fmt):
             break
     print(f"[b1 {fmt}] 128-step greedy: {sum(a == b for a, b in zip(got, ref_ids))}/{n_new} ids equal, "
           f"{ties} near-ties among the teacher-forced steps")
+    stats.check()
+    assert not wrong, f"{fmt}: teacher-forced argmax differs (no near-tie) at steps {wrong}"
 
 
 @pytest.mark.parametrize("fmt", ["nvfp4"])
@@ -163,9 +230,7 @@ def test_verify_8_tokens_cache_600(weights, fmt):
     # make the drafts agree with the oracle for the first three positions, so
     # the accept length is not trivially 0
     ids[1:4] = ref_pred[0:3]
-    odec = gr.OracleDecoder(om, 640)
-    odec.prefill(emb)
-    ref = odec.verify(ids, 600)
+    ref = odec.verify(ids, 600)  # the same slots again: the cache rewound to 600
     ref_pred = ref.float().argmax(-1)
     acc = 0
     while acc < 7 and int(ref_pred[acc]) == int(ids[acc + 1]):
@@ -178,15 +243,15 @@ def test_verify_8_tokens_cache_600(weights, fmt):
     st.set_slot(600, pad_len=600)
     eng.decode_step(st, 0)
     torch.cuda.synchronize()
-    stats = []
+    stats = LogitStats("verify nvfp4")
     ties = [_near_tie(ref[i]) for i in range(8)]
     for i in range(8):
-        _check_logits(st.logits[i], ref[i], f"verify row {i}", stats)
+        stats.add(st.logits[i], ref[i], f"verify row {i}")
         if not ties[i]:
             assert int(st.out_ids[i]) == int(ref_pred[i]), f"verify row {i}: argmax differs"
     if not any(ties[:acc + 1]):
         assert int(st.ctrl[_lib.SB_CTRL_ACCEPT]) == acc
-    _report("verify nvfp4", stats)
+    stats.check()
 
 
 def _b48_lengths(B=48):
@@ -217,7 +282,7 @@ def test_b48_fp8_teacher_forced_steps(weights):
     eng.load_cache_from(odec.cache.k, odec.cache.v)
     st = eng.new_state(B, 1, _lib.SB_MODE_DECODE, out_steps=1, prompt_len=pl, rope_off=T - pl)
     kpos = torch.arange(L)
-    stats = []
+    stats = LogitStats("b48 fp8 teacher-forced")
     for i in range(3):
         tokens = torch.randint(0, D.vocab, (B,), generator=g)
         st.ids[:B] = tokens.cuda()
@@ -226,7 +291,7 @@ def test_b48_fp8_teacher_forced_steps(weights):
         valid = (kpos[None, :] < pl[:, None]) | ((kpos >= T) & (kpos <= T + i))[None, :]
         ref = odec.step(tokens, T + i - (T - pl), valid)
         for b in range(B):
-            _check_logits(st.logits[b], ref[b], f"b48 step {i} stream {b}", stats)
+            stats.add(st.logits[b], ref[b], f"b48 step {i} stream {b}")
             if not _near_tie(ref[b]):
                 assert int(st.out_ids[b]) == int(ref[b].float().argmax()), f"step {i} stream {b}: argmax differs"
         for li in (0, D.layers - 1):
@@ -235,7 +300,7 @@ def test_b48_fp8_teacher_forced_steps(weights):
                 ref_r = (odec.cache.k if kv == 0 else odec.cache.v)[li][:, :, T + i].float()
                 bound = 2 ** -6 * ref_r.abs().amax(-1, keepdim=True) + 1e-6
                 assert ((got_r - ref_r).abs() <= bound).all(), f"step {i} layer {li} {'kv'[kv]} rows differ"
-    _report("b48 fp8 teacher-forced", stats)
+    stats.check()
 
 
 def test_fp8_prefill_4_streams(weights):
@@ -257,10 +322,10 @@ def test_fp8_prefill_4_streams(weights):
     st.hidden.copy_(last)
     eng.lm_head_argmax(st)
     torch.cuda.synchronize()
-    stats = []
+    stats = LogitStats("prefill fp8 b4")
     for b in range(B):
         ref = odec.last_logits[b]
-        _check_logits(st.logits[b], ref, f"prefill stream {b}", stats)
+        stats.add(st.logits[b], ref, f"prefill stream {b}")
         if not _near_tie(ref):
             assert int(st.out_ids[b]) == int(ref_ids[b])
         n = int(pl[b])
@@ -270,4 +335,4 @@ def test_fp8_prefill_4_streams(weights):
                 ref_r = ref_c[b, :, :n].float()
                 bound = 2 ** -5 * ref_r.abs().amax(-1, keepdim=True) + 1e-6
                 assert ((got_r - ref_r).abs() <= bound).all(), f"stream {b} layer {li} {'kv'[kv]}: cache rows differ"
-    _report("prefill fp8 b4", stats)
+    stats.check()
