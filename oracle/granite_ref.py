@@ -29,6 +29,7 @@ from __future__ import annotations
 
 import math
 import os
+from contextlib import contextmanager
 from concurrent.futures import ThreadPoolExecutor
 from dataclasses import dataclass, field
 from typing import Optional
@@ -124,6 +125,18 @@ def weights_checksum(w: dict) -> float:
 # points, used by the tests to measure how far any accumulation order (the
 # BLAS's, the CUDA kernels') sits from it.
 ACCUMULATE = "bf16"
+
+
+@contextmanager
+def accumulate(mode: str):
+    """Run the oracle's matmuls with ``mode`` ("bf16" or "f64") inside the block."""
+    global ACCUMULATE
+    assert mode in ("bf16", "f64")
+    old, ACCUMULATE = ACCUMULATE, mode
+    try:
+        yield
+    finally:
+        ACCUMULATE = old
 
 
 def _matmul(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:

@@ -9,6 +9,7 @@ ncu summaries under profiles/ are captured on).
     python -m starling_b200.kernel_bench step --workload b1 --path fused  # the one-launch fused step
     python -m starling_b200.kernel_bench prefill --layers 40       # one native prefill of the b48 prompts
     python -m starling_b200.kernel_bench verify --layers 40        # one 8-token verify forward, B=1, NVFP4
+    python -m starling_b200.kernel_bench gemv-table                # dequant-GEMV microbench, B=1, 3 formats
 
 Workloads (same as bench.py): b48 = 48 streams, FP8 weights, prompts
 U[300,900]; b1 = one stream, NVFP4 weights, 320 prompt positions.  Weights are
@@ -240,6 +241,52 @@ def cmd_linear(a) -> None:
           f"{nbytes / 1e6:.2f} MB -> {nbytes / us / 1e3:.0f} GB/s")
 
 
+def cmd_gemv_table(a) -> None:
+    """The dequant-GEMV microbench at B = 1: NVFP4 / FP8 / INT8 weights of
+    [8192 x 2048], [2048 x 8192] and the [100352 x 2048] lm_head, N(0, 0.02)
+    weights, an N(0, 1) bf16 activation row, bf16 out.  Launches rotate over
+    enough weight copies that they span >= 8x the 126 MB L2 (at least 16), so
+    every launch streams its weight from HBM.  Algorithmic bytes = packed
+    weight + scales + x + y; fraction of the measured copy peak."""
+    import json
+    from pathlib import Path
+
+    lib = _lib.load()
+    lib.sb_set_nvfp4_path(_lib.SB_NVFP4_AUTO)
+    peak_file = Path(__file__).resolve().parent.parent / "MEASURED_PEAKS.json"
+    peak = json.loads(peak_file.read_text())["hbm_gbs"] if peak_file.exists() else 6650.0
+    g = torch.Generator(device="cuda").manual_seed(0)
+    rows = []
+    for n, k in ((8192, 2048), (2048, 8192), (100352, 2048)):
+        w = (torch.randn(n, k, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+        x = torch.randn(1, k, device="cuda", generator=g).to(torch.bfloat16)
+        y = torch.empty(1, n, dtype=torch.bfloat16, device="cuda")
+        for fmt in ("nvfp4", "fp8", "int8"):
+            first = pack.pack_matrix(w, fmt, tc=False, bs=fmt == "nvfp4")
+            ncopy = max(16, -(-8 * 126_000_000 // first.nbytes))
+            copies = [first] + [pack.pack_matrix(w, fmt, tc=False, bs=fmt == "nvfp4") for _ in range(ncopy - 1)]
+            cs = [c.c_struct() for c in copies]
+            reps = ncopy
+
+            def run():
+                for i in range(reps):
+                    check(lib.sb_linear(C.byref(cs[i]), ptr(x), ptr(y), 1, 1, _lib.current_stream()))
+
+            us = _graph_time(run, reps=3) / reps
+            nbytes = first.nbytes + 2 * k + 2 * n
+            gbs = nbytes / us / 1e3
+            rows.append(dict(fmt=fmt, n=n, k=k, us=round(us, 3), bytes=nbytes, gbs=round(gbs, 1),
+                             frac=round(gbs / peak, 4), copies=ncopy))
+            del copies, cs, first
+            torch.cuda.empty_cache()
+    print(f"| format | W [n x k] | us / launch | algorithmic bytes | GB/s | of measured {peak:.0f} GB/s |")
+    print("|---|---|---|---|---|---|")
+    for r in rows:
+        print(f"| {r['fmt']} | {r['n']} x {r['k']} | {r['us']:.2f} | {r['bytes'] / 1e6:.2f} MB | {r['gbs']:.0f} | "
+              f"{r['frac']:.3f} |")
+    print(json.dumps({"gemv_b1": rows, "peak_gbs": peak}))
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     sub = ap.add_subparsers(dest="cmd", required=True)
@@ -265,10 +312,11 @@ def main(argv=None) -> None:
     p.add_argument("--reps", type=int, default=20)
     p.add_argument("--nvfp4-path", choices=["auto", "block_scaled", "mma_sync"], default="auto",
                    help="kernel for 1..8-row NVFP4 launches (sb_set_nvfp4_path)")
+    sub.add_parser("gemv-table")
     a = ap.parse_args(argv)
     torch.set_grad_enabled(False)
     {"ops": cmd_ops, "step": cmd_step, "attention": cmd_attention, "linear": cmd_linear, "prefill": cmd_prefill,
-     "verify": cmd_verify}[a.cmd](a)
+     "verify": cmd_verify, "gemv-table": cmd_gemv_table}[a.cmd](a)
 
 
 if __name__ == "__main__":

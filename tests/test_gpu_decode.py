@@ -1,10 +1,12 @@
 """Decode-level parity on the GPU: the native decoders vs the CPU oracle and
 vs the golden vectors produced by the reference itself.
 
-Tolerances (floating point): logits within rel 1e-2 of the logit range;
+Tolerances (floating point): every logit within 1e-2 |ref| + 2^-5 max|ref|
+of the oracle's (the bound of the full-size tests, set from the measured
+distance of the reference's own accumulation order from exact arithmetic);
 greedy ids identical, except that a divergence is accepted only where the
-oracle's own top-2 logit margin at that step is within the logit tolerance
-(a genuine near-tie; reported, not hidden).
+oracle's own top-2 logit margin at that step is within the tolerance at the
+top logit (a genuine near-tie; reported, not hidden).
 """
 
 import pytest
@@ -27,6 +29,18 @@ from starling_b200.speculative import SpeculativeDecoder  # noqa: E402
 torch.set_grad_enabled(False)
 EOS, PAD = 100257, 100256
 LOGIT_RTOL = 1e-2
+LOGIT_ATOL_FRAC = 2.0 ** -5
+
+
+@pytest.fixture(autouse=True)
+def _exact_oracle():
+    """Live oracle runs accumulate every matmul in float64 (one rounding to
+    bf16 at each of the reference's rounding points): on these chaotic small
+    models the CPU BLAS's own accumulation order, which can differ between
+    host CPUs, moves the reference logits by about the tolerance.  Checks
+    against the reference-made golden vectors are unaffected."""
+    with gr.accumulate("f64"):
+        yield
 
 
 @pytest.fixture(scope="module")
@@ -38,7 +52,15 @@ def golden(golden_dir):
 
 
 def _logit_tol(ref):
-    return LOGIT_RTOL * float(ref.float().abs().max())
+    """The per-element bound at the top logit (near-tie decisions)."""
+    return (LOGIT_RTOL + LOGIT_ATOL_FRAC) * float(ref.float().abs().max())
+
+
+def _excess(got, ref):
+    """max over elements of |got - ref| - (RTOL |ref| + ATOL_FRAC max|ref|): <= 0 passes."""
+    g, r = got.float().cpu(), ref.float().cpu()
+    bound = LOGIT_RTOL * r.abs() + LOGIT_ATOL_FRAC * r.abs().max()
+    return float(((g - r).abs() - bound).max())
 
 
 def _assert_ids_match(got, ref, margins, tol, what):
@@ -75,7 +97,7 @@ def test_teacher_forced_logits_bf16(golden):
     odec = gr.OracleDecoder(gr.OracleModel(d, w), 96)
     odec.prefill(emb)
     ref0 = odec.last_logits[0]
-    assert (st.logits[0].cpu().float() - ref0.float()).abs().max() <= _logit_tol(ref0)
+    assert _excess(st.logits[0], ref0) <= 0
     ids = g["ids"].tolist()
     for i in range(24):
         # same state on both sides: each comparison measures one step's kernels
@@ -87,8 +109,8 @@ def test_teacher_forced_logits_bf16(golden):
         valid = (torch.arange(96) <= T + i).view(1, -1)
         ref = odec.step(torch.tensor([ids[i]]), torch.tensor([T + i]), valid)[0]
         got = st.logits[0].cpu()
-        err = (got.float() - ref.float()).abs().max()
-        assert err <= _logit_tol(ref), f"step {i}: max logit err {err:.4g} > {_logit_tol(ref):.4g}"
+        err = _excess(got, ref)
+        assert err <= 0, f"step {i}: logits exceed the bound by {err:.4g}"
         if _margin(ref) > _logit_tol(ref):
             assert int(st.out_ids[0]) == int(ref.argmax())
 
@@ -162,8 +184,9 @@ def test_speculative_vs_golden(golden, golden_dir):
     assert res.decode_probes == 0
     got, ref = res.ids[0].tolist(), g["ids"].tolist()
     if got != ref:
-        odec = gr.OracleDecoder(gr.OracleModel(d, w), g["max_cache_len"])
-        oids, _ = gr.speculative_generate(odec, g["inputs_embeds"], g["draft"], g["max_new_tokens"], EOS)
+        with gr.accumulate("bf16"):  # the reference's own order, pinned to its golden run
+            odec = gr.OracleDecoder(gr.OracleModel(d, w), g["max_cache_len"])
+            oids, _ = gr.speculative_generate(odec, g["inputs_embeds"], g["draft"], g["max_new_tokens"], EOS)
         assert oids == ref
         first = next(i for i in range(min(len(got), len(ref))) if got[i] != ref[i])
         pytest.fail(f"speculative ids differ from the reference at {first}: {got[:first + 2]} vs {ref[:first + 2]}")
@@ -184,8 +207,8 @@ def test_verify_logits_match_oracle(golden):
     odec = gr.OracleDecoder(gr.OracleModel(d, w), 96)
     odec.prefill(emb)
     ref = odec.verify(torch.tensor(ids), T)
-    err = (st.logits.cpu().float() - ref.float()).abs().max()
-    assert err <= _logit_tol(ref)
+    for i in range(9):
+        assert _excess(st.logits[i], ref[i]) <= 0, f"verify row {i}"
     for i in range(9):
         if _margin(ref[i]) > _logit_tol(ref):
             assert preds[i] == int(ref[i].argmax())
@@ -228,8 +251,8 @@ def _teacher_forced(golden, fmt):
         eng.decode_step(st, 0)
         valid = (torch.arange(96) <= T + i).view(1, -1)
         ref = odec.step(torch.tensor([ids[i]]), torch.tensor([T + i]), valid)[0]
-        err = (st.logits[0].cpu().float() - ref.float()).abs().max()
-        assert err <= _logit_tol(ref), f"{fmt} step {i}: {err:.4g}"
+        err = _excess(st.logits[0], ref)
+        assert err <= 0, f"{fmt} step {i}: logits exceed the bound by {err:.4g}"
 
 
 def test_one_layer_baseline_dims(golden_dir):
@@ -255,7 +278,8 @@ def test_one_layer_baseline_dims(golden_dir):
     # oracle: layer step + final norm + lm_head on the same weights
     om_layer = gr.make_layer(gr.BASELINE_DIMS, wl, 0)
     kc2, vc2 = kc.clone(), vc.clone()
-    y = gr.layer_step(gr.BASELINE_DIMS, om_layer, kc2, vc2, x, past)
+    with gr.accumulate("bf16"):  # the reference's own order: compared bit for bit with its golden output
+        y = gr.layer_step(gr.BASELINE_DIMS, om_layer, kc2, vc2, x, past)
     assert torch.equal(y.reshape(-1), g["y"])  # oracle == reference golden
     k_got, k_ref = eng.kv[0, 0, 0, :, past].cpu().float(), kc2[0, :, past].float()
     assert torch.allclose(k_got, k_ref, rtol=2 ** -6, atol=1e-2)  # new K row (RoPE'd), 1-ulp slack
@@ -263,7 +287,7 @@ def test_one_layer_baseline_dims(golden_dir):
     ref = torch.nn.functional.linear(hn, w["embed_tokens.weight"].cpu()).reshape(-1) / 8.0
     ref = ref.to(torch.bfloat16)
     got = st.logits[0].cpu()
-    assert (got.float() - ref.float()).abs().max() <= _logit_tol(ref)
+    assert _excess(got, ref) <= 0
     if _margin(ref) > _logit_tol(ref):
         assert int(st.out_ids[0]) == int(ref.float().argmax())
 
@@ -296,8 +320,8 @@ def test_batched_tensor_cores_teacher_forced(golden, fmt):
         ref = odec.step(tokens, T + i - (T - pl), valid)
         got = st.logits[:B].cpu()
         for b in range(B):
-            err = (got[b].float() - ref[b].float()).abs().max()
-            assert err <= _logit_tol(ref[b]), f"{fmt} step {i} stream {b}: {err:.4g}"
+            err = _excess(got[b], ref[b])
+            assert err <= 0, f"{fmt} step {i} stream {b}: logits exceed the bound by {err:.4g}"
             if _margin(ref[b]) > _logit_tol(ref[b]):
                 assert int(st.out_ids[b]) == int(ref[b].argmax())
         # the new cache rows (k after RoPE, v) equal the oracle's up to one
@@ -335,8 +359,8 @@ def _prefill_vs_oracle(d, w, fmt, emb, pl, max_len):
                     f"{fmt} stream {b} layer {li} {'kv'[kv]}: cache rows differ"
         ref = odec.last_logits[b]
         got = st.logits[b].cpu()
-        err = (got.float() - ref.float()).abs().max()
-        assert err <= _logit_tol(ref), f"{fmt} stream {b}: first-token logits differ by {err:.4g}"
+        err = _excess(got, ref)
+        assert err <= 0, f"{fmt} stream {b}: first-token logits exceed the bound by {err:.4g}"
         if _margin(ref) > _logit_tol(ref):
             assert int(st.out_ids[b]) == int(ref_ids[b])
 
