@@ -229,6 +229,68 @@ int sb_lm_head_argmax(const SbModel* model, const SbState* state, int32_t step, 
  * array: calls that overlap on the GPU race. */
 int sb_lm_head_argmax_static(const SbModel* model, const SbState* state, int32_t step, sb_stream_t stream);
 
+/* ---- speculative decoding loop on the device -------------------------------
+ * The verify / accept loop of SpeculativeDecoder.generate
+ * (src/starling/granite/speculative.py:400-539) as ONE CUDA graph: a setup
+ * kernel, then WHILE (continue) { SWITCH (k - 1) { the verify forward of
+ * [last emitted token, draft[draft_pos : draft_pos + k]] (sb_decode_step on
+ * verify[k - 1]) } ; control kernel }.  The control kernel applies the
+ * reference's rules on the device -- accept the longest prefix whose argmax
+ * equals the draft (stopping after an accepted EOS), emit the correction or
+ * the bonus token, move the cache position (the rewind), re-align the draft
+ * pointer on the last emitted token within 40 drafts, the stuck guard (8
+ * rounds), the chunk size 8 -> +4 up to 16 (2 after a boundary miss) -- and
+ * writes the next round's ids, cache slot and k, or ends the loop when an EOS
+ * was emitted, max_new_tokens are out, the draft is used up or k would be 0.
+ * The host reads the emitted ids once, after the loop; the single-step
+ * fallback decode that follows an exhausted draft stays with the caller
+ * (speculative.py:541-560).
+ *
+ * verify: HOST array of max_chunk states, verify[k-1] for k + 1 tokens
+ * (batch 1, m = k + 1, mode SB_MODE_VERIFY), all sharing one ids buffer
+ * (>= max_chunk + 1), one ctrl block and one out_ids buffer.  spec: device
+ * int32 [SB_SPEC_WORDS]: the host writes N_DRAFT, MAX_NEW, PROMPT and
+ * MAX_ROUNDS before each launch, the loop writes the rest.  emitted: device
+ * int64 [emit_capacity], emitted[0] = the prefill's token on entry.  The loop
+ * never runs more than MAX_ROUNDS verify forwards (SB_SPEC_ERR = 1 if it
+ * stopped there).  No reference counterpart for the graph itself (the
+ * reference syncs with the host after every verify). */
+#define SB_SPEC_N_EMIT 0     /* ids in emitted[] */
+#define SB_SPEC_CACHE_POS 1  /* cache position after the last accepted token */
+#define SB_SPEC_DRAFT_POS 2
+#define SB_SPEC_CHUNK 3      /* current chunk size */
+#define SB_SPEC_STUCK 4
+#define SB_SPEC_ACCEPTED 5   /* accepted draft tokens (incl. re-alignments) */
+#define SB_SPEC_VERIFIES 6   /* verify forwards run */
+#define SB_SPEC_STOPPED 7    /* 1: an EOS was emitted */
+#define SB_SPEC_ROUNDS 8
+#define SB_SPEC_K 9          /* draft tokens in the round in flight */
+#define SB_SPEC_ERR 10       /* 1: MAX_ROUNDS reached */
+#define SB_SPEC_N_DRAFT 11   /* in */
+#define SB_SPEC_MAX_NEW 12   /* in */
+#define SB_SPEC_PROMPT 13    /* in: cache position of the first verify */
+#define SB_SPEC_MAX_ROUNDS 14 /* in */
+#define SB_SPEC_WORDS 16
+
+typedef struct SbSpecLoop {
+  const SbState* verify; /* HOST array [max_chunk] */
+  int32_t max_chunk;
+  int32_t draft_capacity;
+  int32_t emit_capacity;
+  int32_t _pad;
+  int64_t eos_id;
+  int32_t* spec;         /* [SB_SPEC_WORDS] */
+  int64_t* emitted;      /* [emit_capacity] */
+  const int64_t* draft;  /* [draft_capacity] */
+} SbSpecLoop;
+
+/* build and instantiate the loop's graph (captures every verify forward on
+ * an internal stream); *loop_out receives an opaque handle */
+int sb_spec_loop_create(const SbModel* model, const SbSpecLoop* loop, void** loop_out);
+/* run the loop once on `stream` (asynchronous) */
+int sb_spec_loop_launch(void* loop, sb_stream_t stream);
+void sb_spec_loop_destroy(void* loop);
+
 /* ---- prefill --------------------------------------------------------------
  * Prefill of `batch` right-padded prompts of T positions each, the eager
  * GraniteModel forward of LLMMega.prefill / BatchedLLMMega.prefill

@@ -21,6 +21,10 @@ SB_MODE_DECODE, SB_MODE_VERIFY, SB_MODE_FIRST = 0, 1, 2
 SB_OP_QKV, SB_OP_ATTN, SB_OP_O, SB_OP_GATE_UP, SB_OP_DOWN, SB_OP_LM_HEAD = range(6)
 SB_STEP_PER_OP, SB_STEP_FUSED = 1, 2
 SB_NVFP4_AUTO, SB_NVFP4_BLOCK_SCALED, SB_NVFP4_MMA_SYNC = 0, 1, 2
+(SB_SPEC_N_EMIT, SB_SPEC_CACHE_POS, SB_SPEC_DRAFT_POS, SB_SPEC_CHUNK, SB_SPEC_STUCK, SB_SPEC_ACCEPTED,
+ SB_SPEC_VERIFIES, SB_SPEC_STOPPED, SB_SPEC_ROUNDS, SB_SPEC_K, SB_SPEC_ERR, SB_SPEC_N_DRAFT, SB_SPEC_MAX_NEW,
+ SB_SPEC_PROMPT, SB_SPEC_MAX_ROUNDS) = range(15)
+SB_SPEC_WORDS = 16
 
 vp = C.c_void_p
 
@@ -63,6 +67,14 @@ class SbState(C.Structure):
     ]
 
 
+class SbSpecLoop(C.Structure):
+    _fields_ = [
+        ("verify", C.POINTER(SbState)), ("max_chunk", C.c_int32), ("draft_capacity", C.c_int32),
+        ("emit_capacity", C.c_int32), ("_pad", C.c_int32), ("eos_id", C.c_int64),
+        ("spec", vp), ("emitted", vp), ("draft", vp),
+    ]
+
+
 EXPORTS = [
     "sb_last_error", "sb_version", "sb_workspace_bytes", "sb_decode_step", "sb_lm_head_argmax",
     "sb_linear", "sb_dequant_f32", "sb_dequant_bf16", "sb_rmsnorm", "sb_silu_mul",
@@ -70,6 +82,7 @@ EXPORTS = [
     "sb_lm_head_argmax_static", "sb_linear_ex", "sb_linear_workspace_bytes", "sb_launch_count",
     "sb_prefill", "sb_prefill_workspace_bytes", "sb_prefill_block_rows", "sb_decode_step_ex",
     "sb_decode_step_fused_ok", "sb_decode_step_scratch_offset", "sb_set_nvfp4_path",
+    "sb_spec_loop_create", "sb_spec_loop_launch", "sb_spec_loop_destroy",
 ]
 
 
@@ -123,6 +136,10 @@ def load() -> C.CDLL:
     lib.sb_residual_scale.argtypes = [vp, vp, vp, C.c_int64, C.c_float, vp]
     lib.sb_rope.argtypes = [vp, C.c_int32, C.c_int32, vp, vp, vp, vp]
     lib.sb_argmax_bf16.argtypes = [vp, C.c_int32, C.c_int32, vp, vp]
+    lib.sb_spec_loop_create.argtypes = [C.POINTER(SbModel), C.POINTER(SbSpecLoop), C.POINTER(vp)]
+    lib.sb_spec_loop_launch.argtypes = [vp, vp]
+    lib.sb_spec_loop_destroy.argtypes = [vp]
+    lib.sb_spec_loop_destroy.restype = None
     _lib = lib
     return lib
 

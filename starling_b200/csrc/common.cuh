@@ -16,6 +16,8 @@ typedef __nv_bfloat16 bf16;
 
 // Kernels launched by this library (host-side counter, reported by sb_launch_count).
 void note_launch();
+// Record the message sb_last_error() returns; returns `code`.
+int set_error(int code, const char* fmt, ...);
 
 // ---- rounding helpers -----------------------------------------------------
 // Every reference op rounds its result to bf16; these make the rounding

@@ -76,16 +76,21 @@ class EngineState:
     def __init__(self, eng: "GraniteEngine", batch: int, m: int, mode: int, out_steps: int = 1,
                  finished: bool = False, prompt_len: Optional[torch.Tensor] = None,
                  rope_off: Optional[torch.Tensor] = None, keep_logits: bool = True,
-                 use_pdl: bool = True):
+                 use_pdl: bool = True, share: Optional["EngineState"] = None):
+        """share: use that state's ids, ctrl and out_ids buffers (at least as
+        large as this state's) instead of new ones."""
         d, dev = eng.dims, eng.device
         T = batch * m
         self.batch, self.m = batch, m
-        self.ids = torch.zeros(T, dtype=torch.int64, device=dev)
-        self.ctrl = torch.zeros(SB_CTRL_WORDS, dtype=torch.int32, device=dev)
+        if share is not None and (share.ids.numel() < T or share.out_ids.numel() < max(out_steps, 1) * max(batch, m)):
+            raise ValueError("the shared state's buffers are smaller than this state's")
+        self.ids = share.ids if share is not None else torch.zeros(T, dtype=torch.int64, device=dev)
+        self.ctrl = share.ctrl if share is not None else torch.zeros(SB_CTRL_WORDS, dtype=torch.int32, device=dev)
         self.prompt_len = None if prompt_len is None else prompt_len.to(dev, torch.int32).contiguous()
         self.rope_off = None if rope_off is None else rope_off.to(dev, torch.int32).contiguous()
         self.finished = torch.zeros(batch, dtype=torch.int32, device=dev) if finished else None
-        self.out_ids = torch.zeros(max(out_steps, 1) * max(batch, m), dtype=torch.int64, device=dev)
+        self.out_ids = (share.out_ids if share is not None else
+                        torch.zeros(max(out_steps, 1) * max(batch, m), dtype=torch.int64, device=dev))
         self.hidden = torch.zeros(T, d.hidden, dtype=BF16, device=dev)
         self.q = torch.zeros(T, d.n_q * d.head_dim, dtype=BF16, device=dev)
         self.attn = torch.zeros(T, d.n_q * d.head_dim, dtype=BF16, device=dev)

@@ -13,13 +13,22 @@ The verify forward is ``sb_decode_step`` with m = L: every projection is a
 skinny GEMM over the L rows, attention applies the causal verify mask
 (query i sees keys [0, start+i], speculative.py:755-765) on the device, and
 the lm_head kernel returns the L argmaxes plus the accepted-prefix length.
-One CUDA graph per L is captured up front (speculative.py:685-781).  The CTC
-draft extraction (speculative.py:93-236) belongs to the encoder side and is
-not part of this package: callers pass the draft ids.
+One CUDA graph per L is captured up front (speculative.py:685-781).
+
+By default (``device_loop=True``) the whole verify / accept loop runs on the
+device as one CUDA graph (``sb_spec_loop_*``): a WHILE node over rounds whose
+body switches to the captured verify forward of the round's chunk length,
+followed by a control kernel that applies the rules above and plans the next
+round, so the host reads the emitted ids once, after the loop, instead of
+after every verify.  ``device_loop=False`` runs the same loop on the host, one
+graph replay and one device->host read per round, as the reference does.
+The CTC draft extraction (speculative.py:93-236) belongs to the encoder side
+and is not part of this package: callers pass the draft ids.
 """
 
 from __future__ import annotations
 
+import ctypes as C
 import time
 from dataclasses import dataclass
 from typing import Any, Optional
@@ -27,6 +36,7 @@ from typing import Any, Optional
 import torch
 
 from . import _lib
+from ._lib import check, ptr
 from .config import LLM_EOS_TOKEN_ID
 
 
@@ -52,12 +62,14 @@ class SpeculativeDecoder:
     BOUNDARY_CHUNK: int = 2
     MAX_CHUNK: int = 16
 
-    def __init__(self, llm: Any, embed_tokens: Any = None) -> None:
+    def __init__(self, llm: Any, embed_tokens: Any = None, device_loop: bool = True) -> None:
         self.llm = llm
         self.engine = llm.engine
         self.embed_tokens = embed_tokens
+        self.device_loop = bool(device_loop)
         self._verify_graphs: dict = {}
         self._pinned = torch.zeros(self.MAX_CHUNK + 1, dtype=torch.int64).pin_memory()
+        self._loop = None  # the device loop's graph and buffers, built on first use
 
     # ------------------------------------------------------------------ #
     def _capture_verify_graph(self, L: int) -> None:
@@ -98,9 +110,117 @@ class SpeculativeDecoder:
         return res[:L], res[L]
 
     # ------------------------------------------------------------------ #
+    def _device_loop(self, eos: int, n_draft: int) -> dict:
+        """The loop graph (sb_spec_loop_create) and its buffers: built once,
+        rebuilt only for a new EOS id or a longer draft."""
+        lp = self._loop
+        if lp is not None and lp["eos"] == eos and lp["draft"].numel() >= n_draft:
+            return lp
+        if lp is not None:
+            self.engine.lib.sb_spec_loop_destroy(lp["handle"])
+            self._loop = None
+        eng, llm = self.engine, self.llm
+        dev = eng.device
+        big = eng.new_state(1, self.MAX_CHUNK + 1, _lib.SB_MODE_VERIFY, out_steps=1, use_pdl=False)
+        states = [eng.new_state(1, k + 1, _lib.SB_MODE_VERIFY, out_steps=1, use_pdl=False, share=big)
+                  for k in range(1, self.MAX_CHUNK)] + [big]
+        for st in states:  # every kernel configuration runs once before it is captured
+            st.ids.fill_(1)
+            st.set_slot(llm.max_cache_len - st.m - 2)
+            eng.decode_step(st, 0)
+        torch.cuda.synchronize()
+        cap = max(4096, n_draft)
+        buf = dict(spec=torch.zeros(_lib.SB_SPEC_WORDS, dtype=torch.int32, device=dev),
+                   emitted=torch.zeros(llm.max_cache_len + 2, dtype=torch.int64, device=dev),
+                   draft=torch.zeros(cap, dtype=torch.int64, device=dev))
+        arr = (_lib.SbState * self.MAX_CHUNK)(*[st.c for st in states])
+        spec = _lib.SbSpecLoop()
+        spec.verify = C.cast(arr, C.POINTER(_lib.SbState))
+        spec.max_chunk = self.MAX_CHUNK
+        spec.draft_capacity = cap
+        spec.emit_capacity = buf["emitted"].numel()
+        spec.eos_id = int(eos)
+        spec.spec, spec.emitted, spec.draft = ptr(buf["spec"]), ptr(buf["emitted"]), ptr(buf["draft"])
+        handle = C.c_void_p()
+        check(eng.lib.sb_spec_loop_create(C.byref(eng.cmodel), C.byref(spec), C.byref(handle)), "sb_spec_loop_create")
+        self._loop = dict(handle=handle, states=states, eos=eos, **buf)
+        return self._loop
+
+    def __del__(self):
+        lp = getattr(self, "_loop", None)
+        if lp is not None:
+            try:
+                self.engine.lib.sb_spec_loop_destroy(lp["handle"])
+            except Exception:
+                pass
+
     @torch.inference_mode()
     def generate(self, inputs_embeds: torch.Tensor, draft: list, max_new_tokens: int = 200,
                  eos_token_id: int = LLM_EOS_TOKEN_ID) -> SpecResult:
+        if not self.device_loop:
+            return self._generate_host(inputs_embeds, draft, max_new_tokens, eos_token_id)
+        llm = self.llm
+        P = inputs_embeds.shape[1]
+        draft = [int(t) for t in draft]
+        draft_count = len(draft)
+        max_safe = llm.max_cache_len - P + 1
+        if max_new_tokens > max_safe:
+            raise ValueError(
+                f"max_new_tokens={max_new_tokens} would overflow the static KV "
+                f"cache (prompt T={P}, max_cache_len={llm.max_cache_len})."
+            )
+        if inputs_embeds.shape[0] != 1:
+            raise ValueError("SpeculativeDecoder only supports batch=1.")
+        if max_new_tokens <= 0:
+            return self._finalize([], 0.0, draft_count, 0, 0, 0, 0)
+        first = llm.prefill(inputs_embeds)
+        emitted = [int(first.item())]
+        if emitted[-1] == eos_token_id or len(emitted) >= max_new_tokens:
+            return self._finalize(emitted, 0.0, draft_count, 0, 0, 0, 0)
+        if not llm._captured:
+            llm.capture(first, P)
+        lp = self._device_loop(int(eos_token_id), draft_count)
+        t0 = time.perf_counter()
+        inputs = torch.zeros(_lib.SB_SPEC_WORDS, dtype=torch.int32)
+        inputs[_lib.SB_SPEC_N_DRAFT] = draft_count
+        inputs[_lib.SB_SPEC_MAX_NEW] = max_new_tokens
+        inputs[_lib.SB_SPEC_PROMPT] = P
+        # each round advances the draft or emits a token, except up to 8 stuck rounds in a row
+        inputs[_lib.SB_SPEC_MAX_ROUNDS] = 8 * (draft_count + max_new_tokens) + 16
+        lp["spec"].copy_(inputs)
+        lp["emitted"][:1].copy_(first.reshape(-1)[:1])
+        if draft_count:
+            lp["draft"][:draft_count].copy_(torch.tensor(draft, dtype=torch.int64))
+        check(self.engine.lib.sb_spec_loop_launch(lp["handle"], _lib.current_stream()), "sb_spec_loop_launch")
+        out = torch.cat([lp["spec"].long(), lp["emitted"]]).tolist()  # the one device->host read
+        spec, ids = out[:_lib.SB_SPEC_WORDS], out[_lib.SB_SPEC_WORDS:]
+        if spec[_lib.SB_SPEC_ERR]:
+            raise _lib.StarlingError(f"speculative loop stopped at its round limit or capacity (state {spec})")
+        emitted = ids[:spec[_lib.SB_SPEC_N_EMIT]]
+        accepted, verify_forwards = spec[_lib.SB_SPEC_ACCEPTED], spec[_lib.SB_SPEC_VERIFIES]
+        cache_pos = spec[_lib.SB_SPEC_CACHE_POS]
+        decode_steps = 0
+        if not spec[_lib.SB_SPEC_STOPPED]:
+            # single-step fallback once the draft is exhausted (speculative.py:541-560)
+            while len(emitted) < max_new_tokens:
+                llm._prime(torch.tensor([emitted[-1]], device=llm.state.ids.device), cache_pos)
+                if llm._captured:
+                    llm._graph.replay()
+                else:
+                    llm._decode_step_eager()
+                decode_steps += 1
+                tid = int(llm.state.out_ids[0].item())
+                emitted.append(tid)
+                cache_pos += 1
+                if tid == eos_token_id:
+                    break
+        torch.cuda.synchronize()
+        return self._finalize(emitted, (time.perf_counter() - t0) * 1000.0, draft_count, accepted,
+                              verify_forwards, decode_steps, 0)
+
+    @torch.inference_mode()
+    def _generate_host(self, inputs_embeds: torch.Tensor, draft: list, max_new_tokens: int = 200,
+                       eos_token_id: int = LLM_EOS_TOKEN_ID) -> SpecResult:
         llm = self.llm
         P = inputs_embeds.shape[1]
         draft = [int(t) for t in draft]

@@ -52,11 +52,12 @@ def test_struct_layout_matches_header(tmp_path):
         '#include <stdio.h>\n#include <stddef.h>\n#include "starling_b200.h"\n'
         "#define P(T, f) printf(#T \".\" #f \" %zu\\n\", offsetof(T, f));\n"
         "int main(void){\n"
-        'printf("SbLinear %zu\\nSbLayer %zu\\nSbModel %zu\\nSbState %zu\\n", sizeof(SbLinear), sizeof(SbLayer),'
-        " sizeof(SbModel), sizeof(SbState));\n"
+        'printf("SbLinear %zu\\nSbLayer %zu\\nSbModel %zu\\nSbState %zu\\nSbSpecLoop %zu\\n", sizeof(SbLinear),'
+        " sizeof(SbLayer), sizeof(SbModel), sizeof(SbState), sizeof(SbSpecLoop));\n"
         "P(SbLinear, w) P(SbLinear, global_scale) P(SbLinear, w_tc) P(SbLinear, w_bs) P(SbLayer, qkv) P(SbLayer, k_cache) P(SbModel, eps)"
         " P(SbModel, embed) P(SbModel, lm_head) P(SbModel, layers) P(SbState, eos_id) P(SbState, ids)"
-        " P(SbState, workspace_bytes)\nreturn 0;}\n"
+        " P(SbState, workspace_bytes) P(SbSpecLoop, max_chunk) P(SbSpecLoop, eos_id) P(SbSpecLoop, spec)"
+        " P(SbSpecLoop, draft)\nreturn 0;}\n"
     )
     exe = tmp_path / "layout"
     subprocess.run(["gcc", "-I", str(REPO / "include"), str(src), "-o", str(exe)], check=True)
@@ -65,6 +66,7 @@ def test_struct_layout_matches_header(tmp_path):
     assert int(out["SbLayer"]) == C.sizeof(_lib.SbLayer)
     assert int(out["SbModel"]) == C.sizeof(_lib.SbModel)
     assert int(out["SbState"]) == C.sizeof(_lib.SbState)
+    assert int(out["SbSpecLoop"]) == C.sizeof(_lib.SbSpecLoop)
     for key, val in out.items():
         if "." in key:
             t, f = key.split(".")

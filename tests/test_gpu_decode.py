@@ -433,3 +433,34 @@ def test_lm_head_argmax_full_vocab(fmt, B):
     wd = quant.dequantize(fmt, quant.quantize(fmt, w["embed_tokens.weight"]))
     ref = ((xn @ wd.T).to(torch.bfloat16).float() / d.logits_scaling).to(torch.bfloat16).float()
     assert (logits - ref).abs().max() <= 2.0 ** -6 * ref.abs().max()
+
+
+def _drafts(ref_ids, vocab):
+    """Drafts over the greedy continuation: exact, corrupted every 5th token,
+    with a token inserted (re-alignment), random (stuck guard), short."""
+    g = torch.Generator().manual_seed(9)
+    cont = ref_ids[1:]
+    bad = [t if (i % 5) != 4 else int(torch.randint(0, vocab, (1,), generator=g)) for i, t in enumerate(cont)]
+    ins = cont[:6] + [int(torch.randint(0, vocab, (1,), generator=g))] + cont[6:]
+    rnd = torch.randint(0, vocab, (len(cont),), generator=g).tolist()
+    return {"exact": cont, "corrupt5": bad, "insert": ins, "random": rnd, "short": cont[:5]}
+
+
+@pytest.mark.parametrize("kind", ["exact", "corrupt5", "insert", "random", "short"])
+def test_speculative_device_loop_matches_host_loop(golden, kind):
+    """The loop as one device graph (WHILE over rounds, SWITCH over chunk
+    lengths, control kernel) against the same loop on the host (one sync per
+    verify): identical emitted ids and identical counts of verify forwards,
+    accepted drafts and fallback decode steps."""
+    d, w, g = golden
+    emb = g["inputs_embeds"].cuda()
+    llm = LLMMega(weights=w, dims=d.__dict__, max_cache_len=96)
+    ref = MultiStepLLMMega(engine=llm.engine, steps_per_replay=4).generate(emb, max_new_tokens=40).ids[0].tolist()
+    draft = _drafts(ref, d.vocab)[kind]
+    host = SpeculativeDecoder(llm, device_loop=False).generate(emb, draft, max_new_tokens=40)
+    dev = SpeculativeDecoder(llm, device_loop=True).generate(emb, draft, max_new_tokens=40)
+    assert dev.ids[0].tolist() == host.ids[0].tolist()
+    assert (dev.verify_forwards, dev.accepted, dev.decode_steps) == \
+        (host.verify_forwards, host.accepted, host.decode_steps)
+    if kind == "exact":
+        assert host.accepted > 0
