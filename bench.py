@@ -224,6 +224,8 @@ PROFILED_TRAFFIC = {
     ("b48", "attention"): (80.179456e6 + 2.41664e6, 61.5e6, "profiles/attention_b48_decode.md"),
     ("b48", "gate_up"): (33.9008e6, 33.62e6, "profiles/tcgen05_gemm_gate_up_fp8_b48.md"),
     ("b1", "gate_up"): (18.93376e6, 18.87e6, "profiles/gemv_gate_up_nvfp4_b1.md"),
+    # 4 layers + lm_head: 4 x 34.21 MB + 115.61 MB of NVFP4 weights + K/V rows
+    ("b1", "step"): (255.4e6 + 4.4e6, 4 * 34.21e6 + 115.61e6 + 2.6e6, "profiles/fused_step_b1_nvfp4.md"),
 }
 
 
@@ -444,6 +446,20 @@ def bench_workload(name, args, rank, world, local_rank, dev, with_cpu):
     value = B * K * world / (t["ms"] / 1000.0)
     peak, peak_kind = _peaks()
     dom = dominant_kernel(eng, t["state"], d, B, inp.T, fmt, t["reset"], name)
+    if eng.fused_step_ok(t["state"]) and B == 1:
+        # the step is ONE launch of the fused kernel: its roofline is the
+        # step's algorithmic bytes (every weight once + the valid K/V rows)
+        # over the device time of a step
+        wbytes = eng.lm_head.nbytes + sum(L[k].nbytes for L in eng.layers for k in ("qkv", "o", "gate_up", "down"))
+        kvb = (inp.T + 1 + K // 2) * d.layers * 2 * d.n_kv * d.head_dim * 2  # mean context over the timed steps
+        step_s = t["ms"] / K / 1e3
+        gbs = (wbytes + kvb) / step_s / 1e9
+        prof = PROFILED_TRAFFIC[("b1", "step")]
+        dom["roofline"] = {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                           "frac": round(gbs / peak, 4), "traffic": round(prof[0] * (wbytes + kvb) / prof[1]),
+                           "traffic_source": f"ncu capture in {prof[2]}, scaled by algorithmic bytes",
+                           "kernel": "k_step (the whole decode step, one cooperative launch)",
+                           "algorithmic_bytes_per_launch": wbytes + kvb, "avg_launch_us": round(step_s * 1e6, 3)}
     dom["roofline"]["peak_kind"] = peak_kind
     e2e = run_e2e(eng, wl, inp, B, dev, world)
     out = {

@@ -175,12 +175,14 @@ int32_t sb_set_nvfp4_path(int32_t mode);
  * (src/starling/granite/multistep.py:157-188); with m > 1 it is the verify
  * forward SpeculativeDecoder._verify_step_fused (speculative.py:598-680) with
  * the acceptance compare of speculative.py:430-459 fused on device.
- * `step` indexes out_ids in DECODE mode.  About 5 launches per layer
- * (sb_decode_step_ex selects the one-launch fused step instead). */
+ * `step` indexes out_ids in DECODE mode.  One-token forwards (batch * m ==
+ * 1, B = 1 decode) run as the one-launch fused step where it serves them
+ * (see sb_decode_step_ex), every other forward as about 5 launches per
+ * layer. */
 int sb_decode_step(const SbModel* model, const SbState* state, int32_t step, sb_stream_t stream);
 
 /* sb_decode_step with the kernel path chosen by the caller:
- * flags = 0 or SB_STEP_PER_OP: the per-op kernels (sb_decode_step);
+ * flags = 0: as sb_decode_step; SB_STEP_PER_OP: the per-op kernels;
  * SB_STEP_FUSED: forwards of up to 8 token rows (batch * m) as ONE
  * cooperative launch (weights streamed through shared memory across layers,
  * activations handed between CTAs through flagged words; needs one weight

@@ -490,8 +490,11 @@ int sb_decode_step_ex(const SbModel* md, const SbState* st, int32_t step, int32_
   if (!md->layers || md->n_layers < 1) return fail(SB_ERR_ARG, "no layers");
   if ((flags & SB_STEP_PER_OP) && (flags & SB_STEP_FUSED)) return fail(SB_ERR_ARG, "conflicting step flags");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  // flags 0: the default path, the per-op kernels
-  if (flags & SB_STEP_FUSED) {
+  // flags 0: one-token forwards (B = 1 decode) as the fused step where it
+  // serves them (measured faster there: 1.46 vs 1.53 ms per 40-layer NVFP4
+  // step on B200), everything else on the per-op kernels
+  const bool fused_default = flags == 0 && st->batch * st->m == 1;
+  if ((flags & SB_STEP_FUSED) || fused_default) {
     StepPlan pl;
     const char* why = "";
     if (step_plan(md, st, pl, &why)) {
@@ -502,7 +505,7 @@ int sb_decode_step_ex(const SbModel* md, const SbState* st, int32_t step, int32_
       if (rc != 0) return fail(rc, "fused step launch: %s", rc < 1000 ? cudaGetErrorString((cudaError_t)rc) : "config");
       return 0;
     }
-    return fail(SB_ERR_CONFIG, "the fused step does not serve this forward: %s", why);
+    if (flags & SB_STEP_FUSED) return fail(SB_ERR_CONFIG, "the fused step does not serve this forward: %s", why);
   }
   for (int l = 0; l < md->n_layers; ++l)
     for (int op = SB_OP_QKV; op <= SB_OP_DOWN; ++op) SB_TRY(launch_op(md, st, l, op, step, s));

@@ -208,9 +208,10 @@ class GraniteEngine:
         return EngineState(self, batch, m, mode, **kw)
 
     # ---- native calls ----------------------------------------------------- #
-    # decode-step kernel path: "auto" (the library's default: per-op kernels),
-    # "fused"
-    # (required), "prefer_fused" (fused where it serves the forward) or "ops"
+    # decode-step kernel path: "auto" (the library's default: the fused step for
+    # one-token forwards where it serves them, else the per-op kernels),
+    # "fused" (required), "prefer_fused" (fused wherever it serves the
+    # forward) or "ops" (per-op kernels only)
     step_path = "auto"
 
     def decode_step(self, st: EngineState, step: int = 0) -> None:
