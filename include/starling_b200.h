@@ -202,8 +202,11 @@ size_t sb_decode_step_scratch_offset(const SbModel* model, int32_t tokens);
 
 /* Launch ONE kernel of the decode step on its own (profiling / live timing
  * of a single kernel with the step's exact configuration): op = SB_OP_*,
- * layer ignored for SB_OP_LM_HEAD.  No reference counterpart (the reference
- * step has no separable kernels of this kind). */
+ * layer ignored for SB_OP_LM_HEAD.  Where the o projection runs on the
+ * tensor-core GEMM (9..128 token rows) the attention launch writes its
+ * activation operand, so SB_OP_O computes from what the last SB_OP_ATTN of
+ * the same state and token count wrote.  No reference counterpart (the
+ * reference step has no separable kernels of this kind). */
 #define SB_OP_QKV 0
 #define SB_OP_ATTN 1
 #define SB_OP_O 2

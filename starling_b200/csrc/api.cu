@@ -353,10 +353,37 @@ static int launch_lm_head(const SbModel* md, const SbState* st, int step, cudaSt
   return run_linear(md->lm_head, p, tcs, tcb, st->use_pdl != 0, s);
 }
 
+// Whether the attention kernel writes the o-projection's tcgen05 operand
+// itself (so the o GEMM runs without a preparation launch): the o projection
+// takes the tensor-core GEMM with one token tile, and for fp8 its K split has
+// one rank per KV head (each rank's 512 columns are one attention CTA's
+// output, scaled by that CTA's own power of two); bf16 operands need no scale.
+static bool o_operand_from_attn(const SbModel* md, const SbState* st, const SbLayer& L, void* tcs, TcPlan& tp) {
+  const int T = st->batch * st->m;
+  if (!tcs || !lin_ok(L.o) || !tc_plan_for(L.o, T, tp) || tp.mtiles != 1) return false;
+  if (L.o.fmt != SB_FMT_FP8) return true;
+  const int G = md->n_q / md->n_kv;
+  return tp.split == md->n_kv && tp.kb % tp.split == 0 && tp.kb / tp.split == G;
+}
+
 static int launch_attention(const SbModel* md, const SbState* st, int l, cudaStream_t s) {
   const SbLayer& L = md->layers[l];
   AttnParams a;
   memset(&a, 0, sizeof(a));
+  {
+    size_t tcb = 0;
+    void* tcs = nullptr;
+    TcPlan tp;
+    SB_TRY(tc_scratch_of(md, st, tcs, tcb));
+    if (o_operand_from_attn(md, st, L, tcs, tp)) {
+      const int T = st->batch * st->m;
+      a.opnd = static_cast<uint8_t*>(tcs);
+      a.opnd_shift = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(tcs) + tc_shift_offset(L.o.fmt, L.o.k, T));
+      a.opnd_mp = tp.mp;
+      a.opnd_np = tp.np;
+      a.opnd_fp8 = L.o.fmt == SB_FMT_FP8 ? 1 : 0;
+    }
+  }
   a.q = st->q;
   a.k_cache = L.k_cache;
   a.v_cache = L.v_cache;
@@ -440,6 +467,15 @@ static int launch_op(const SbModel* md, const SbState* st, int l, int op, int st
     p.epi = EPI_RESID;
     p.y = st->hidden;
     p.res_mult = md->res_mult;
+    TcPlan tp;
+    if (op == SB_OP_O && o_operand_from_attn(md, st, L, tcs, tp)) {  // the attention wrote the operand
+      const size_t need = tc_operand_bytes(lin.fmt, lin.k, T);
+      if (need > tcb) return fail(SB_ERR_ARG, "tensor-core operand scratch too small (%zu < %zu)", tcb, need);
+      const int rc = tc_launch(p, lin.w_tc, tcs, tp, lin.fmt, pdl, s, true);
+      if (rc != 0) return fail(rc, "tensor-core gemm launch (o, n=%d k=%d m=%d): %s", p.n, p.k, p.m,
+                               rc < 1000 ? cudaGetErrorString((cudaError_t)rc) : "config");
+      return 0;
+    }
     return run_linear(lin, p, tcs, tcb, pdl, s);
   }
   // gate/up: RMSNorm -> interleaved gate|up -> SiLU(gate)*up

@@ -33,6 +33,7 @@
 #include <cudaTypedefs.h>
 
 #include "attention.cuh"
+#include "operand.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -416,6 +417,16 @@ __global__ void __launch_bounds__(256, 2)
 
   // ---- combine the cluster's partial outputs, round, store -----------------------------
   if (split > 1) cg::this_cluster().sync(); else __syncthreads();
+  // o-projection operand: the largest |output| of each token's slice, as the
+  // outputs are stored (a slice is G * 128 consecutive i, a multiple of 32,
+  // so every warp iteration belongs to one token); float bits of |x| order
+  // like the values
+  int* s_tmax = reinterpret_cast<int*>(wmax);  // [m_per] (the row-max scratch is free by now)
+  const bool opnd8 = p.opnd && p.opnd_fp8;
+  if (rank == 0 && opnd8) {
+    for (int mi = tid; mi < p.m_per; mi += blockDim.x) s_tmax[mi] = 0;
+    __syncthreads();
+  }
   if (rank == 0) {
     for (int i = tid; i < R * 128; i += blockDim.x) {
       float s = 0.f;
@@ -424,9 +435,43 @@ __global__ void __launch_bounds__(256, 2)
       const int mi = r / G, gi = r % G;
       const size_t t = static_cast<size_t>(zb) * p.m_per + mi;
       p.out[t * p.n_q * 128 + (kvh * G + gi) * 128 + dd] = f_to_bf16_bits(s);
+      if (p.opnd) {
+        const float v = bf(s);  // the value the o-projection reads (only this thread reads outp[i] here)
+        outp[i] = v;
+        if (opnd8) {
+          const float m = warp_max(fabsf(v));
+          if (lane == 0) atomicMax(s_tmax + mi, __float_as_int(m));
+        }
+      }
     }
   }
   if (split > 1) cg::this_cluster().sync();
+  if (rank == 0 && p.opnd) {
+    // this (stream, KV head)'s output slice -- columns kvh * G * 128 .. of each
+    // of its m_per tokens -- as the o-projection's operand, one 16-byte chunk
+    // per thread
+    __syncthreads();
+    const size_t kb_bytes = static_cast<size_t>(p.opnd_np) * 128;
+    const int slice = G * 128;  // elements of the slice (one K-split rank of the o GEMM)
+    const int per = opnd8 ? slice / 16 : slice / 8;  // chunks per token
+    for (int j = tid; j < p.m_per * per; j += blockDim.x) {
+      const int mi = j / per, cj = j % per;
+      const int t = zb * p.m_per + mi;
+      const float* row = outp + static_cast<size_t>(mi) * slice;  // rows mi*G .. mi*G+G-1, contiguous
+      if (opnd8) {
+        const int shift = tc_fp8_shift(__int_as_float(s_tmax[mi]));
+        uint4 w0, w1;
+        e4m3_split16(row + cj * 16, shift, w0, w1);
+        const int c = kvh * per + cj;  // 16-byte chunk of e4m3 along K
+        *reinterpret_cast<uint4*>(p.opnd + tc_operand_offset(kb_bytes, t, c)) = w0;
+        *reinterpret_cast<uint4*>(p.opnd + tc_operand_offset(kb_bytes, p.opnd_mp + t, c)) = w1;
+        if (cj == 0) p.opnd_shift[kvh * p.opnd_mp + t] = shift;
+      } else {
+        const int c = kvh * per + cj;  // 16-byte chunk of bf16 along K
+        *reinterpret_cast<uint4*>(p.opnd + tc_operand_offset(kb_bytes, t, c)) = pack8(row + cj * 8);
+      }
+    }
+  }
 }
 
 // ---- host side ------------------------------------------------------------------

@@ -19,6 +19,14 @@ struct AttnParams {
   long long cache_rows;       // max_batch * n_kv * max_len (rows of 128 of each cache)
   int qblocks;                // query blocks of m_per tokens per stream: block qb has its tokens
                               // at cache slots ctrl[SLOT] + qb * m_per + (0..m_per-1) (prefill); 1 otherwise
+  // When opnd is set (qblocks == 1), the output rows are also written as the
+  // o-projection GEMM's activation operand (one token tile, gemm_tc.cu's
+  // layout): bf16 rows, or (opnd_fp8) two e4m3 terms per element with one
+  // power-of-two shift per (KV head, token) -- the o GEMM splits K over n_kv
+  // ranks, one KV head's n_q / n_kv heads each -- in opnd_shift[kvh][opnd_mp].
+  uint8_t* opnd;
+  int32_t* opnd_shift;
+  int opnd_mp, opnd_np, opnd_fp8;
 };
 
 int attn_tile_keys(int split);

@@ -47,6 +47,7 @@
 #include <cooperative_groups.h>
 
 #include "gemm_tc.cuh"
+#include "operand.cuh"
 #include "tc_common.cuh"
 #include "gemv_epi.cuh"
 #include "tc_epi.cuh"
@@ -79,36 +80,6 @@ __device__ __forceinline__ float block_max256(float v, float* s_red) {
   return t;
 }
 
-// 16 activation values -> the two e4m3 terms of the fp8 operand, x 2^shift =
-// t0 + t1 / 16 with t0 = e4m3(x 2^shift), t1 = e4m3(16 (x 2^shift - t0)), both
-// round-to-nearest saturating, bytes in element order.  The power-of-two
-// scaling and both subtractions are exact; the conversions go two at a time.
-__device__ __forceinline__ void e4m3_split16(const float* f, int shift, uint4& w0, uint4& w1) {
-  const bool fast = shift >= -126 && shift <= 126;  // 2^shift is a normal float
-  const float s2 = fast ? __int_as_float((shift + 127) << 23) : 0.f;
-  uint32_t a[4], b[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    float v[4], r[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) v[e] = fast ? f[4 * i + e] * s2 : ldexpf(f[4 * i + e], shift);
-    const uint32_t p0 = __nv_cvt_float2_to_fp8x2(make_float2(v[0], v[1]), __NV_SATFINITE, __NV_E4M3);
-    const uint32_t p1 = __nv_cvt_float2_to_fp8x2(make_float2(v[2], v[3]), __NV_SATFINITE, __NV_E4M3);
-    const float2 d0 = __half22float2(__half2(__nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(p0), __NV_E4M3)));
-    const float2 d1 = __half22float2(__half2(__nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(p1), __NV_E4M3)));
-    r[0] = (v[0] - d0.x) * 16.f;
-    r[1] = (v[1] - d0.y) * 16.f;
-    r[2] = (v[2] - d1.x) * 16.f;
-    r[3] = (v[3] - d1.y) * 16.f;
-    const uint32_t p2 = __nv_cvt_float2_to_fp8x2(make_float2(r[0], r[1]), __NV_SATFINITE, __NV_E4M3);
-    const uint32_t p3 = __nv_cvt_float2_to_fp8x2(make_float2(r[2], r[3]), __NV_SATFINITE, __NV_E4M3);
-    a[i] = (p0 & 0xFFFFu) | (p1 << 16);
-    b[i] = (p2 & 0xFFFFu) | (p3 << 16);
-  }
-  w0 = make_uint4(a[0], a[1], a[2], a[3]);
-  w1 = make_uint4(b[0], b[1], b[2], b[3]);
-}
-
 }  // namespace
 
 struct TcArgs {
@@ -118,6 +89,7 @@ struct TcArgs {
   uint32_t idesc;
   int mp, np, tiles, kb, split, stages, ncols;
   int mtiles;  // token tiles of mp rows (EPI_STORE only when > 1: prefill projections)
+  int rank_shift;  // fp8: xshift holds one row of shifts per K-split rank (operand written per rank)
 };
 
 // ---- B operand: prologue + layout ------------------------------------------------
@@ -534,7 +506,8 @@ __global__ void __launch_bounds__(kTcThreads, 2) k_tc_gemm(const __grid_constant
       const int Mt = M - tok0 < a.mp ? M - tok0 : a.mp;  // tokens of this tile
       if (FMT == SB_FMT_FP8) {
         epi_sync();  // every warp is done with the previous tile's scales
-        for (int i = tid; i < Mt; i += kTcEpiWarps * 32) s_unscale[i] = ldexpf(1.f, -a.xshift[tok0 + i]);
+        const int32_t* xs = a.xshift + (a.rank_shift ? q * a.mp : 0);  // this rank's K range has its own scale
+        for (int i = tid; i < Mt; i += kTcEpiWarps * 32) s_unscale[i] = ldexpf(1.f, -xs[tok0 + i]);
         epi_sync();
       }
       const uint32_t taddr = tmem + buf * half_cols + (static_cast<uint32_t>(lq * 32) << 16);
@@ -621,6 +594,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) k_tc_gemm(const __grid_constant
 // ---- host side ------------------------------------------------------------------
 static const int kSMs = 148;
 static const size_t kTcSmem = 220 * 1024;
+static const int kTcShiftRanks = 8;  // the widest K split (clusters of 8)
 
 static int elem_bytes(int fmt) { return tc_bf16_operand(fmt) ? 2 : 1; }
 static int pad_rows(int fmt, int m) { return tc_bf16_operand(fmt) ? (m + 15) / 16 * 16 : (m + 7) / 8 * 8; }
@@ -628,11 +602,19 @@ static int pad_rows(int fmt, int m) { return tc_bf16_operand(fmt) ? (m + 15) / 1
 // token rows above 128 are processed in tiles of 128 (one launch)
 static int tile_rows(int fmt, int m) { return m > 128 ? 128 : pad_rows(fmt, m); }
 
+size_t tc_shift_offset(int fmt, int k, int m) {
+  const int mp = tile_rows(fmt, m), mtiles = (m + mp - 1) / mp;
+  const int np = fmt == SB_FMT_FP8 ? 2 * mp : mp;
+  return static_cast<size_t>(mtiles) * np * k * elem_bytes(fmt);
+}
+
 size_t tc_operand_bytes(int fmt, int k, int m) {
   if (!tc_format(fmt) || m < 1) return 0;
   const int mp = tile_rows(fmt, m), mtiles = (m + mp - 1) / mp;
   const int np = fmt == SB_FMT_FP8 ? 2 * mp : mp;
-  return static_cast<size_t>(mtiles) * np * k * elem_bytes(fmt) + static_cast<size_t>(mtiles) * mp * 4;
+  // shifts: one row per token tile, or one per K-split rank (operand written per rank)
+  const int srows = mtiles > kTcShiftRanks ? mtiles : kTcShiftRanks;
+  return static_cast<size_t>(mtiles) * np * k * elem_bytes(fmt) + static_cast<size_t>(srows) * mp * 4;
 }
 
 static int tc_ctas_per_sm_max() { return 2; }
@@ -723,7 +705,7 @@ static int gemm_launch(const cudaLaunchConfig_t& cfg, const GemvParams& p, const
 
 template <int FMT>
 static int tc_launch_t(const GemvParams& p0, const void* w_tc, void* operand, const TcPlan& pl, bool pdl,
-                       cudaStream_t stream) {
+                       cudaStream_t stream, bool operand_ready) {
   GemvParams p = p0;
   p.n_ctas = pl.n_ctas;
   uint8_t* xq = static_cast<uint8_t*>(operand);
@@ -741,10 +723,12 @@ static int tc_launch_t(const GemvParams& p0, const void* w_tc, void* operand, co
   cfg.stream = stream;
   cfg.attrs = at;
   cfg.numAttrs = pdl ? 1 : 0;
-  note_launch();
-  cudaError_t e = per_warp ? cudaLaunchKernelEx(&cfg, k_tc_prep_warp<FMT>, p, xq, xshift, pl.mp, pl.np, rows)
-                           : cudaLaunchKernelEx(&cfg, k_tc_prep_cta<FMT>, p, xq, xshift, pl.mp, pl.np);
-  if (e != cudaSuccess) return e;
+  if (!operand_ready) {  // else the preceding kernel wrote the operand (and, fp8, its per-rank shifts)
+    note_launch();
+    cudaError_t e = per_warp ? cudaLaunchKernelEx(&cfg, k_tc_prep_warp<FMT>, p, xq, xshift, pl.mp, pl.np, rows)
+                             : cudaLaunchKernelEx(&cfg, k_tc_prep_cta<FMT>, p, xq, xshift, pl.mp, pl.np);
+    if (e != cudaSuccess) return e;
+  }
 
   TcArgs a;
   a.wt = static_cast<const uint8_t*>(w_tc);
@@ -761,6 +745,7 @@ static int tc_launch_t(const GemvParams& p0, const void* w_tc, void* operand, co
   a.stages = pl.stages;
   a.ncols = pl.ncols;
   a.mtiles = pl.mtiles;
+  a.rank_shift = operand_ready && FMT == SB_FMT_FP8 ? 1 : 0;
   cfg.gridDim = dim3(pl.n_ctas);
   cfg.blockDim = dim3(kTcThreads);
   cfg.dynamicSmemBytes = pl.smem;
@@ -786,12 +771,12 @@ static int tc_launch_t(const GemvParams& p0, const void* w_tc, void* operand, co
 }
 
 int tc_launch(const GemvParams& p, const void* w_tc, void* operand, const TcPlan& pl, int fmt, bool pdl,
-              cudaStream_t stream) {
+              cudaStream_t stream, bool operand_ready) {
   switch (fmt) {
-    case SB_FMT_BF16: return tc_launch_t<SB_FMT_BF16>(p, w_tc, operand, pl, pdl, stream);
-    case SB_FMT_FP8: return tc_launch_t<SB_FMT_FP8>(p, w_tc, operand, pl, pdl, stream);
-    case SB_FMT_INT8: return tc_launch_t<SB_FMT_INT8>(p, w_tc, operand, pl, pdl, stream);
-    case SB_FMT_NVFP4: return tc_launch_t<SB_FMT_NVFP4>(p, w_tc, operand, pl, pdl, stream);
+    case SB_FMT_BF16: return tc_launch_t<SB_FMT_BF16>(p, w_tc, operand, pl, pdl, stream, operand_ready);
+    case SB_FMT_FP8: return tc_launch_t<SB_FMT_FP8>(p, w_tc, operand, pl, pdl, stream, operand_ready);
+    case SB_FMT_INT8: return tc_launch_t<SB_FMT_INT8>(p, w_tc, operand, pl, pdl, stream, operand_ready);
+    case SB_FMT_NVFP4: return tc_launch_t<SB_FMT_NVFP4>(p, w_tc, operand, pl, pdl, stream, operand_ready);
   }
   return SB_ERR_ARG;
 }

@@ -65,8 +65,13 @@ __host__ __device__ inline TcLayout tc_layout(int np, int stages, int m, int spl
 size_t tc_operand_bytes(int fmt, int k, int m);
 bool tc_plan(int fmt, int n, int k, int m, TcPlan& pl);
 // p: the GEMV parameters (prologue + epilogue); w_tc: tile copy of the weight;
-// operand: tc_operand_bytes() of scratch (device).
+// operand: tc_operand_bytes() of scratch (device).  operand_ready: the
+// preceding kernel has written the operand (one token tile) and, for fp8, one
+// row of shifts per K-split rank (rank r's K range scaled by 2^xshift[r][m]),
+// so no preparation kernel runs.
 int tc_launch(const GemvParams& p, const void* w_tc, void* operand, const TcPlan& pl, int fmt, bool pdl,
-              cudaStream_t stream);
+              cudaStream_t stream, bool operand_ready = false);
+// where the shifts start inside an operand of tc_operand_bytes(fmt, k, m)
+size_t tc_shift_offset(int fmt, int k, int m);
 
 }  // namespace sb
