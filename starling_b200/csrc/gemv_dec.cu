@@ -338,10 +338,13 @@ bool gemv_dec_plan(int fmt, int n_tiles, int k, int m, DecPlan& pl) {
   const int n_ctas = n_tiles < cap ? n_tiles : cap;
   const int per = (n_tiles + n_ctas - 1) / n_ctas;
   int slots = static_cast<int>((two ? 88 : 160) * 1024 / slot);
+  if (slots == 0 && !two && per == 1 && slot <= 200 * 1024) slots = 1;
   if (slots > 2 * per) slots = 2 * per;
   if (slots > 16) slots = 16;
-  if (slots < 2) return false;
-  int batch = slots / 2;
+  // a CTA that owns a single tile loads nothing after it: one slot serves
+  // (the [2048 x 8192] down projection in 1-byte formats: 131 KiB tiles)
+  if (slots < 2 && !(slots == 1 && per == 1)) return false;
+  int batch = slots >= 2 ? slots / 2 : 1;  // >= 1: the tile loop advances by batch
   // reduction buffers: batch * (W + 1) * 16 * m floats
   while (batch > 1 && static_cast<size_t>(batch) * (W + 1) * 16 * m * 4 > 48 * 1024) --batch;
   const size_t smem = dec_layout(wbytes + sbytes, slots, batch, W, m, ksw * 16).total;

@@ -213,6 +213,13 @@ def cmd_verify(a) -> None:
             eng.step_path = "auto"
             print(f"verify 8 tokens, cache 600, {d.layers} layers, NVFP4 {name}: forward {full:.1f} us "
                   f"(per launch: {', '.join(ops)}, lm_head {lm:.2f} us)")
+        lib.sb_set_nvfp4_path(_lib.SB_NVFP4_AUTO)
+        if eng.fused_step_ok(st):
+            eng.step_path = "fused"
+            st.set_slot(600, pad_len=600)
+            fused = _graph_time(lambda: eng.decode_step(st, 0))
+            eng.step_path = "auto"
+            print(f"verify 8 tokens, cache 600, {d.layers} layers, NVFP4 fused step: forward {fused:.1f} us")
     finally:
         lib.sb_set_nvfp4_path(prev)
 
