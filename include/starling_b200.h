@@ -175,10 +175,10 @@ int32_t sb_set_nvfp4_path(int32_t mode);
  * (src/starling/granite/multistep.py:157-188); with m > 1 it is the verify
  * forward SpeculativeDecoder._verify_step_fused (speculative.py:598-680) with
  * the acceptance compare of speculative.py:430-459 fused on device.
- * `step` indexes out_ids in DECODE mode.  One-token forwards (batch * m ==
- * 1, B = 1 decode) run as the one-launch fused step where it serves them
- * (see sb_decode_step_ex), every other forward as about 5 launches per
- * layer. */
+ * `step` indexes out_ids in DECODE mode.  Forwards of one stream (batch 1:
+ * B = 1 decode, verify of up to 8 tokens) run as the one-launch fused step
+ * where it serves them (see sb_decode_step_ex), every other forward as about
+ * 5 launches per layer. */
 int sb_decode_step(const SbModel* model, const SbState* state, int32_t step, sb_stream_t stream);
 
 /* sb_decode_step with the kernel path chosen by the caller:

@@ -526,10 +526,11 @@ int sb_decode_step_ex(const SbModel* md, const SbState* st, int32_t step, int32_
   if (!md->layers || md->n_layers < 1) return fail(SB_ERR_ARG, "no layers");
   if ((flags & SB_STEP_PER_OP) && (flags & SB_STEP_FUSED)) return fail(SB_ERR_ARG, "conflicting step flags");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  // flags 0: one-token forwards (B = 1 decode) as the fused step where it
-  // serves them (measured faster there: 1.46 vs 1.53 ms per 40-layer NVFP4
-  // step on B200), everything else on the per-op kernels
-  const bool fused_default = flags == 0 && st->batch * st->m == 1;
+  // flags 0: forwards of one stream (B = 1 decode, verify of <= 8 tokens) as
+  // the fused step where it serves them (measured faster there on B200, 40
+  // NVFP4 layers: 1.46 vs 1.49-1.53 ms per decode step, 4.04 vs 4.20 ms per
+  // 8-token verify), everything else on the per-op kernels
+  const bool fused_default = flags == 0 && st->batch == 1;
   if ((flags & SB_STEP_FUSED) || fused_default) {
     StepPlan pl;
     const char* why = "";

@@ -209,7 +209,7 @@ class GraniteEngine:
 
     # ---- native calls ----------------------------------------------------- #
     # decode-step kernel path: "auto" (the library's default: the fused step for
-    # one-token forwards where it serves them, else the per-op kernels),
+    # forwards of one stream where it serves them, else the per-op kernels),
     # "fused" (required), "prefer_fused" (fused wherever it serves the
     # forward) or "ops" (per-op kernels only)
     step_path = "auto"

@@ -464,3 +464,27 @@ def test_speculative_device_loop_matches_host_loop(golden, kind):
         (host.verify_forwards, host.accepted, host.decode_steps)
     if kind == "exact":
         assert host.accepted > 0
+
+
+@pytest.mark.parametrize("case", ["eos_in_draft", "max_new_5"])
+def test_speculative_device_loop_stops_like_host_loop(golden, case):
+    """Stopping rules on the device: an EOS among the accepted draft tokens
+    ends the loop right after it (speculative.py:433-439), and the token
+    budget ends it mid-draft; both exactly as the host loop."""
+    d, w, g = golden
+    emb = g["inputs_embeds"].cuda()
+    llm = LLMMega(weights=w, dims=d.__dict__, max_cache_len=96)
+    ref = MultiStepLLMMega(engine=llm.engine, steps_per_replay=4).generate(emb, max_new_tokens=40,
+                                                                           eos_token_id=-1).ids[0].tolist()
+    draft = ref[1:]
+    if case == "eos_in_draft":
+        eos, n_new = ref[7], 40  # a token the greedy run emits at step 7
+    else:
+        eos, n_new = -1, 5
+    host = SpeculativeDecoder(llm, device_loop=False).generate(emb, draft, max_new_tokens=n_new, eos_token_id=eos)
+    dev = SpeculativeDecoder(llm, device_loop=True).generate(emb, draft, max_new_tokens=n_new, eos_token_id=eos)
+    assert dev.ids[0].tolist() == host.ids[0].tolist()
+    assert (dev.verify_forwards, dev.accepted, dev.decode_steps) == \
+        (host.verify_forwards, host.accepted, host.decode_steps)
+    if case == "eos_in_draft":
+        assert host.ids[0].tolist()[-1] == eos and len(host.ids[0]) <= 9
