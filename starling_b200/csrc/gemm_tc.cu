@@ -353,6 +353,10 @@ __global__ void __launch_bounds__(kTcThreads, 2) k_tc_gemm(const __grid_constant
   int* s_shift = reinterpret_cast<int*>(smem + L.shift);
   float* wb_val = reinterpret_cast<float*>(smem + L.wbv);
   int* wb_idx = reinterpret_cast<int*>(smem + L.wbi);
+  // QKV, one token tile: RoPE position per token + the cache slot of token 0
+  // (the argmax scratch is unused by this epilogue)
+  int* s_tokpos = reinterpret_cast<int*>(wb_val);
+  const int* tokpos = EPI == EPI_QKV && a.mtiles == 1 ? s_tokpos : nullptr;
   int32_t* err = p.ctrl ? p.ctrl + SB_CTRL_ERR : nullptr;
 
   const int S = a.split;
@@ -474,8 +478,12 @@ __global__ void __launch_bounds__(kTcThreads, 2) k_tc_gemm(const __grid_constant
     pdl_wait();
     pdl_launch();
     // bring the epilogue's global inputs into L1 while the main loop runs: the
-    // residual rows this CTA updates (first tile, or its rank's rows of the
-    // shared tile), and the RoPE rows at each token's position
+    // weight row scales and residual rows of the CTA's first tile (or its
+    // rank's rows of the shared tile), and the RoPE rows at each token's position
+    if ((FMT == SB_FMT_FP8 || FMT == SB_FMT_INT8) && my_tiles > 0 && tid < 4) {
+      const int r = (cid / nlive) * 128 + tid * 32;  // 32 fp32 scales = one 128-byte line
+      if (r < p.n) asm volatile("prefetch.global.L1 [%0];" ::"l"(reinterpret_cast<const float*>(p.scale) + r));
+    }
     if (a.mtiles > 1) {
       // prefill token tiles: no prefetch
     } else if constexpr (EPI == EPI_RESID) {
@@ -487,14 +495,20 @@ __global__ void __launch_bounds__(kTcThreads, 2) k_tc_gemm(const __grid_constant
         if (ra < rb)
           asm volatile("prefetch.global.L1 [%0];" ::"l"(p.y + static_cast<size_t>(i / nseg) * p.n + ra + (i % nseg) * 64));
     } else if constexpr (EPI == EPI_QKV) {
+      // each token's RoPE position and the cache slot, once, into shared
+      // memory (the epilogue would otherwise chain three dependent global
+      // loads per call: control block, rope_off, tables)
       const int slot_base = p.ctrl[SB_CTRL_SLOT];
       for (int i = tid; i < M; i += kTcEpiWarps * 32) {
         const int b = i / p.m_per;
         int pos = slot_base + i % p.m_per - (p.rope_off ? p.rope_off[b] : 0);
         pos = pos < 0 ? 0 : (pos >= p.rope_max ? p.rope_max - 1 : pos);
+        s_tokpos[i] = pos;
         asm volatile("prefetch.global.L1 [%0];" ::"l"(p.cos_tab + static_cast<size_t>(pos) * 64));
         asm volatile("prefetch.global.L1 [%0];" ::"l"(p.sin_tab + static_cast<size_t>(pos) * 64));
       }
+      if (tid == 0) s_tokpos[128] = slot_base;
+      epi_sync();
     }
     float* s_unscale = reinterpret_cast<float*>(s_shift);  // 2^-shift per token of the tile: exact
     const int lq = warp & 3, h = warp >> 2;
@@ -530,7 +544,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) k_tc_gemm(const __grid_constant
         }
         if (S == 1) {
           const int row = t * 128 + lrow;
-          tc_epi<FMT, 8, EPI>(p, row, row < p.n, v, m0, Mt, wb_val, wb_idx, warp, tok0);
+          tc_epi<FMT, 8, EPI>(p, row, row < p.n, v, m0, Mt, wb_val, wb_idx, warp, tok0, tokpos);
         } else {
           // push this K partial to the rank that finishes the row (16-byte DSMEM stores)
           float* dst = cg::this_cluster().map_shared_rank(part, lrow / rp) + (q * rp + lrow % rp) * ms + m0;
@@ -564,7 +578,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) k_tc_gemm(const __grid_constant
           v[3] += x4.w;
         }
       const int row = cid * 128 + r0 + lr;
-      tc_epi<FMT, 4, EPI>(p, row, ok && row < p.n, v, m0, M, wb_val, wb_idx, warp, 0);
+      tc_epi<FMT, 4, EPI>(p, row, ok && row < p.n, v, m0, M, wb_val, wb_idx, warp, 0, tokpos);
     }
   }
   if constexpr (EPI == EPI_ARGMAX) {  // combine the warps' running bests (order-independent total order)

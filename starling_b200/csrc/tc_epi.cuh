@@ -19,9 +19,13 @@ namespace sb {
 // Must be called by full warps with warp-uniform m0.  ARGMAX keeps a running
 // best per (warp, token) in wb_val/wb_idx[warp * 128 + m].
 // EPI: the epilogue (EPI_*), fixed at compile time.
+// QKV: tokpos (shared memory, one token tile) holds each token's RoPE
+// position and, at [128], the cache slot of token 0; nullptr: read them from
+// the control block and rope_off here.
 template <int FMT, int CNT, int EPI>
 __device__ __forceinline__ void tc_epi(const GemvParams& p, int row, bool row_ok, float* v, int m0, int M,
-                                       float* wb_val, int* wb_idx, int warp, int tok0) {
+                                       float* wb_val, int* wb_idx, int warp, int tok0,
+                                       const int* tokpos = nullptr) {
   const int lane = threadIdx.x & 31;
   float rs = 1.f;
   if (row_ok) {
@@ -60,7 +64,7 @@ __device__ __forceinline__ void tc_epi(const GemvParams& p, int row, bool row_ok
     // q/k: RoPE with each product rounded to bf16 (llm_mega.py:539-543); k/v to
     // cache slot ctrl[SLOT] + token (StaticLayer.update, cache_utils.py:308-335)
     const int qk_rows = (p.n_q + p.n_kv) * 128;
-    const int slot_base = p.ctrl[SB_CTRL_SLOT];
+    const int slot_base = tokpos ? tokpos[128] : p.ctrl[SB_CTRL_SLOT];
     const int head = row >> 7, within = row & 127;
     const bool odd = within & 1;
     const int j = within >> 1;
@@ -72,8 +76,13 @@ __device__ __forceinline__ void tc_epi(const GemvParams& p, int row, bool row_ok
       sn[i] = 0.f;
       if (is_qk && row_ok && m0 + i < M) {
         const int m = tok0 + m0 + i, b = m / p.m_per, mi = m % p.m_per;
-        int pos = slot_base + mi - (p.rope_off ? p.rope_off[b] : 0);
-        pos = pos < 0 ? 0 : (pos >= p.rope_max ? p.rope_max - 1 : pos);
+        int pos;
+        if (tokpos) {
+          pos = tokpos[m];
+        } else {
+          pos = slot_base + mi - (p.rope_off ? p.rope_off[b] : 0);
+          pos = pos < 0 ? 0 : (pos >= p.rope_max ? p.rope_max - 1 : pos);
+        }
         cs[i] = u16_to_f(p.cos_tab[pos * 64 + j]);
         sn[i] = u16_to_f(p.sin_tab[pos * 64 + j]);
       }
