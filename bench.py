@@ -221,7 +221,7 @@ def decode_timing(eng, B, emb, prompt_lengths, T, K, W, kr, world, dev, local_ra
 # algorithmic bytes of the captured case: the bench scales the traffic to its
 # own launch by the ratio of algorithmic bytes (same kernel, same tiling).
 PROFILED_TRAFFIC = {
-    ("b48", "attention"): (80.179456e6 + 2.41664e6, 61.5e6, "profiles/attention_b48_decode.md"),
+    ("b48", "attention"): (66.056448e6 + 0.626432e6, 61.5e6, "profiles/attention_b48_decode.md"),
     ("b48", "gate_up"): (33.9008e6, 33.62e6, "profiles/tcgen05_gemm_gate_up_fp8_b48.md"),
     ("b1", "gate_up"): (18.93376e6, 18.87e6, "profiles/gemv_gate_up_nvfp4_b1.md"),
     # 4 layers + lm_head: 4 x 34.21 MB + 115.61 MB of NVFP4 weights + K/V rows
