@@ -44,6 +44,7 @@
 // in rank order (deterministic) and runs the epilogue on 128/split rows.
 // Every wait is bounded (2 s of %globaltimer); on expiry the kernel records
 // SB_CTRL_ERR = 2 and carries on with invalid results instead of hanging.
+#include <atomic>
 #include <cooperative_groups.h>
 
 #include "gemm_tc.cuh"
@@ -333,12 +334,16 @@ __global__ void __launch_bounds__(kPrepCtaThreads) k_tc_prep_cta(const __grid_co
 }
 
 // ---- the GEMM ----------------------------------------------------------------------
-template <int FMT, int EPI>
-__global__ void __launch_bounds__(kTcThreads, 2) k_tc_gemm(const __grid_constant__ GemvParams p, const __grid_constant__ TcArgs a) {
+// NEPI epilogue warps: 8 with two CTAs per SM, 16 with one
+template <int FMT, int EPI, int NEPI>
+__global__ void __launch_bounds__((NEPI + 2) * 32, NEPI == kTcEpiWarps ? 2 : 1)
+    k_tc_gemm(const __grid_constant__ GemvParams p, const __grid_constant__ TcArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int nepi = NEPI;
+  auto epi_bar = [&]() { asm volatile("bar.sync 1, %0;" ::"n"(NEPI * 32) : "memory"); };
   const int M = p.m;
-  const TcLayout L = tc_layout(a.np, a.stages, M, a.split);
+  const TcLayout L = tc_layout(a.np, a.stages, M, a.split, NEPI);
   uint8_t* ring = smem;
   float* part = reinterpret_cast<float*>(smem + L.part);  // split: inbox [src rank][row][ms]
   const int ms = tc_inbox_stride(M);
@@ -392,7 +397,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) k_tc_gemm(const __grid_constant
   const int rot = cid % nk;
   const uint32_t half_cols = static_cast<uint32_t>(a.ncols) / 2;  // accumulator buffer stride
 
-  constexpr int kProd = kTcEpiWarps, kMma = kTcEpiWarps + 1;  // warp roles
+  constexpr int kProd = nepi, kMma = nepi + 1;  // warp roles
   if (warp == kProd && lane == 0) {
     for (int s = 0; s < a.stages; ++s) {
       mbar_init(full + s, 1);
@@ -400,13 +405,13 @@ __global__ void __launch_bounds__(kTcThreads, 2) k_tc_gemm(const __grid_constant
     }
     for (int b2 = 0; b2 < 2; ++b2) {
       mbar_init(acc_full + b2, 1);
-      mbar_init(acc_empty + b2, kTcEpiWarps * 32);
+      mbar_init(acc_empty + b2, nepi * 32);
     }
     mbar_fence_init();
   }
   if (warp == kMma) tmem_alloc(s_tmem, static_cast<uint32_t>(a.ncols));
   if constexpr (EPI == EPI_ARGMAX)
-    for (int i = tid; i < (kTcEpiWarps + 2) * 128; i += blockDim.x) {
+    for (int i = tid; i < (nepi + 2) * 128; i += blockDim.x) {
       wb_val[i] = -INFINITY;
       wb_idx[i] = 0x7fffffff;
     }
@@ -491,7 +496,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) k_tc_gemm(const __grid_constant
       const int ra = cid * 128 + (S > 1 ? q * rp0 : 0), nr = S > 1 ? rp0 : 128;
       const int rb = min(ra + nr, p.n);
       const int nseg = (rb - ra + 63) / 64;  // 128-byte lines of bf16 rows
-      for (int i = tid; i < M * nseg; i += kTcEpiWarps * 32)
+      for (int i = tid; i < M * nseg; i += nepi * 32)
         if (ra < rb)
           asm volatile("prefetch.global.L1 [%0];" ::"l"(p.y + static_cast<size_t>(i / nseg) * p.n + ra + (i % nseg) * 64));
     } else if constexpr (EPI == EPI_QKV) {
@@ -499,7 +504,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) k_tc_gemm(const __grid_constant
       // memory (the epilogue would otherwise chain three dependent global
       // loads per call: control block, rope_off, tables)
       const int slot_base = p.ctrl[SB_CTRL_SLOT];
-      for (int i = tid; i < M; i += kTcEpiWarps * 32) {
+      for (int i = tid; i < M; i += nepi * 32) {
         const int b = i / p.m_per;
         int pos = slot_base + i % p.m_per - (p.rope_off ? p.rope_off[b] : 0);
         pos = pos < 0 ? 0 : (pos >= p.rope_max ? p.rope_max - 1 : pos);
@@ -508,10 +513,11 @@ __global__ void __launch_bounds__(kTcThreads, 2) k_tc_gemm(const __grid_constant
         asm volatile("prefetch.global.L1 [%0];" ::"l"(p.sin_tab + static_cast<size_t>(pos) * 64));
       }
       if (tid == 0) s_tokpos[128] = slot_base;
-      epi_sync();
+      epi_bar();
     }
     float* s_unscale = reinterpret_cast<float*>(s_shift);  // 2^-shift per token of the tile: exact
-    const int lq = warp & 3, h = warp >> 2;
+    constexpr int nh = nepi >> 2;
+    const int lq = warp & 3, h = warp >> 2;  // lane quarter; token chunk offset (stride nh)
     const int lrow = lq * 32 + lane;
     const int rp = tc_rows_per_rank(S);
     for (int tc = 0; tc < my_tiles; ++tc) {
@@ -519,15 +525,15 @@ __global__ void __launch_bounds__(kTcThreads, 2) k_tc_gemm(const __grid_constant
       const int t = item / nlive, tok0 = s_live[1 + item % nlive] * a.mp;
       const int Mt = M - tok0 < a.mp ? M - tok0 : a.mp;  // tokens of this tile
       if (FMT == SB_FMT_FP8) {
-        epi_sync();  // every warp is done with the previous tile's scales
+        epi_bar();  // every warp is done with the previous tile's scales
         const int32_t* xs = a.xshift + (a.rank_shift ? q * a.mp : 0);  // this rank's K range has its own scale
-        for (int i = tid; i < Mt; i += kTcEpiWarps * 32) s_unscale[i] = ldexpf(1.f, -xs[tok0 + i]);
-        epi_sync();
+        for (int i = tid; i < Mt; i += nepi * 32) s_unscale[i] = ldexpf(1.f, -xs[tok0 + i]);
+        epi_bar();
       }
       const uint32_t taddr = tmem + buf * half_cols + (static_cast<uint32_t>(lq * 32) << 16);
       wait_bounded(acc_full + buf, static_cast<uint32_t>((tc / 2) & 1), err);
       tc_fence_after();
-      for (int m0 = h * 8; m0 < Mt; m0 += 16) {
+      for (int m0 = h * 8; m0 < Mt; m0 += 8 * nh) {
         // 8 tokens of this lane's row: D0 (and D1 for the fp8 split) columns
         uint32_t d0[8], d1[8];
         tmem_ld8(taddr + m0, d0);
@@ -586,7 +592,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) k_tc_gemm(const __grid_constant
     for (int m = tid; m < M; m += blockDim.x) {
       float bv = -INFINITY;
       int bi = 0x7fffffff;
-      for (int w = 0; w < kTcEpiWarps + 2; ++w)
+      for (int w = 0; w < nepi + 2; ++w)
         if (am_better(wb_val[w * 128 + m], wb_idx[w * 128 + m], bv, bi)) {
           bv = wb_val[w * 128 + m];
           bi = wb_idx[w * 128 + m];
@@ -674,17 +680,18 @@ static bool tc_plan_for(int fmt, int n, int k, int m, int per_sm, TcPlan& pl) {
   }
   pl.ncols = 32;
   while (pl.ncols < 2 * pl.np) pl.ncols *= 2;  // two accumulator buffers
+  pl.epi_warps = per_sm > 1 ? kTcEpiWarps : kTcMaxEpiWarps;  // (the layout below depends on it)
   if (per_sm > 1 && pl.ncols > 256) return false;
   const size_t budget = per_sm > 1 ? kTcSmemTwo : kTcSmem;
   pl.stages = 0;
   const int ml = m < pl.mp ? m : pl.mp;  // token rows of one tile
   for (int st = 8; st >= 2; --st)
-    if (tc_layout(pl.np, st, ml, pl.split).total <= budget) {
+    if (tc_layout(pl.np, st, ml, pl.split, pl.epi_warps).total <= budget) {
       pl.stages = st;
       break;
     }
   if (!pl.stages) return false;
-  pl.smem = tc_layout(pl.np, pl.stages, ml, pl.split).total;
+  pl.smem = tc_layout(pl.np, pl.stages, ml, pl.split, pl.epi_warps).total;
   return true;
 }
 
@@ -696,25 +703,24 @@ bool tc_plan(int fmt, int n, int k, int m, TcPlan& pl) {
   return tc_plan_for(fmt, n, k, m, 1, pl);
 }
 
-template <int FMT, int EPI>
-static int gemm_configure() {
+template <int FMT, int EPI, int NEPI>
+static int gemm_launch_n(const cudaLaunchConfig_t& cfg, const GemvParams& p, const TcArgs& a) {
   int dev = 0;
   cudaGetDevice(&dev);
-  static unsigned configured = 0;
-  if (!(configured & (1u << dev))) {
-    cudaError_t e = cudaFuncSetAttribute(k_tc_gemm<FMT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  static std::atomic<unsigned> configured{0};  // one bit per device
+  if (!(configured.load(std::memory_order_relaxed) & (1u << dev))) {
+    cudaError_t e = cudaFuncSetAttribute(k_tc_gemm<FMT, EPI, NEPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(kTcSmem));
     if (e != cudaSuccess) return e;
-    configured |= 1u << dev;
+    configured.fetch_or(1u << dev, std::memory_order_relaxed);
   }
-  return 0;
+  return cudaLaunchKernelEx(&cfg, k_tc_gemm<FMT, EPI, NEPI>, p, a);
 }
 
 template <int FMT, int EPI>
-static int gemm_launch(const cudaLaunchConfig_t& cfg, const GemvParams& p, const TcArgs& a) {
-  const int rc = gemm_configure<FMT, EPI>();
-  if (rc) return rc;
-  return cudaLaunchKernelEx(&cfg, k_tc_gemm<FMT, EPI>, p, a);
+static int gemm_launch(int epi_warps, const cudaLaunchConfig_t& cfg, const GemvParams& p, const TcArgs& a) {
+  return epi_warps == kTcEpiWarps ? gemm_launch_n<FMT, EPI, kTcEpiWarps>(cfg, p, a)
+                                  : gemm_launch_n<FMT, EPI, kTcMaxEpiWarps>(cfg, p, a);
 }
 
 template <int FMT>
@@ -761,7 +767,7 @@ static int tc_launch_t(const GemvParams& p0, const void* w_tc, void* operand, co
   a.mtiles = pl.mtiles;
   a.rank_shift = operand_ready && FMT == SB_FMT_FP8 ? 1 : 0;
   cfg.gridDim = dim3(pl.n_ctas);
-  cfg.blockDim = dim3(kTcThreads);
+  cfg.blockDim = dim3((pl.epi_warps + 2) * 32);
   cfg.dynamicSmemBytes = pl.smem;
   int na = 0;
   if (pdl) at[na++] = at[0];
@@ -775,11 +781,11 @@ static int tc_launch_t(const GemvParams& p0, const void* w_tc, void* operand, co
   cfg.numAttrs = na;
   note_launch();
   switch (p.epi) {
-    case EPI_STORE: return gemm_launch<FMT, EPI_STORE>(cfg, p, a);
-    case EPI_QKV: return gemm_launch<FMT, EPI_QKV>(cfg, p, a);
-    case EPI_RESID: return gemm_launch<FMT, EPI_RESID>(cfg, p, a);
-    case EPI_SWIGLU: return gemm_launch<FMT, EPI_SWIGLU>(cfg, p, a);
-    case EPI_ARGMAX: return gemm_launch<FMT, EPI_ARGMAX>(cfg, p, a);
+    case EPI_STORE: return gemm_launch<FMT, EPI_STORE>(pl.epi_warps, cfg, p, a);
+    case EPI_QKV: return gemm_launch<FMT, EPI_QKV>(pl.epi_warps, cfg, p, a);
+    case EPI_RESID: return gemm_launch<FMT, EPI_RESID>(pl.epi_warps, cfg, p, a);
+    case EPI_SWIGLU: return gemm_launch<FMT, EPI_SWIGLU>(pl.epi_warps, cfg, p, a);
+    case EPI_ARGMAX: return gemm_launch<FMT, EPI_ARGMAX>(pl.epi_warps, cfg, p, a);
   }
   return SB_ERR_ARG;
 }

@@ -22,6 +22,7 @@ struct TcPlan {
   int split;   // CTAs per cluster splitting K (1 = persistent over tiles)
   int stages;  // ring depth
   int ncols;   // TMEM columns allocated
+  int epi_warps;  // epilogue warps (the block has epi_warps + 2)
   int n_ctas;
   size_t smem;
 };
@@ -36,10 +37,14 @@ __host__ __device__ inline int tc_rows_per_rank(int split) {
 }
 // floats per inbox row: whole 8-token chunks (16-byte aligned stores) + 4 (bank spread)
 __host__ __device__ inline int tc_inbox_stride(int m) { return (m + 7) / 8 * 8 + 4; }
-// warps of the GEMM block: 8 epilogue warps (two per TMEM lane quarter), producer, MMA
+// warps of a tcgen05 GEMM block: epilogue warps (a multiple of 4: each TMEM
+// lane quarter is read by epilogue_warps / 4 warps), producer, MMA.  The
+// block-scaled GEMM (gemm_bs.cu) runs 8; this GEMM 16 with one CTA per SM and
+// 8 with two (its register budget is the same for both).
 constexpr int kTcEpiWarps = 8;
 constexpr int kTcThreads = (kTcEpiWarps + 2) * 32;
-__host__ __device__ inline TcLayout tc_layout(int np, int stages, int m, int split) {
+constexpr int kTcMaxEpiWarps = 16;
+__host__ __device__ inline TcLayout tc_layout(int np, int stages, int m, int split, int epi_warps) {
   auto up = [](size_t x, size_t a) { return (x + a - 1) & ~(a - 1); };
   TcLayout L;
   L.stage_bytes = 16384 + static_cast<size_t>(np) * 128;
@@ -55,8 +60,8 @@ __host__ __device__ inline TcLayout tc_layout(int np, int stages, int m, int spl
   L.bval = L.best + 128 * 4;
   L.shift = L.bval + 128 * 4;
   L.wbv = L.shift + 128 * 4;                    // [warps][128] running argmax value
-  L.wbi = L.wbv + (kTcEpiWarps + 2) * 128 * 4;  // [warps][128] running argmax index
-  L.live = L.wbi + (kTcEpiWarps + 2) * 128 * 4;  // [1 + 64] token tiles holding a real row (prefill)
+  L.wbi = L.wbv + static_cast<size_t>(epi_warps + 2) * 128 * 4;   // [warps][128] running argmax index
+  L.live = L.wbi + static_cast<size_t>(epi_warps + 2) * 128 * 4;  // [1 + 64] token tiles holding a real row (prefill)
   L.total = L.live + 65 * 4;
   return L;
 }
