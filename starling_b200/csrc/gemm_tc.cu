@@ -358,10 +358,11 @@ __global__ void __launch_bounds__((NEPI + 2) * 32, NEPI == kTcEpiWarps ? 2 : 1)
   int* s_shift = reinterpret_cast<int*>(smem + L.shift);
   float* wb_val = reinterpret_cast<float*>(smem + L.wbv);
   int* wb_idx = reinterpret_cast<int*>(smem + L.wbi);
-  // QKV, one token tile: RoPE position per token + the cache slot of token 0
-  // (the argmax scratch is unused by this epilogue)
+  // QKV: per token of the current token tile its RoPE position, stream and
+  // position in the stream, plus the cache slot of position 0 (tc_epi's
+  // tokpos layout; the argmax scratch is unused by this epilogue)
   int* s_tokpos = reinterpret_cast<int*>(wb_val);
-  const int* tokpos = EPI == EPI_QKV && a.mtiles == 1 ? s_tokpos : nullptr;
+  const int* tokpos = EPI == EPI_QKV ? s_tokpos : nullptr;
   int32_t* err = p.ctrl ? p.ctrl + SB_CTRL_ERR : nullptr;
 
   const int S = a.split;
@@ -499,21 +500,6 @@ __global__ void __launch_bounds__((NEPI + 2) * 32, NEPI == kTcEpiWarps ? 2 : 1)
       for (int i = tid; i < M * nseg; i += nepi * 32)
         if (ra < rb)
           asm volatile("prefetch.global.L1 [%0];" ::"l"(p.y + static_cast<size_t>(i / nseg) * p.n + ra + (i % nseg) * 64));
-    } else if constexpr (EPI == EPI_QKV) {
-      // each token's RoPE position and the cache slot, once, into shared
-      // memory (the epilogue would otherwise chain three dependent global
-      // loads per call: control block, rope_off, tables)
-      const int slot_base = p.ctrl[SB_CTRL_SLOT];
-      for (int i = tid; i < M; i += nepi * 32) {
-        const int b = i / p.m_per;
-        int pos = slot_base + i % p.m_per - (p.rope_off ? p.rope_off[b] : 0);
-        pos = pos < 0 ? 0 : (pos >= p.rope_max ? p.rope_max - 1 : pos);
-        s_tokpos[i] = pos;
-        asm volatile("prefetch.global.L1 [%0];" ::"l"(p.cos_tab + static_cast<size_t>(pos) * 64));
-        asm volatile("prefetch.global.L1 [%0];" ::"l"(p.sin_tab + static_cast<size_t>(pos) * 64));
-      }
-      if (tid == 0) s_tokpos[128] = slot_base;
-      epi_bar();
     }
     float* s_unscale = reinterpret_cast<float*>(s_shift);  // 2^-shift per token of the tile: exact
     constexpr int nh = nepi >> 2;
@@ -524,10 +510,28 @@ __global__ void __launch_bounds__((NEPI + 2) * 32, NEPI == kTcEpiWarps ? 2 : 1)
       const int item = cid + tc * ncl, buf = tc & 1;
       const int t = item / nlive, tok0 = s_live[1 + item % nlive] * a.mp;
       const int Mt = M - tok0 < a.mp ? M - tok0 : a.mp;  // tokens of this tile
-      if (FMT == SB_FMT_FP8) {
-        epi_bar();  // every warp is done with the previous tile's scales
-        const int32_t* xs = a.xshift + (a.rank_shift ? q * a.mp : 0);  // this rank's K range has its own scale
-        for (int i = tid; i < Mt; i += nepi * 32) s_unscale[i] = ldexpf(1.f, -xs[tok0 + i]);
+      if (FMT == SB_FMT_FP8 || EPI == EPI_QKV) {
+        epi_bar();  // every warp is done with the previous tile's scales / token table
+        if (FMT == SB_FMT_FP8) {
+          const int32_t* xs = a.xshift + (a.rank_shift ? q * a.mp : 0);  // this rank's K range has its own scale
+          for (int i = tid; i < Mt; i += nepi * 32) s_unscale[i] = ldexpf(1.f, -xs[tok0 + i]);
+        }
+        if constexpr (EPI == EPI_QKV) {
+          // the tile's tokens, once (the epilogue would otherwise chain three
+          // dependent global loads per call: control block, rope_off, tables)
+          const int slot_base = p.ctrl[SB_CTRL_SLOT];
+          for (int i = tid; i < Mt; i += nepi * 32) {
+            const int m = tok0 + i, b = m / p.m_per, mi = m % p.m_per;
+            int pos = slot_base + mi - (p.rope_off ? p.rope_off[b] : 0);
+            pos = pos < 0 ? 0 : (pos >= p.rope_max ? p.rope_max - 1 : pos);
+            s_tokpos[i] = pos;
+            s_tokpos[129 + i] = b;
+            s_tokpos[257 + i] = mi;
+            asm volatile("prefetch.global.L1 [%0];" ::"l"(p.cos_tab + static_cast<size_t>(pos) * 64));
+            asm volatile("prefetch.global.L1 [%0];" ::"l"(p.sin_tab + static_cast<size_t>(pos) * 64));
+          }
+          if (tid == 0) s_tokpos[128] = slot_base;
+        }
         epi_bar();
       }
       const uint32_t taddr = tmem + buf * half_cols + (static_cast<uint32_t>(lq * 32) << 16);

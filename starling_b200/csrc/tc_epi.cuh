@@ -19,9 +19,10 @@ namespace sb {
 // Must be called by full warps with warp-uniform m0.  ARGMAX keeps a running
 // best per (warp, token) in wb_val/wb_idx[warp * 128 + m].
 // EPI: the epilogue (EPI_*), fixed at compile time.
-// QKV: tokpos (shared memory, one token tile) holds each token's RoPE
-// position and, at [128], the cache slot of token 0; nullptr: read them from
-// the control block and rope_off here.
+// QKV: tokpos (shared memory) describes token m0 + i of the call (the token
+// tile starting at tok0): [m0 + i] its RoPE position, [129 + m0 + i] its
+// stream, [257 + m0 + i] its position in the stream, [128] the cache slot of
+// position 0; nullptr: compute them from the control block and rope_off here.
 template <int FMT, int CNT, int EPI>
 __device__ __forceinline__ void tc_epi(const GemvParams& p, int row, bool row_ok, float* v, int m0, int M,
                                        float* wb_val, int* wb_idx, int warp, int tok0,
@@ -75,11 +76,11 @@ __device__ __forceinline__ void tc_epi(const GemvParams& p, int row, bool row_ok
       cs[i] = 0.f;
       sn[i] = 0.f;
       if (is_qk && row_ok && m0 + i < M) {
-        const int m = tok0 + m0 + i, b = m / p.m_per, mi = m % p.m_per;
         int pos;
         if (tokpos) {
-          pos = tokpos[m];
+          pos = tokpos[m0 + i];
         } else {
+          const int m = tok0 + m0 + i, b = m / p.m_per, mi = m % p.m_per;
           pos = slot_base + mi - (p.rope_off ? p.rope_off[b] : 0);
           pos = pos < 0 ? 0 : (pos >= p.rope_max ? p.rope_max - 1 : pos);
         }
@@ -92,7 +93,7 @@ __device__ __forceinline__ void tc_epi(const GemvParams& p, int row, bool row_ok
       const float other = __shfl_xor_sync(0xffffffffu, v[i], 1);
       if (!row_ok || m0 + i >= M) continue;
       const int m = tok0 + m0 + i;
-      const int b = m / p.m_per, mi = m % p.m_per;
+      const int b = tokpos ? tokpos[129 + m0 + i] : m / p.m_per, mi = tokpos ? tokpos[257 + m0 + i] : m % p.m_per;
       const int slot = slot_base + mi;
       const bool slot_ok = slot >= 0 && slot < p.max_len;
       if (is_qk) {
