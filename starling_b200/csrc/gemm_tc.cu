@@ -209,6 +209,145 @@ __global__ void __launch_bounds__(kPrepThreads) k_tc_prep_warp(const __grid_cons
   }
 }
 
+// Many rows, K a multiple of 2048 up to 16384 (prefill): each row is held in
+// registers, one warp per 2048-element section (lane l: 16-element chunks
+// l, l + 32, l + 64, l + 96 of the section, all loaded before any is used),
+// S = K / 2048 warps per row and 8 / S rows per CTA.  Every input element is
+// read once; the RMSNorm sum of squares and the fp8 maximum are warp shuffles,
+// combined over a row's S warps through shared memory in section order.
+constexpr int kRowsChunks = 4;  // 16-element chunks per lane: 2048 elements per warp
+template <int FMT>
+__global__ void __launch_bounds__(256) k_tc_prep_rows(const __grid_constant__ GemvParams p, uint8_t* xq,
+                                                      int32_t* xshift, int mp, int np, int rows, int S) {
+  __shared__ float s_part[2][8];  // per warp: sum of squares, maximum
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int rl = warp / S, sec = warp % S;
+  const int m = blockIdx.x * (8 / S) + rl;  // token (padded to whole token tiles)
+  const int K = p.k;
+  const size_t kb_bytes = static_cast<size_t>(np) * 128;
+  constexpr int CPE = tc_bf16_operand(FMT) ? 2 : 1;  // 16-byte output chunks per 16 elements and term
+  const bool live = m < rows;
+  uint8_t* xt = xq + static_cast<size_t>(live ? m / mp : 0) * (K * (tc_bf16_operand(FMT) ? 2 : 1) / 128) * kb_bytes;
+  const int ml = m % mp;
+  auto off = [&](int n, int c) -> size_t {
+    return static_cast<size_t>(c >> 3) * kb_bytes + static_cast<size_t>(n >> 3) * 1024 + (c & 7) * 128 + (n & 7) * 16;
+  };
+  auto chunk = [&](int j) { return sec * 32 * kRowsChunks + lane + 32 * j; };  // 16-element chunk index
+  pdl_wait();
+  pdl_launch();
+  const bool pad_row = live && m < p.m && p.row_len && (m % p.row_T) >= p.row_len[p.row_b0 + m / p.row_T];
+  const bool zero = live && (m >= p.m || pad_row);  // past the tokens, or a prompt's padding
+  const bool work = live && !zero;
+  const bool embed = p.pro == PRO_EMBED;
+  uint4 raw[kRowsChunks][2];
+  if (work) {
+    const uint16_t* src;
+    if (embed) {
+      int64_t id = p.ids[m];
+      id = id < 0 ? 0 : (id >= p.embed_rows ? p.embed_rows - 1 : id);  // never read outside the table
+      src = p.embed + static_cast<size_t>(id) * K;
+    } else {
+      src = p.x + static_cast<size_t>(m) * K;
+    }
+#pragma unroll
+    for (int j = 0; j < kRowsChunks; ++j) {
+      raw[j][0] = *reinterpret_cast<const uint4*>(src + chunk(j) * 16);
+      raw[j][1] = *reinterpret_cast<const uint4*>(src + chunk(j) * 16 + 8);
+    }
+  }
+  // the 16 input values of chunk j (embedding rows: embed_tokens(ids) * 12, llm_mega.py:514)
+  auto in16 = [&](int j, float* f) {
+    unpack8(raw[j][0], f);
+    unpack8(raw[j][1], f + 8);
+    if (embed)
+#pragma unroll
+      for (int e = 0; e < 16; ++e) f[e] = bf(f[e] * p.emb_mult);
+  };
+  // a row's total of per-warp values over its S sections (section order)
+  auto row_total = [&](float v, int slot, bool is_max) {
+    if (S == 1) return v;
+    if (lane == 0) s_part[slot][warp] = v;
+    __syncthreads();
+    float t = 0.f;  // maxima are of magnitudes
+    for (int q = 0; q < S; ++q) t = is_max ? fmaxf(t, s_part[slot][rl * S + q]) : t + s_part[slot][rl * S + q];
+    return t;
+  };
+  float rstd = 0.f;
+  if (p.pro != PRO_NONE) {  // RMSNorm statistics (modeling_granite.py:192-197)
+    float ss = 0.f;
+    if (work)
+#pragma unroll
+      for (int j = 0; j < kRowsChunks; ++j) {
+        float f[16];
+        in16(j, f);
+        if (embed && p.hidden_out) {  // the residual stream of layer 0
+          uint4* ho = reinterpret_cast<uint4*>(p.hidden_out + static_cast<size_t>(m) * K + chunk(j) * 16);
+          ho[0] = pack8(f);
+          ho[1] = pack8(f + 8);
+        }
+#pragma unroll
+        for (int e = 0; e < 16; ++e) ss += f[e] * f[e];
+      }
+    ss = row_total(warp_sum(ss), 0, false);
+    rstd = 1.f / sqrtf(ss / static_cast<float>(K) + p.eps);
+  }
+  // prologue output of chunk j: weight * bf16(x * rstd), or the input
+  auto values16 = [&](int j, float* f) {
+    in16(j, f);
+    if (p.pro != PRO_NONE) {
+      float wn[16];
+      unpack8(__ldg(reinterpret_cast<const uint4*>(p.norm_w + chunk(j) * 16)), wn);
+      unpack8(__ldg(reinterpret_cast<const uint4*>(p.norm_w + chunk(j) * 16 + 8)), wn + 8);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) f[e] = bf(wn[e] * bf(f[e] * rstd));
+    }
+  };
+  if constexpr (tc_bf16_operand(FMT)) {
+    if (work)
+#pragma unroll
+      for (int j = 0; j < kRowsChunks; ++j) {
+        float f[16];
+        values16(j, f);
+        *reinterpret_cast<uint4*>(xt + off(ml, 2 * chunk(j))) = pack8(f);
+        *reinterpret_cast<uint4*>(xt + off(ml, 2 * chunk(j) + 1)) = pack8(f + 8);
+      }
+  } else {
+    float am = 0.f;
+    if (work)
+#pragma unroll
+      for (int j = 0; j < kRowsChunks; ++j) {
+        float f[16];
+        values16(j, f);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) am = fmaxf(am, fabsf(f[e]));
+      }
+    am = row_total(warp_max(am), 1, true);
+    const int shift = tc_fp8_shift(am);  // max |x| 2^shift in [128, 256)
+    if (work) {
+      if (sec == 0 && lane == 0) xshift[m] = shift;
+#pragma unroll
+      for (int j = 0; j < kRowsChunks; ++j) {
+        float f[16];
+        values16(j, f);
+        uint4 w0, w1;
+        e4m3_split16(f, shift, w0, w1);
+        *reinterpret_cast<uint4*>(xt + off(ml, chunk(j))) = w0;
+        *reinterpret_cast<uint4*>(xt + off(mp + ml, chunk(j))) = w1;
+      }
+    }
+  }
+  if (zero) {
+#pragma unroll
+    for (int j = 0; j < kRowsChunks; ++j)
+#pragma unroll
+      for (int e = 0; e < CPE; ++e) {
+        *reinterpret_cast<uint4*>(xt + off(ml, CPE * chunk(j) + e)) = make_uint4(0, 0, 0, 0);
+        if (FMT == SB_FMT_FP8) *reinterpret_cast<uint4*>(xt + off(mp + ml, chunk(j))) = make_uint4(0, 0, 0, 0);
+      }
+    if (FMT == SB_FMT_FP8 && sec == 0 && lane == 0) xshift[m] = 0;
+  }
+}
+
 // One CTA per (padded) token row; the row is read once into registers (16
 // consecutive elements per thread and chunk), then RMSNorm statistics, the
 // power-of-two scale and the e4m3 split are all computed from registers.
@@ -742,15 +881,20 @@ static int tc_launch_t(const GemvParams& p0, const void* w_tc, void* operand, co
   cudaLaunchConfig_t cfg = {};
   const int rows = pl.mp * pl.mtiles;
   const bool per_warp = pl.mtiles > 1;
-  cfg.gridDim = dim3(per_warp ? (rows + kPrepRows - 1) / kPrepRows : rows);
-  cfg.blockDim = dim3(per_warp ? kPrepThreads : kPrepCtaThreads);
+  // many rows: rows held in registers when K is 2048 x (1, 2, 4 or 8), else one warp per row
+  const int S = p.k % (32 * 16 * kRowsChunks) == 0 ? p.k / (32 * 16 * kRowsChunks) : 0;
+  const bool in_regs = per_warp && (S == 1 || S == 2 || S == 4 || S == 8);
+  cfg.gridDim = dim3(in_regs ? (rows + 8 / S - 1) / (8 / S) : per_warp ? (rows + kPrepRows - 1) / kPrepRows : rows);
+  cfg.blockDim = dim3(in_regs ? 256 : per_warp ? kPrepThreads : kPrepCtaThreads);
   cfg.stream = stream;
   cfg.attrs = at;
   cfg.numAttrs = pdl ? 1 : 0;
   if (!operand_ready) {  // else the preceding kernel wrote the operand (and, fp8, its per-rank shifts)
     note_launch();
-    cudaError_t e = per_warp ? cudaLaunchKernelEx(&cfg, k_tc_prep_warp<FMT>, p, xq, xshift, pl.mp, pl.np, rows)
-                             : cudaLaunchKernelEx(&cfg, k_tc_prep_cta<FMT>, p, xq, xshift, pl.mp, pl.np);
+    cudaError_t e =
+        in_regs    ? cudaLaunchKernelEx(&cfg, k_tc_prep_rows<FMT>, p, xq, xshift, pl.mp, pl.np, rows, S)
+        : per_warp ? cudaLaunchKernelEx(&cfg, k_tc_prep_warp<FMT>, p, xq, xshift, pl.mp, pl.np, rows)
+                   : cudaLaunchKernelEx(&cfg, k_tc_prep_cta<FMT>, p, xq, xshift, pl.mp, pl.np);
     if (e != cudaSuccess) return e;
   }
 
