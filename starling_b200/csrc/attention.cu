@@ -457,7 +457,30 @@ __global__ void __launch_bounds__(256, 2)
     for (int mi = tid; mi < p.m_per; mi += blockDim.x) s_tmax[mi] = 0;
     __syncthreads();
   }
-  if (rank == 0) {
+  // without the o operand every rank of a cluster finishes a slice of the
+  // outputs (four at a time); with it rank 0 finishes them all, as it builds
+  // the operand from each token's whole slice.  Sums run in rank order either way.
+  const bool spread = split > 1 && !p.opnd;
+  if (spread) {
+    const int n4 = R * 32, per = (n4 + split - 1) / split;
+    const int g1 = (rank + 1) * per < n4 ? (rank + 1) * per : n4;
+    for (int gi4 = rank * per + tid; gi4 < g1; gi4 += blockDim.x) {
+      float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int q = 0; q < split; ++q) {
+        const float4 v = reinterpret_cast<const float4*>(cg::this_cluster().map_shared_rank(outp, q))[gi4];
+        s4.x += v.x;
+        s4.y += v.y;
+        s4.z += v.z;
+        s4.w += v.w;
+      }
+      const int i = gi4 * 4, r = i >> 7, dd = i & 127;
+      const int mi = r / G, gi = r % G;
+      const size_t t = static_cast<size_t>(zb) * p.m_per + mi;
+      const uint32_t lo = static_cast<uint32_t>(f_to_bf16_bits(s4.x)) | (static_cast<uint32_t>(f_to_bf16_bits(s4.y)) << 16);
+      const uint32_t hi = static_cast<uint32_t>(f_to_bf16_bits(s4.z)) | (static_cast<uint32_t>(f_to_bf16_bits(s4.w)) << 16);
+      *reinterpret_cast<uint2*>(p.out + t * p.n_q * 128 + (kvh * G + gi) * 128 + dd) = make_uint2(lo, hi);
+    }
+  } else if (rank == 0) {
     for (int i = tid; i < R * 128; i += blockDim.x) {
       float s = 0.f;
       for (int q = 0; q < split; ++q) s += split > 1 ? cg::this_cluster().map_shared_rank(outp, q)[i] : outp[i];
