@@ -866,8 +866,38 @@ __device__ __forceinline__ void attn_phase(const StepParams& P, Cx& cx, int laye
   }
   csync();
 
-  // scores: 4 lanes per (row, key) pair, lane quarter qd takes words qd, qd+4, ..
-  // in an order rotated by the key (conflict-free); score = bf16(bf16(q.k) * scale)
+  // scores, score = bf16(bf16(q.k) * scale).  Eight or more query rows (verify):
+  // mma.sync m16n8k16 over (16-row block, 8-key block) tiles, one per warp, the
+  // fragments read as 32-bit words of the q and K rows.  Fewer: 4 lanes per
+  // (row, key) pair, lane quarter qd taking words qd, qd+4, .. in an order
+  // rotated by the key (conflict-free).
+  if (R >= 8) {
+    const int nrb = (R + 15) / 16, nkb = (nk + 7) / 8, g = lane >> 2, c = lane & 3;
+    for (int t = warp; t < nrb * nkb; t += kCW) {
+      const int rb = t / nkb, kb = t % nkb;
+      const int r0 = rb * 16 + g, r1 = r0 + 8, key = kb * 8 + g;
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        uint32_t af[4];
+        af[0] = r0 < R ? cx.aq[r0 * 64 + ks * 8 + c] : 0u;
+        af[1] = r1 < R ? cx.aq[r1 * 64 + ks * 8 + c] : 0u;
+        af[2] = r0 < R ? cx.aq[r0 * 64 + ks * 8 + c + 4] : 0u;
+        af[3] = r1 < R ? cx.aq[r1 * 64 + ks * 8 + c + 4] : 0u;
+        const uint32_t b0 = key < nk ? kw[key * 64 + ks * 8 + c] : 0u;
+        const uint32_t b1 = key < nk ? kw[key * 64 + ks * 8 + c + 4] : 0u;
+        mma_bf16(d, af, b0, b1);
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int r = e < 2 ? r0 : r1, j = kb * 8 + 2 * c + (e & 1);
+        if (r < R && j < nk) {
+          const bool valid = u.pos(u.ka + j) <= slot + r / G;  // causal limit slot + token
+          cx.asc[r * kStepKeys + j] = valid ? bf(bf(d[e]) * P.attn_mult) : -INFINITY;
+        }
+      }
+    }
+  } else
   for (int base = 0; base < R * nk; base += kCW * 8) {
     const int pp = base + warp * 8 + (lane >> 2), qd = lane & 3;
     const bool on = pp < R * nk;
@@ -919,6 +949,32 @@ __device__ __forceinline__ void attn_phase(const StepParams& P, Cx& cx, int laye
   }
   csync();
   float* part = P.attn_part + (static_cast<size_t>(u.bh) * NS) * R * 128;
+  if (R >= 8) {
+    // P.V on mma.sync: one (16-row block, 8-dim block) tile per warp, the
+    // probabilities (bf16 values) and V rows packed into fragments, keys past
+    // the split's own zero
+    const int nrb = (R + 15) / 16, g = lane >> 2, c = lane & 3;
+    float* pp = part + static_cast<size_t>(u.s) * R * 128;
+    auto pv = [&](int r, int j) { return r < R && j < nk ? cx.asc[r * kStepKeys + j] : 0.f; };
+    for (int t = warp; t < nrb * 16; t += kCW) {
+      const int rb = t >> 4, db = t & 15;
+      const int r0 = rb * 16 + g, r1 = r0 + 8, dim = db * 8 + g;
+      auto vv = [&](int j) -> uint32_t { return j < nk ? static_cast<uint32_t>(vr[j * 128 + dim]) : 0u; };
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int ks = 0; ks * 16 < nk; ++ks) {
+        const int k0 = ks * 16 + 2 * c;
+        uint32_t af[4];
+        af[0] = pack_bf2(pv(r0, k0), pv(r0, k0 + 1));
+        af[1] = pack_bf2(pv(r1, k0), pv(r1, k0 + 1));
+        af[2] = pack_bf2(pv(r0, k0 + 8), pv(r0, k0 + 9));
+        af[3] = pack_bf2(pv(r1, k0 + 8), pv(r1, k0 + 9));
+        mma_bf16(d, af, vv(k0) | (vv(k0 + 1) << 16), vv(k0 + 8) | (vv(k0 + 9) << 16));
+      }
+      const int dd = db * 8 + 2 * c;
+      if (r0 < R) *reinterpret_cast<float2*>(pp + r0 * 128 + dd) = make_float2(d[0], d[1]);
+      if (r1 < R) *reinterpret_cast<float2*>(pp + r1 * 128 + dd) = make_float2(d[2], d[3]);
+    }
+  } else
   for (int o = tid; o < R * 128; o += kCW * 32) {
     const int r = o >> 7, d = o & 127;
     const float* pr = cx.asc + r * kStepKeys;
