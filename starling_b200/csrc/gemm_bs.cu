@@ -355,8 +355,12 @@ __global__ void __launch_bounds__(kTcThreads, 2) k_bs_gemm(const __grid_constant
       eb2 = eb2 < E - 9 ? E - 9 : (eb2 > E + 8 ? E + 8 : eb2);
       const int d = eb2 - E;  // -9..8: e4m3 2^d, subnormal below 2^-6
       const uint8_t s8 = static_cast<uint8_t>(d >= -6 ? (d + 7) << 3 : 1 << (d + 9));
+      // x 2^-eb2: an exact multiply when 2^-eb2 is a normal float (the same
+      // result as ldexpf, which stays for the extreme exponents)
+      const bool fast = eb2 >= -126 && eb2 <= 126;
+      const float sc = fast ? __int_as_float((127 - eb2) << 23) : 0.f;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) y[e] = ldexpf(y[e], -eb2);
+      for (int e = 0; e < 8; ++e) y[e] = fast ? y[e] * sc : ldexpf(y[e], -eb2);
       const int kbl = e0 >> 8, eb = e0 & 255;         // K block of the CTA range, element within it
       const int kbyte = eb >> 1;                       // byte of the 128-byte row (4-byte aligned)
       const int kstep = eb >> 6, blk = (eb >> 4) & 3;  // MMA of the block (64 elements), 16-element block
@@ -427,7 +431,11 @@ __global__ void __launch_bounds__(kTcThreads, 2) k_bs_gemm(const __grid_constant
             const int E = s_gexp[m0 + i];
             float acc = 0.f;
 #pragma unroll
-            for (int tt = 0; tt < kBsTerms; ++tt) acc = fmaf(__uint_as_float(d[i][tt]), ldexpf(1.f, E - 2 * tt), acc);
+            for (int tt = 0; tt < kBsTerms; ++tt) {
+              const int e2 = E - 2 * tt;  // 2^e2 exactly: bit pattern when normal, else ldexpf
+              const float w2 = e2 >= -126 && e2 <= 127 ? __int_as_float((e2 + 127) << 23) : ldexpf(1.f, e2);
+              acc = fmaf(__uint_as_float(d[i][tt]), w2, acc);
+            }
             v[i] = acc;
           }
       }
