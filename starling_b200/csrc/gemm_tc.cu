@@ -23,18 +23,20 @@
 //    of e4m3 values are exact, so the result differs from the dequantised
 //    fp32 reference only by fp32 accumulation order.
 //
-// Kernel (320 threads, one CTA per SM):
-//  * warp 8 (one thread) streams (A block, B block) pairs into a ring of
+// Kernel (NEPI epilogue warps + 2: 16 + 2 with one CTA per SM, 8 + 2 with two):
+//  * warp NEPI (one thread) streams (A block, B block) pairs into a ring of
 //    shared-memory stages with bulk copies completing on mbarriers; the weight
 //    blocks of the first ring are issued BEFORE griddepcontrol.wait, so they
 //    overlap the previous kernel.  CTAs start their K loop at different
 //    blocks so that they do not all read the same activation block from L2;
-//  * warp 9 (one thread) issues four tcgen05.mma (K = 32 bytes each) per
-//    stage into one of two TMEM accumulators and frees the stage with
+//  * warp NEPI + 1 (one thread) issues four tcgen05.mma (K = 32 bytes each)
+//    per stage into one of two TMEM accumulators and frees the stage with
 //    tcgen05.commit;
-//  * warps 0-7 read the 128 x N fp32 accumulator (warps w and w + 4 share
-//    TMEM lanes 32w..32w+31 = tile rows and split the tokens), undo the
-//    activation scaling and run the fused row-owned epilogue (tc_epi.cuh).
+//  * warps 0..NEPI-1 read the 128 x N fp32 accumulator (warp w reads TMEM
+//    lanes 32 (w % 4).. = tile rows; the NEPI / 4 warps of a lane quarter
+//    interleave over 8-token chunks), undo the activation scaling and run the
+//    fused row-owned epilogue (tc_epi.cuh).  Sixteen warps keep a 128-token
+//    prefill tile's epilogue shorter than its MMAs.
 // With many tiles (lm_head, gate/up) each CTA is persistent over tiles and the
 // epilogue of one tile overlaps the MMAs of the next (double-buffered
 // accumulator; with one token tile and hundreds of weight tiles, two CTAs of
