@@ -114,11 +114,14 @@ def _linear_tc(p, x, pdl=0):
 @pytest.mark.parametrize("fmt", ["bf16", "fp8"])
 @pytest.mark.parametrize("n,k,m", [(3072, 2048, 48), (2048, 8192, 48), (16384, 2048, 48), (2051, 512, 9),
                                    (4096, 1024, 16), (1000, 2048, 33), (2048, 2048, 64), (640, 1024, 128),
-                                   (384, 512, 300), (2048, 2048, 1000), (1000, 1024, 8300)])
+                                   (384, 512, 300), (2048, 2048, 1000), (1000, 1024, 8300),
+                                   (1024, 4096, 300), (512, 8192, 200)])
 def test_linear_tensor_cores(fmt, n, k, m):
     """tcgen05 GEMM (9..128 rows per block, fp8 activations as two e4m3 terms)
     vs the fp32 reference over the exactly dequantised weight: same bar as the
-    GEMV (one bf16 rounding step)."""
+    GEMV (one bf16 rounding step).  Above 128 rows with K = 2048 x (1, 2, 4)
+    the activation operand is prepared with each row in registers (one warp
+    per 2048-element section); other K use one warp per row."""
     w = _w(n, k, seed=n + k + m)
     x = torch.randn(m, k, generator=torch.Generator().manual_seed(6)).to(BF16)
     p = pack.pack_matrix(w, fmt, tc=True)
