@@ -225,7 +225,7 @@ PROFILED_TRAFFIC = {
     ("b48", "gate_up"): (33.9008e6, 33.62e6, "profiles/tcgen05_gemm_gate_up_fp8_b48.md"),
     ("b1", "gate_up"): (18.93376e6, 18.87e6, "profiles/gemv_gate_up_nvfp4_b1.md"),
     # 4 layers + lm_head: 4 x 34.21 MB + 115.61 MB of NVFP4 weights + K/V rows
-    ("b1", "step"): (255.4e6 + 4.4e6, 4 * 34.21e6 + 115.61e6 + 2.6e6, "profiles/fused_step_b1_nvfp4.md"),
+    ("b1", "step"): (255.986688e6 + 4.75648e6, 4 * 34.21e6 + 115.61e6 + 2.6e6, "profiles/fused_step_b1_nvfp4.md"),
 }
 
 
