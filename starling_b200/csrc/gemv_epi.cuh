@@ -143,10 +143,28 @@ __device__ __forceinline__ void gemv_argmax_finish(const GemvParams& p, int* s_b
   __syncthreads();
   if (!*s_flag) return;
   __threadfence();
+  // a warp per token; each lane's partials are all loaded before any is
+  // compared (one L2 round trip instead of one per 32 CTAs).  The order is
+  // total, so the result does not depend on the comparison order.
+  constexpr int kPerLane = 12;  // up to 384 CTAs in registers; more take a second loop
   for (int m = warp; m < M; m += W) {
     float bv = -INFINITY;
     int bi = 0x7fffffff;
-    for (int q = lane; q < p.n_ctas; q += 32) {
+    float vv[kPerLane];
+    int iv[kPerLane];
+#pragma unroll
+    for (int j = 0; j < kPerLane; ++j) {
+      const int q = lane + 32 * j;
+      vv[j] = q < p.n_ctas ? __ldcg(p.part_val + static_cast<size_t>(q) * M + m) : -INFINITY;
+      iv[j] = q < p.n_ctas ? __ldcg(p.part_idx + static_cast<size_t>(q) * M + m) : 0x7fffffff;
+    }
+#pragma unroll
+    for (int j = 0; j < kPerLane; ++j)
+      if (am_better(vv[j], iv[j], bv, bi)) {
+        bv = vv[j];
+        bi = iv[j];
+      }
+    for (int q = lane + 32 * kPerLane; q < p.n_ctas; q += 32) {
       const float v = __ldcg(p.part_val + static_cast<size_t>(q) * M + m);
       const int ix = __ldcg(p.part_idx + static_cast<size_t>(q) * M + m);
       if (am_better(v, ix, bv, bi)) {

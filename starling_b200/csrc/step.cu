@@ -1038,7 +1038,24 @@ __device__ void lm_finish(const StepParams& P, Cx& cx, bool has_rows) {
   for (int m = warp; m < M; m += kCW) {
     float bv = -INFINITY;
     int bi = 0x7fffffff;
-    for (int q = lane; q < nct; q += 32) {
+    // every partial of this lane loaded before any is compared (one L2 round
+    // trip); the order is total, so the comparison order does not matter
+    constexpr int kPerLane = 8;  // up to 256 CTAs in registers
+    float vv[kPerLane];
+    int iv[kPerLane];
+#pragma unroll
+    for (int j = 0; j < kPerLane; ++j) {
+      const int q = lane + 32 * j;
+      vv[j] = q < nct ? __ldcg(P.am_val + static_cast<size_t>(q) * M + m) : -INFINITY;
+      iv[j] = q < nct ? __ldcg(P.am_idx + static_cast<size_t>(q) * M + m) : 0x7fffffff;
+    }
+#pragma unroll
+    for (int j = 0; j < kPerLane; ++j)
+      if (am_better(vv[j], iv[j], bv, bi)) {
+        bv = vv[j];
+        bi = iv[j];
+      }
+    for (int q = lane + 32 * kPerLane; q < nct; q += 32) {
       const float v = __ldcg(P.am_val + static_cast<size_t>(q) * M + m);
       const int ix = __ldcg(P.am_idx + static_cast<size_t>(q) * M + m);
       if (am_better(v, ix, bv, bi)) {
