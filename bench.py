@@ -342,7 +342,7 @@ def _oracle_model():
 
     if "m" not in _ORACLE:
         torch.set_grad_enabled(False)
-        d = gr.BASELINE_DIMS
+        d = gr.GRANITE_1B_DIMS
         _ORACLE["m"] = gr.OracleModel(d, gr.make_weights(d, seed=0, std=0.02))
     return _ORACLE["m"]
 

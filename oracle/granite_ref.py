@@ -64,7 +64,7 @@ class Dims:
 
 
 # Granite multipliers come from src/starling/config.py:57-60.
-BASELINE_DIMS = Dims()
+GRANITE_1B_DIMS = Dims()
 # Small model for golden fixtures: head_dim stays 128 (the kernels' head size),
 # an odd vocabulary exercises the lm_head row tail.
 TINY_DIMS = Dims(hidden=512, n_q=4, n_kv=2, head_dim=128, inter=1024, vocab=2051, layers=2)

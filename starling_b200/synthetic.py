@@ -22,7 +22,7 @@ import torch
 from .engine import GraniteDims
 
 BF16 = torch.bfloat16
-BASELINE = GraniteDims()
+GRANITE_1B = GraniteDims()
 
 
 def weight_shapes(d: GraniteDims):
@@ -44,7 +44,7 @@ def weight_shapes(d: GraniteDims):
     return out
 
 
-def make_weights(d: GraniteDims = BASELINE, seed: int = 0, std: float = 0.02, device="cuda") -> dict:
+def make_weights(d: GraniteDims = GRANITE_1B, seed: int = 0, std: float = 0.02, device="cuda") -> dict:
     """N(0, std) bf16 matrices drawn on ``device`` from one seeded generator."""
     g = torch.Generator(device=device).manual_seed(seed)
     w = {}

@@ -182,8 +182,8 @@ def main():
     )
     print("spec ids equal greedy:", rs.ids[0].tolist() == greedy, rs.accepted, rs.verify_forwards)
 
-    # -- one BASELINE-size decoder layer, 256 cached positions ----------------
-    D = gr.BASELINE_DIMS
+    # -- one Granite-1B-size decoder layer, 256 cached positions ----------------
+    D = gr.GRANITE_1B_DIMS
     w, kc, vc, x, past = gr.layer_step_case(D, seed=0, past=256, std=0.02)
     cfg = hf_config(gr.Dims(**{**D.__dict__, "layers": 1}))
     with local_torch_dtype(torch.bfloat16):

@@ -260,8 +260,8 @@ def test_one_layer_baseline_dims(golden_dir):
     intermediate 8192), 256 cached positions, then final norm + lm_head."""
     g = torch.load(golden_dir / "layer_step.pt")
     # embedding multiplier 1 so that the layer input is exactly the embedding row
-    D = gr.Dims(**{**gr.BASELINE_DIMS.__dict__, "layers": 1, "emb_mult": 1.0})
-    wl, kc, vc, x, past = gr.layer_step_case(gr.BASELINE_DIMS, seed=g["seed"], past=g["past"], std=g["std"])
+    D = gr.Dims(**{**gr.GRANITE_1B_DIMS.__dict__, "layers": 1, "emb_mult": 1.0})
+    wl, kc, vc, x, past = gr.layer_step_case(gr.GRANITE_1B_DIMS, seed=g["seed"], past=g["past"], std=g["std"])
     gen = torch.Generator().manual_seed(4)
     w = dict(wl)
     tok = 5
@@ -276,10 +276,10 @@ def test_one_layer_baseline_dims(golden_dir):
     st.set_slot(past, pad_len=past)
     eng.decode_step(st, 0)
     # oracle: layer step + final norm + lm_head on the same weights
-    om_layer = gr.make_layer(gr.BASELINE_DIMS, wl, 0)
+    om_layer = gr.make_layer(gr.GRANITE_1B_DIMS, wl, 0)
     kc2, vc2 = kc.clone(), vc.clone()
     with gr.accumulate("bf16"):  # the reference's own order: compared bit for bit with its golden output
-        y = gr.layer_step(gr.BASELINE_DIMS, om_layer, kc2, vc2, x, past)
+        y = gr.layer_step(gr.GRANITE_1B_DIMS, om_layer, kc2, vc2, x, past)
     assert torch.equal(y.reshape(-1), g["y"])  # oracle == reference golden
     k_got, k_ref = eng.kv[0, 0, 0, :, past].cpu().float(), kc2[0, :, past].float()
     assert torch.allclose(k_got, k_ref, rtol=2 ** -6, atol=1e-2)  # new K row (RoPE'd), 1-ulp slack

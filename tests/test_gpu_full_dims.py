@@ -46,7 +46,7 @@ from starling_b200.multistep import MultiStepLLMMega  # noqa: E402
 torch.set_grad_enabled(False)
 torch.set_num_threads(min(os.cpu_count() or 1, 16))
 
-D = gr.BASELINE_DIMS
+D = gr.GRANITE_1B_DIMS
 RTOL = 1e-2
 ATOL_FRAC = 2.0 ** -5  # 4 bf16 steps of the largest logit
 REL_L2 = 0.05  # 1.5x the reference's own distance from the float64 result

@@ -324,7 +324,7 @@ def test_glue_rmsnorm_silu_residual():
 
 
 def test_glue_rope_bit_exact():
-    d = gr.BASELINE_DIMS
+    d = gr.GRANITE_1B_DIMS
     cs, sn = rope_tables(128, d.theta, 1024)
     pos = torch.tensor([0, 7, 300, 1023], dtype=torch.int32)
     q = (torch.randn(4, 16, 128, generator=torch.Generator().manual_seed(2)) * 20).to(BF16)
@@ -337,7 +337,7 @@ def test_glue_rope_bit_exact():
 
 
 def test_rope_table_matches_hf_formula():
-    d = gr.BASELINE_DIMS
+    d = gr.GRANITE_1B_DIMS
     cs, sn = rope_tables(128, d.theta, 700)
     c, s = gr.rope_cos_sin(d, torch.arange(700).view(1, -1))
     assert torch.equal(cs, c[0, :, :64]) and torch.equal(sn, s[0, :, :64])

@@ -56,7 +56,7 @@ def test_speculative(tiny, golden_dir):
 
 def test_layer_step_baseline_dims(golden_dir):
     g = torch.load(golden_dir / "layer_step.pt")
-    D = gr.BASELINE_DIMS
+    D = gr.GRANITE_1B_DIMS
     w, kc, vc, x, past = gr.layer_step_case(D, seed=g["seed"], past=g["past"], std=g["std"])
     assert torch.equal(x, g["x"])
     L = gr.make_layer(D, w, 0)
