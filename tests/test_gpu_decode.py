@@ -488,3 +488,38 @@ def test_speculative_device_loop_stops_like_host_loop(golden, case):
         (host.verify_forwards, host.accepted, host.decode_steps)
     if case == "eos_in_draft":
         assert host.ids[0].tolist()[-1] == eos and len(host.ids[0]) <= 9
+
+
+@pytest.mark.gpu
+def test_static_cache_budget_errors(golden):
+    """The reference's static-cache budget checks, with its error texts
+    (multistep.py:72-95, batched.py generate): too many new tokens for the
+    cache, K-rounded chunks past the cache end, a batch the decoder is not
+    sized for; the decoders stay usable after each error."""
+    d, w, g = golden
+    emb = g["inputs_embeds"].cuda()
+    T, L = emb.shape[1], 96
+    max_safe = L - T + 1
+    dec = MultiStepLLMMega(weights=w, dims=d.__dict__, max_cache_len=L, steps_per_replay=8)
+    with pytest.raises(ValueError, match="would overflow the static KV"):
+        dec.generate(emb, max_new_tokens=max_safe + 1)
+    with pytest.raises(ValueError, match="only supports batch=1"):
+        dec.generate(emb.repeat(2, 1, 1), max_new_tokens=4)
+    # a budget that fits, but whose K-step chunks, rounded up, do not
+    K = next(k for k in (8, 16, 32) if any(T - 1 + -(-(n - 1) // k) * k >= L for n in range(2, max_safe + 1)))
+    n = next(n for n in range(2, max_safe + 1) if T - 1 + -(-(n - 1) // K) * K >= L)
+    deck = MultiStepLLMMega(weights=w, dims=d.__dict__, max_cache_len=L, steps_per_replay=K)
+    with pytest.raises(ValueError, match="rounded-up decode"):
+        deck.generate(emb, max_new_tokens=n)
+    got = dec.generate(emb, max_new_tokens=8).ids[0].tolist()
+    margins = [_margin(g["prefill_logits"])] + [_margin(x) for x in g["step_logits"]]
+    _assert_ids_match(got, g["ids"].tolist()[:8], margins, _logit_tol(g["prefill_logits"]),
+                      "decode after the budget errors")
+
+    bdec = BatchedLLMMega(weights=w, dims=d.__dict__, max_cache_len=L, max_batch_size=2, steps_per_replay=8)
+    with pytest.raises(ValueError, match="!= max_batch_size"):
+        bdec.generate(emb.repeat(3, 1, 1), max_new_tokens=4)
+    with pytest.raises(ValueError, match="would overflow the static KV cache"):
+        bdec.generate(emb.repeat(2, 1, 1), max_new_tokens=max_safe + 1)
+    res = bdec.generate(emb.repeat(2, 1, 1), max_new_tokens=8)
+    assert res.ids_list[0].tolist() == res.ids_list[1].tolist() == got
