@@ -227,12 +227,17 @@ __global__ void __launch_bounds__(256, 2)
 
   const int total = 2 * nT;
   const int first = total < p.slots ? total : p.slots;
-  // zero the ring once: rows of a slot that a tail tile does not load then
-  // hold zeros or an older tile's finite keys / values, which its masked
-  // scores and zero probabilities cancel
-  for (size_t i = tid; i < static_cast<size_t>(p.slots) * kTileBytes / 16; i += blockDim.x)
-    reinterpret_cast<uint4*>(ring)[i] = make_uint4(0u, 0u, 0u, 0u);
-  fence_proxy_async();  // before the tensor copies write the same bytes
+  // rows of a slot that a tail tile does not load must hold finite values
+  // (its masked scores and zero probabilities cancel them): an older tile's
+  // keys / values, or, where the slot's first tile is already a tail, zeros
+  bool zeroed = false;
+  for (int s0 = 0; s0 < first; ++s0)
+    if (item_bytes(s0) < kTileBytes) {
+      uint4* z = reinterpret_cast<uint4*>(ring + static_cast<size_t>(s0) * kTileBytes);
+      for (int i = tid; i < kTileBytes / 16; i += blockDim.x) z[i] = make_uint4(0u, 0u, 0u, 0u);
+      zeroed = true;
+    }
+  if (zeroed) fence_proxy_async();  // before the tensor copies write the same bytes
   __syncthreads();
   if (tid == 0) {
     for (int s = 0; s < p.slots; ++s) mbar_init(bars + s, 1);
