@@ -205,8 +205,13 @@ size_t sb_decode_step_scratch_offset(const SbModel* model, int32_t tokens);
  * layer ignored for SB_OP_LM_HEAD.  Where the o projection runs on the
  * tensor-core GEMM (9..128 token rows) the attention launch writes its
  * activation operand, so SB_OP_O computes from what the last SB_OP_ATTN of
- * the same state and token count wrote.  No reference counterpart (the
- * reference step has no separable kernels of this kind). */
+ * the same state and token count wrote.  With fp8 weights at 9..64 token
+ * rows the o, gate/up and down launches likewise write the next
+ * projection's operand (and, after a residual, the next RMSNorm's
+ * statistics): SB_OP_GATE_UP computes from what the last SB_OP_O wrote,
+ * SB_OP_DOWN from the last SB_OP_GATE_UP, SB_OP_QKV of layers > 0 from the
+ * last SB_OP_DOWN.  No reference counterpart (the reference step has no
+ * separable kernels of this kind). */
 #define SB_OP_QKV 0
 #define SB_OP_ATTN 1
 #define SB_OP_O 2

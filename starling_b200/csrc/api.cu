@@ -91,6 +91,37 @@ static bool tc_plan_for(const SbLinear& l, int m, TcPlan& pl) {
   return m > min_rows && l.w_tc && tc_plan(l.fmt, l.n, l.k, m, pl);
 }
 
+// Tensor-core decode chain (fp8 weights, 9..64 token rows, every layer): the
+// o and down GEMMs' residual epilogues and the gate/up GEMM's SwiGLU epilogue
+// write the next projection's block-scaled operand -- with, after a residual,
+// per-32-row sums of squares for the RMSNorm that follows -- so q/k/v (layers
+// >= 1), gate/up and down run without a preparation launch.  Layer 0's q/k/v
+// (embedding input) and the lm_head keep theirs.
+struct ChainPlan {
+  TcPlan qkv, gu, down;  // the consumers' block-scaled plans
+};
+static bool chain_plan(const SbModel* md, int T, ChainPlan& c) {
+  if (!md->layers || md->n_layers < 1 || T < 9 || T > 64) return false;
+  for (int l = 0; l < md->n_layers; ++l) {
+    const SbLayer& L = md->layers[l];
+    const SbLinear* lins[4] = {&L.qkv, &L.o, &L.gate_up, &L.down};
+    for (const SbLinear* x : lins)
+      if (x->fmt != SB_FMT_FP8 || !x->w_tc) return false;
+  }
+  const SbLayer& L = md->layers[0];
+  TcPlan op;  // o keeps its own operand (the attention's) and only produces
+  if (!tc_plan_for(L.o, T, op) || op.mtiles != 1 || (op.split != 2 && op.split != 4) || op.epi_warps != kTcMaxEpiWarps)
+    return false;
+  // a producer writes whole 32-element blocks from one CTA: a residual GEMM
+  // the rows of its rank (K split 2 or 4: 64 or 32 rows), the SwiGLU GEMM a
+  // whole tile's 64 activations (no K split)
+  if (!tc_plan_bs(L.qkv.n, L.qkv.k, T, 8, c.qkv) || !tc_plan_bs(L.gate_up.n, L.gate_up.k, T, 1, c.gu) ||
+      !tc_plan_bs(L.down.n, L.down.k, T, 4, c.down))
+    return false;
+  return c.gu.split == 1 && (c.down.split == 2 || c.down.split == 4) && L.o.n % 128 == 0 && L.down.k % 128 == 0 &&
+         L.qkv.k == L.o.n && L.gate_up.k == L.o.n && L.gate_up.n == 2 * L.down.k;
+}
+
 static int run_gemv(GemvParams& p, int fmt, bool pdl, cudaStream_t s) {
   DecPlan pl;
   if (p.m <= 8 && dec_plan_for(fmt, p.n_tiles, p.k, p.m, pl)) {
@@ -238,9 +269,10 @@ static LmWork lm_work(const SbModel* md, int tokens, void* base, bool exact = fa
   return w;
 }
 
-// Workspace = [lm_head argmax partials | tensor-core operand scratch | fused-step scratch].
+// Workspace = [lm_head argmax partials | tensor-core operand scratch | fused-step
+// scratch | decode-chain operands: hidden-wide, inter-wide, sums of squares].
 struct WsLayout {
-  size_t lm_bytes, tc_off, tc_bytes, step_off, step_bytes, total;
+  size_t lm_bytes, tc_off, tc_bytes, step_off, step_bytes, chain_off, chain_op1, chain_op2, chain_ssq, total;
 };
 static size_t tc_scratch_need(const SbLinear& l, int tokens) {
   TcPlan pl;
@@ -264,6 +296,16 @@ static WsLayout ws_layout(const SbModel* md, int tokens) {
   w.step_bytes = md->n_q > 0 ? step_ws_bytes(md, tokens) : 0;
   w.step_off = (w.total + 255) & ~size_t(255);
   if (w.step_bytes) w.total = w.step_off + w.step_bytes;
+  w.chain_off = w.chain_op1 = w.chain_op2 = w.chain_ssq = 0;
+  ChainPlan c;
+  if (chain_plan(md, tokens, c)) {
+    const SbLayer& L = md->layers[0];
+    w.chain_off = (w.total + 255) & ~size_t(255);
+    w.chain_op1 = (tc_bs_operand_bytes(L.o.n, tokens) + 255) & ~size_t(255);
+    w.chain_op2 = (tc_bs_operand_bytes(L.down.k, tokens) + 255) & ~size_t(255);
+    w.chain_ssq = static_cast<size_t>(L.o.n / 32) * 64 * 4;
+    w.total = w.chain_off + w.chain_op1 + w.chain_op2 + w.chain_ssq;
+  }
   return w;
 }
 // The state's workspace must hold ws_layout().total bytes; tc scratch is
@@ -273,6 +315,23 @@ static int tc_scratch_of(const SbModel* md, const SbState* st, void*& ptr, size_
   if (st->workspace_bytes < w.total) return fail(SB_ERR_ARG, "workspace too small (%zu < %zu)", st->workspace_bytes, w.total);
   ptr = w.tc_bytes ? static_cast<char*>(st->workspace) + w.tc_off : nullptr;
   bytes = w.tc_bytes ? st->workspace_bytes - w.tc_off : 0;
+  return 0;
+}
+
+// The decode chain's buffers inside the state's workspace (chain_plan holds).
+struct ChainBufs {
+  uint8_t* op1;  // hidden-wide operand: q/k/v's (from down) and gate/up's (from o)
+  uint8_t* op2;  // inter-wide operand: down's (from gate/up)
+  float* ssq;    // [64 tokens][hidden / 32] sums of squares of the last residual's rows
+};
+static int chain_bufs(const SbModel* md, const SbState* st, ChainBufs& b) {
+  const WsLayout w = ws_layout(md, st->batch * st->m);
+  if (!w.chain_off) return fail(SB_ERR_CONFIG, "no decode chain for this model / token count");
+  if (st->workspace_bytes < w.total) return fail(SB_ERR_ARG, "workspace too small (%zu < %zu)", st->workspace_bytes, w.total);
+  char* base = static_cast<char*>(st->workspace) + w.chain_off;
+  b.op1 = reinterpret_cast<uint8_t*>(base);
+  b.op2 = reinterpret_cast<uint8_t*>(base + w.chain_op1);
+  b.ssq = reinterpret_cast<float*>(base + w.chain_op1 + w.chain_op2);
   return 0;
 }
 
@@ -423,6 +482,17 @@ static int launch_op(const SbModel* md, const SbState* st, int l, int op, int st
   size_t tcb = 0;
   void* tcs = nullptr;
   SB_TRY(tc_scratch_of(md, st, tcs, tcb));
+  ChainPlan cp;
+  ChainBufs cb;
+  const bool chain = chain_plan(md, T, cp);
+  if (chain) SB_TRY(chain_bufs(md, st, cb));
+  auto launch_bs = [&](const char* what, const GemvParams& p, const SbLinear& lin, const void* operand,
+                       const TcPlan& pl) {
+    const int rc = tc_launch_bs(p, lin.w_tc, operand, pl, pdl, s);
+    if (rc != 0) return fail(rc, "tensor-core gemm launch (%s, block-scaled operand, n=%d k=%d m=%d): %s", what, p.n,
+                             p.k, p.m, rc < 1000 ? cudaGetErrorString((cudaError_t)rc) : "config");
+    return 0;
+  };
   // the tensor-core path computes the RMSNorm prologue in its operand preparation
   auto sep_norm_for = [&](const SbLinear& lin) {
     TcPlan tp;
@@ -457,6 +527,12 @@ static int launch_op(const SbModel* md, const SbState* st, int l, int op, int st
     p.rope_max = md->rope_max_pos;
     p.rope_off = st->rope_off;
     p.ctrl = st->ctrl;
+    if (chain && l > 0) {  // the previous layer's down GEMM wrote the operand and the norm statistics
+      p.pro = PRO_NONE;
+      p.x = nullptr;
+      p.ssq_in = cb.ssq;
+      return launch_bs("q/k/v", p, L.qkv, cb.op1, cp.qkv);
+    }
     return run_linear(L.qkv, p, tcs, tcb, pdl, s);
   }
   if (op == SB_OP_O || op == SB_OP_DOWN) {  // o / down -> residual scale-add into hidden
@@ -467,6 +543,17 @@ static int launch_op(const SbModel* md, const SbState* st, int l, int op, int st
     p.epi = EPI_RESID;
     p.y = st->hidden;
     p.res_mult = md->res_mult;
+    if (chain) {
+      if (op == SB_OP_O || l + 1 < md->n_layers) {  // write gate/up's operand, or the next layer's q/k/v's
+        const TcPlan& nx = op == SB_OP_O ? cp.gu : cp.qkv;
+        p.nx_op = cb.op1;
+        p.nx_g = op == SB_OP_O ? L.post_norm : md->layers[l + 1].in_norm;
+        p.nx_ssq = cb.ssq;
+        p.nx_np = nx.np;
+        p.nx_mp = nx.mp;
+      }
+      if (op == SB_OP_DOWN) return launch_bs("down", p, L.down, cb.op2, cp.down);  // gate/up wrote the operand
+    }
     TcPlan tp;
     if (op == SB_OP_O && o_operand_from_attn(md, st, L, tcs, tp)) {  // the attention wrote the operand
       const size_t need = tc_operand_bytes(lin.fmt, lin.k, T);
@@ -479,6 +566,17 @@ static int launch_op(const SbModel* md, const SbState* st, int l, int op, int st
     return run_linear(lin, p, tcs, tcb, pdl, s);
   }
   // gate/up: RMSNorm -> interleaved gate|up -> SiLU(gate)*up
+  if (chain) {  // o wrote the operand and the norm statistics; write down's operand
+    GemvParams p = base_params(L.gate_up, T);
+    p.eps = md->eps;
+    p.ssq_in = cb.ssq;
+    p.epi = EPI_SWIGLU;
+    p.y = st->act;
+    p.nx_op = cb.op2;
+    p.nx_np = cp.down.np;
+    p.nx_mp = cp.down.mp;
+    return launch_bs("gate/up", p, L.gate_up, cb.op1, cp.gu);
+  }
   GemvParams p = base_params(L.gate_up, T);
   p.pro = PRO_RMSNORM;
   p.x = st->hidden;

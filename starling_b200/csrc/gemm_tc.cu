@@ -61,6 +61,23 @@ namespace sb {
 
 namespace {
 
+__device__ __forceinline__ void tc_fence_proxy_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// 128 rows x 4 bytes of scales from shared memory into four TMEM columns
+// (row r in column r / 32 of lane r % 32, in every lane quarter)
+__device__ __forceinline__ void tc_cp_scales(uint32_t taddr, uint64_t src) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(src) : "memory");
+}
+// e4m3 x e4m3 with a UE8M0 scale per 32 K-elements of each A and B row; the
+// byte of each scale word used is chosen by the descriptor's scale ids
+__device__ __forceinline__ void tc_mma_mx8(uint32_t tmem, uint64_t ad, uint64_t bd, uint32_t idesc, uint32_t tsfa,
+                                          uint32_t tsfb, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n}\n" ::"r"(tmem),
+      "l"(ad), "l"(bd), "r"(idesc), "r"(acc), "r"(tsfa), "r"(tsfb)
+      : "memory");
+}
+
 // fixed-order block reductions over 256 threads
 __device__ __forceinline__ float block_sum256(float v, float* s_red) {
   v = warp_sum(v);
@@ -93,6 +110,9 @@ struct TcArgs {
   int mp, np, tiles, kb, split, stages, ncols;
   int mtiles;  // token tiles of mp rows (EPI_STORE only when > 1: prefill projections)
   int rank_shift;  // fp8: xshift holds one row of shifts per K-split rank (operand written per rank)
+  // block-scaled operand (OPB): TMEM columns allocated; first column of the
+  // weight's scales (4) and of the B scales (4 per stage)
+  int tmem_cols, sfa_col, sfb_col;
 };
 
 // ---- B operand: prologue + layout ------------------------------------------------
@@ -476,7 +496,9 @@ __global__ void __launch_bounds__(kPrepCtaThreads) k_tc_prep_cta(const __grid_co
 
 // ---- the GEMM ----------------------------------------------------------------------
 // NEPI epilogue warps: 8 with two CTAs per SM, 16 with one
-template <int FMT, int EPI, int NEPI>
+// OPB: the B operand is block-scaled (written by the preceding GEMM's epilogue;
+// fp8 only), the MMA kind::mxf8f6f4 with UE8M0 scales
+template <int FMT, int EPI, int NEPI, int OPB>
 __global__ void __launch_bounds__((NEPI + 2) * 32, NEPI == kTcEpiWarps ? 2 : 1)
     k_tc_gemm(const __grid_constant__ GemvParams p, const __grid_constant__ TcArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -484,7 +506,7 @@ __global__ void __launch_bounds__((NEPI + 2) * 32, NEPI == kTcEpiWarps ? 2 : 1)
   constexpr int nepi = NEPI;
   auto epi_bar = [&]() { asm volatile("bar.sync 1, %0;" ::"n"(NEPI * 32) : "memory"); };
   const int M = p.m;
-  const TcLayout L = tc_layout(a.np, a.stages, M, a.split, NEPI);
+  const TcLayout L = tc_layout(a.np, a.stages, M, a.split, NEPI, OPB != 0);
   uint8_t* ring = smem;
   float* part = reinterpret_cast<float*>(smem + L.part);  // split: inbox [src rank][row][ms]
   const int ms = tc_inbox_stride(M);
@@ -533,7 +555,7 @@ __global__ void __launch_bounds__((NEPI + 2) * 32, NEPI == kTcEpiWarps ? 2 : 1)
   // CTAs working at the same time share weight tiles (L2 hits)
   const int items = a.tiles * nlive;
   const int my_tiles = cid < items ? (items - cid + ncl - 1) / ncl : 0;
-  const uint32_t a_bytes = 16384u, b_bytes = static_cast<uint32_t>(a.np) * 128u;
+  const uint32_t a_bytes = 16384u, b_bytes = static_cast<uint32_t>(a.np) * 128u + (OPB ? 512u : 0u);
   // CTAs start their K blocks at different offsets so that they do not all read
   // the same activation block from L2 at the same time
   const int rot = cid % nk;
@@ -551,7 +573,11 @@ __global__ void __launch_bounds__((NEPI + 2) * 32, NEPI == kTcEpiWarps ? 2 : 1)
     }
     mbar_fence_init();
   }
-  if (warp == kMma) tmem_alloc(s_tmem, static_cast<uint32_t>(a.ncols));
+  if (warp == kMma) tmem_alloc(s_tmem, static_cast<uint32_t>(OPB ? a.tmem_cols : a.ncols));
+  if constexpr (OPB != 0) {  // the weight's block scales: all 1.0 (its row scales come in the epilogue)
+    if (tid < 128) reinterpret_cast<uint32_t*>(smem + L.sfa)[tid] = 0x7F7F7F7Fu;
+    tc_fence_proxy_smem();  // generic writes read by tcgen05.cp
+  }
   if constexpr (EPI == EPI_ARGMAX)
     for (int i = tid; i < (nepi + 2) * 128; i += blockDim.x) {
       wb_val[i] = -INFINITY;
@@ -598,6 +624,7 @@ __global__ void __launch_bounds__((NEPI + 2) * 32, NEPI == kTcEpiWarps ? 2 : 1)
     pdl_wait();
     pdl_launch();
     if (lane == 0) {
+      if constexpr (OPB != 0) tc_cp_scales(tmem + static_cast<uint32_t>(a.sfa_col), sdesc(su32(smem + L.sfa), 0u, 128u));
       int it = 0;
       for (int tc = 0; tc < my_tiles; ++tc) {
         const int buf = tc & 1;
@@ -609,10 +636,23 @@ __global__ void __launch_bounds__((NEPI + 2) * 32, NEPI == kTcEpiWarps ? 2 : 1)
           wait_bounded(full + s, static_cast<uint32_t>((it / a.stages) & 1), err);
           tc_fence_after();
           const uint32_t sa = su32(ring + s * L.stage_bytes), sbb = sa + 16384u;
+          if constexpr (OPB != 0) {
+            // this stage's B scales into its own four TMEM columns (no copy
+            // rewrites columns that an issued MMA may still read), then one
+            // MMA per 32-element block, each reading byte kk of the scale words
+            const uint32_t tsfb = tmem + static_cast<uint32_t>(a.sfb_col + 4 * s);
+            tc_cp_scales(tsfb, sdesc(sbb + static_cast<uint32_t>(a.np) * 128u, 0u, 128u));
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            tc_mma<FMT>(dacc, sdesc(sa + kk * 256u, 128u, 1024u), sdesc(sbb + kk * 256u, 128u, 1024u), a.idesc,
-                        (j > 0 || kk > 0) ? 1u : 0u);
+            for (int kk = 0; kk < 4; ++kk)
+              tc_mma_mx8(dacc, sdesc(sa + kk * 256u, 128u, 1024u), sdesc(sbb + kk * 256u, 128u, 1024u),
+                         a.idesc | (static_cast<uint32_t>(kk) << 4) | (static_cast<uint32_t>(kk) << 29),
+                         tmem + static_cast<uint32_t>(a.sfa_col), tsfb, (j > 0 || kk > 0) ? 1u : 0u);
+          } else {
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              tc_mma<FMT>(dacc, sdesc(sa + kk * 256u, 128u, 1024u), sdesc(sbb + kk * 256u, 128u, 1024u), a.idesc,
+                          (j > 0 || kk > 0) ? 1u : 0u);
+          }
           tc_commit(empty + s);  // the stage is free once these MMAs have read it
         }
         tc_commit(acc_full + buf);
@@ -647,13 +687,37 @@ __global__ void __launch_bounds__((NEPI + 2) * 32, NEPI == kTcEpiWarps ? 2 : 1)
     const int lq = warp & 3, h = warp >> 2;  // lane quarter; token chunk offset (stride nh)
     const int lrow = lq * 32 + lane;
     const int rp = tc_rows_per_rank(S);
+    float* s_stage = reinterpret_cast<float*>(wb_val);  // decode chain: [tokens][64 activations]
     for (int tc = 0; tc < my_tiles; ++tc) {
       const int item = cid + tc * ncl, buf = tc & 1;
       const int t = item / nlive, tok0 = s_live[1 + item % nlive] * a.mp;
       const int Mt = M - tok0 < a.mp ? M - tok0 : a.mp;  // tokens of this tile
       if (FMT == SB_FMT_FP8 || EPI == EPI_QKV) {
         epi_bar();  // every warp is done with the previous tile's scales / token table
-        if (FMT == SB_FMT_FP8) {
+        if constexpr (OPB != 0) {
+          // the block scales are in the MMA; what remains is the consumer's
+          // RMSNorm 1 / rms from the producer's sums of squares (fixed order;
+          // one warp per token, up to four tokens per warp, every load in
+          // flight at once)
+          if (p.ssq_in) {
+            const int ns = p.k >> 5;  // slices of 32 rows per token
+            float ss[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int i = warp + u * nepi;
+              if (i < Mt)
+                for (int j = lane; j < ns; j += 32) ss[u] += p.ssq_in[static_cast<size_t>(tok0 + i) * ns + j];
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int i = warp + u * nepi;
+              const float t = warp_sum(ss[u]);
+              if (lane == 0 && i < Mt) s_unscale[i] = 1.f / sqrtf(t / static_cast<float>(p.k) + p.eps);
+            }
+          } else {
+            for (int i = tid; i < Mt; i += nepi * 32) s_unscale[i] = 1.f;
+          }
+        } else if (FMT == SB_FMT_FP8) {
           const int32_t* xs = a.xshift + (a.rank_shift ? q * a.mp : 0);  // this rank's K range has its own scale
           for (int i = tid; i < Mt; i += nepi * 32) s_unscale[i] = ldexpf(1.f, -xs[tok0 + i]);
         }
@@ -696,6 +760,14 @@ __global__ void __launch_bounds__((NEPI + 2) * 32, NEPI == kTcEpiWarps ? 2 : 1)
         if (S == 1) {
           const int row = t * 128 + lrow;
           tc_epi<FMT, 8, EPI>(p, row, row < p.n, v, m0, Mt, wb_val, wb_idx, warp, tok0, tokpos);
+          if constexpr (EPI == EPI_SWIGLU) {
+            // decode chain: stage the activations (even lanes) for the down
+            // projection's operand, written by the whole epilogue below
+            if (p.nx_op && !(lane & 1) && row < p.n)
+#pragma unroll
+              for (int i = 0; i < 8; ++i)
+                if (m0 + i < Mt) s_stage[(m0 + i) * 64 + (lrow >> 1)] = v[i];
+          }
         } else {
           // push this K partial to the rank that finishes the row (16-byte DSMEM stores)
           float* dst = cg::this_cluster().map_shared_rank(part, lrow / rp) + (q * rp + lrow % rp) * ms + m0;
@@ -705,6 +777,12 @@ __global__ void __launch_bounds__((NEPI + 2) * 32, NEPI == kTcEpiWarps ? 2 : 1)
       }
       tc_fence_before();
       mbar_arrive(acc_empty + buf);  // the MMA warp may overwrite this accumulator
+      if constexpr (EPI == EPI_SWIGLU) {
+        if (S == 1 && p.nx_op) {  // the tile's 64 activations of every token -> the down projection's operand
+          epi_bar();
+          tc_bs_write_tile(p.nx_op, p.nx_np, p.nx_mp, t * 64, 64, s_stage, Mt, nullptr, nullptr, 0, tid, nepi * 32);
+        }
+      }
     }
   }
 
@@ -730,6 +808,21 @@ __global__ void __launch_bounds__((NEPI + 2) * 32, NEPI == kTcEpiWarps ? 2 : 1)
         }
       const int row = cid * 128 + r0 + lr;
       tc_epi<FMT, 4, EPI>(p, row, ok && row < p.n, v, m0, M, wb_val, wb_idx, warp, 0, tokpos);
+      if constexpr (EPI == EPI_RESID) {
+        if (p.nx_op && ok)  // decode chain: stage the new hidden values for the next operand
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            if (m0 + i < M) reinterpret_cast<float*>(wb_val)[(m0 + i) * nr + lr] = v[i];
+      }
+    }
+    if constexpr (EPI == EPI_RESID) {
+      if (p.nx_op) {
+        // the rank's new rows of every token, times the next RMSNorm weight, as
+        // the next projection's operand, plus their sums of squares per 32 rows
+        __syncthreads();
+        tc_bs_write_tile(p.nx_op, p.nx_np, p.nx_mp, cid * 128 + r0, nr, reinterpret_cast<const float*>(wb_val), M,
+                         p.nx_g, p.nx_ssq, p.n >> 5, tid, blockDim.x);
+      }
     }
   }
   if constexpr (EPI == EPI_ARGMAX) {  // combine the warps' running bests (order-independent total order)
@@ -752,7 +845,7 @@ __global__ void __launch_bounds__((NEPI + 2) * 32, NEPI == kTcEpiWarps ? 2 : 1)
   __syncthreads();
   if (warp == kMma) {
     tc_fence_after();
-    tmem_dealloc(tmem, static_cast<uint32_t>(a.ncols));
+    tmem_dealloc(tmem, static_cast<uint32_t>(OPB ? a.tmem_cols : a.ncols));
   }
 }
 
@@ -791,7 +884,10 @@ static const size_t kTcSmemTwo = 110 * 1024;  // two CTAs per SM
 // MMA-issuing threads per SM, which is what bounds the streaming of a CTA at
 // these shapes (four MMAs per stage, issue latency rather than tensor-pipe
 // time).
-static bool tc_plan_for(int fmt, int n, int k, int m, int per_sm, TcPlan& pl) {
+// bs: block-scaled operand (one CTA per SM; TMEM also holds the scales);
+// max_split: the widest K split allowed
+static bool tc_plan_for(int fmt, int n, int k, int m, int per_sm, TcPlan& pl, bool bs = false, int max_split = 8) {
+  if (bs && per_sm != 1) return false;
   const int eb = elem_bytes(fmt);
   pl.mp = tile_rows(fmt, m);
   pl.mtiles = (m + pl.mp - 1) / pl.mp;
@@ -816,7 +912,8 @@ static bool tc_plan_for(int fmt, int n, int k, int m, int per_sm, TcPlan& pl) {
   } else {
     // one CTA per SM: clusters of more than 4 CTAs of ~200 KiB do not all fit at once
     int s = slots / pl.tiles;
-    const int smax = per_sm > 1 ? 8 : 4;
+    int smax = per_sm > 1 ? 8 : 4;
+    if (smax > max_split) smax = max_split;
     if (s > smax) s = smax;
     if (s > pl.kb) s = pl.kb;
     if (s < 1) s = 1;
@@ -830,13 +927,17 @@ static bool tc_plan_for(int fmt, int n, int k, int m, int per_sm, TcPlan& pl) {
   const size_t budget = per_sm > 1 ? kTcSmemTwo : kTcSmem;
   pl.stages = 0;
   const int ml = m < pl.mp ? m : pl.mp;  // token rows of one tile
+  pl.bs = bs ? 1 : 0;
+  pl.tmem_cols = pl.ncols;
   for (int st = 8; st >= 2; --st)
-    if (tc_layout(pl.np, st, ml, pl.split, pl.epi_warps).total <= budget) {
+    if (tc_layout(pl.np, st, ml, pl.split, pl.epi_warps, bs).total <= budget && (!bs || pl.ncols + 4 + 4 * st <= 512)) {
       pl.stages = st;
       break;
     }
   if (!pl.stages) return false;
-  pl.smem = tc_layout(pl.np, pl.stages, ml, pl.split, pl.epi_warps).total;
+  if (bs)  // the accumulators, then the weight's scales (4 columns) and 4 per stage for B's
+    while (pl.tmem_cols < pl.ncols + 4 + 4 * pl.stages) pl.tmem_cols *= 2;
+  pl.smem = tc_layout(pl.np, pl.stages, ml, pl.split, pl.epi_warps, bs).total;
   return true;
 }
 
@@ -848,18 +949,18 @@ bool tc_plan(int fmt, int n, int k, int m, TcPlan& pl) {
   return tc_plan_for(fmt, n, k, m, 1, pl);
 }
 
-template <int FMT, int EPI, int NEPI>
+template <int FMT, int EPI, int NEPI, int OPB = 0>
 static int gemm_launch_n(const cudaLaunchConfig_t& cfg, const GemvParams& p, const TcArgs& a) {
   int dev = 0;
   cudaGetDevice(&dev);
   static std::atomic<unsigned> configured{0};  // one bit per device
   if (!(configured.load(std::memory_order_relaxed) & (1u << dev))) {
-    cudaError_t e = cudaFuncSetAttribute(k_tc_gemm<FMT, EPI, NEPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(k_tc_gemm<FMT, EPI, NEPI, OPB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(kTcSmem));
     if (e != cudaSuccess) return e;
     configured.fetch_or(1u << dev, std::memory_order_relaxed);
   }
-  return cudaLaunchKernelEx(&cfg, k_tc_gemm<FMT, EPI, NEPI>, p, a);
+  return cudaLaunchKernelEx(&cfg, k_tc_gemm<FMT, EPI, NEPI, OPB>, p, a);
 }
 
 template <int FMT, int EPI>
@@ -947,6 +1048,74 @@ int tc_launch(const GemvParams& p, const void* w_tc, void* operand, const TcPlan
     case SB_FMT_FP8: return tc_launch_t<SB_FMT_FP8>(p, w_tc, operand, pl, pdl, stream, operand_ready);
     case SB_FMT_INT8: return tc_launch_t<SB_FMT_INT8>(p, w_tc, operand, pl, pdl, stream, operand_ready);
     case SB_FMT_NVFP4: return tc_launch_t<SB_FMT_NVFP4>(p, w_tc, operand, pl, pdl, stream, operand_ready);
+  }
+  return SB_ERR_ARG;
+}
+
+}  // namespace sb
+
+namespace sb {
+
+bool tc_plan_bs(int n, int k, int m, int max_split, TcPlan& pl) {
+  if (m < 9 || m > 64 || n < 1 || k % 128 != 0) return false;
+  return tc_plan_for(SB_FMT_FP8, n, k, m, 1, pl, true, max_split) && pl.mtiles == 1 &&
+         pl.epi_warps == kTcMaxEpiWarps;
+}
+
+size_t tc_bs_operand_bytes(int k, int m) {
+  const int np = 2 * pad_rows(SB_FMT_FP8, m);
+  return static_cast<size_t>(k / 128) * tc_bs_block_bytes(np);
+}
+
+int tc_launch_bs(const GemvParams& p0, const void* w_tc, const void* operand, const TcPlan& pl, bool pdl,
+                 cudaStream_t stream) {
+  if (!pl.bs || pl.epi_warps != kTcMaxEpiWarps || pl.mtiles != 1) return SB_ERR_ARG;
+  GemvParams p = p0;
+  p.n_ctas = pl.n_ctas;
+  TcArgs a;
+  memset(&a, 0, sizeof(a));
+  a.wt = static_cast<const uint8_t*>(w_tc);
+  a.xq = static_cast<const uint8_t*>(operand);
+  // instruction descriptor (block-scaled): A/B e4m3 (0), K-major, UE8M0 scales
+  // (bit 23), N, M = 128; the scale ids (bits 4-5, 29-30) are set per MMA
+  a.idesc = (1u << 23) | (static_cast<uint32_t>(pl.np >> 3) << 17) | ((128u >> 4) << 24);
+  a.mp = pl.mp;
+  a.np = pl.np;
+  a.tiles = pl.tiles;
+  a.kb = pl.kb;
+  a.split = pl.split;
+  a.stages = pl.stages;
+  a.ncols = pl.ncols;
+  a.mtiles = pl.mtiles;
+  a.tmem_cols = pl.tmem_cols;
+  a.sfa_col = pl.ncols;
+  a.sfb_col = pl.ncols + 4;
+  cudaLaunchAttribute at[2];
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(pl.n_ctas);
+  cfg.blockDim = dim3((pl.epi_warps + 2) * 32);
+  cfg.dynamicSmemBytes = pl.smem;
+  cfg.stream = stream;
+  cfg.attrs = at;
+  int na = 0;
+  if (pdl) {
+    at[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (pl.split > 1) {
+    at[na].id = cudaLaunchAttributeClusterDimension;
+    at[na].val.clusterDim.x = pl.split;
+    at[na].val.clusterDim.y = 1;
+    at[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  cfg.numAttrs = na;
+  note_launch();
+  switch (p.epi) {
+    case EPI_QKV: return gemm_launch_n<SB_FMT_FP8, EPI_QKV, kTcMaxEpiWarps, 1>(cfg, p, a);
+    case EPI_RESID: return gemm_launch_n<SB_FMT_FP8, EPI_RESID, kTcMaxEpiWarps, 1>(cfg, p, a);
+    case EPI_SWIGLU: return gemm_launch_n<SB_FMT_FP8, EPI_SWIGLU, kTcMaxEpiWarps, 1>(cfg, p, a);
   }
   return SB_ERR_ARG;
 }

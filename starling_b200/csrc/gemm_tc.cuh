@@ -21,7 +21,9 @@ struct TcPlan {
   int mtiles;  // token tiles of mp rows (> 1 only for the store epilogue: prefill)
   int split;   // CTAs per cluster splitting K (1 = persistent over tiles)
   int stages;  // ring depth
-  int ncols;   // TMEM columns allocated
+  int ncols;   // TMEM columns of the two accumulators (allocated, unless bs)
+  int bs;      // block-scaled operand: TMEM also holds the scales (tmem_cols allocated)
+  int tmem_cols;
   int epi_warps;  // epilogue warps (the block has epi_warps + 2)
   int n_ctas;
   size_t smem;
@@ -29,7 +31,7 @@ struct TcPlan {
 
 // Shared-memory layout, computed identically on the host and in the kernel.
 struct TcLayout {
-  size_t stage_bytes, part, out, bars, tmem, flag, best, bval, shift, wbv, wbi, live, total;
+  size_t stage_bytes, part, out, bars, tmem, flag, best, bval, shift, wbv, wbi, live, sfa, total;
 };
 __host__ __device__ inline int tc_rows_per_rank(int split) {
   const int rp = (128 + split - 1) / split;
@@ -44,10 +46,12 @@ __host__ __device__ inline int tc_inbox_stride(int m) { return (m + 7) / 8 * 8 +
 constexpr int kTcEpiWarps = 8;
 constexpr int kTcThreads = (kTcEpiWarps + 2) * 32;
 constexpr int kTcMaxEpiWarps = 16;
-__host__ __device__ inline TcLayout tc_layout(int np, int stages, int m, int split, int epi_warps) {
+// bs: the B operand carries block scales (512 bytes per stage) and the
+// weight's unit scales take 512 bytes (tcgen05.mma kind::mxf8f6f4)
+__host__ __device__ inline TcLayout tc_layout(int np, int stages, int m, int split, int epi_warps, bool bs = false) {
   auto up = [](size_t x, size_t a) { return (x + a - 1) & ~(a - 1); };
   TcLayout L;
-  L.stage_bytes = 16384 + static_cast<size_t>(np) * 128;
+  L.stage_bytes = 16384 + static_cast<size_t>(np) * 128 + (bs ? 512 : 0);
   L.part = L.stage_bytes * stages;
   // split > 1: inbox [split source ranks][rows per rank][tc_inbox_stride(m)] of K partials
   const size_t part_bytes =
@@ -62,7 +66,8 @@ __host__ __device__ inline TcLayout tc_layout(int np, int stages, int m, int spl
   L.wbv = L.shift + 128 * 4;                    // [warps][128] running argmax value
   L.wbi = L.wbv + static_cast<size_t>(epi_warps + 2) * 128 * 4;   // [warps][128] running argmax index
   L.live = L.wbi + static_cast<size_t>(epi_warps + 2) * 128 * 4;  // [1 + 64] token tiles holding a real row (prefill)
-  L.total = L.live + 65 * 4;
+  L.sfa = up(L.live + 65 * 4, 128);  // bs: 512 bytes of UE8M0 1.0 (the weight's block scales)
+  L.total = bs ? L.sfa + 512 : L.live + 65 * 4;
   return L;
 }
 
@@ -78,5 +83,15 @@ int tc_launch(const GemvParams& p, const void* w_tc, void* operand, const TcPlan
               cudaStream_t stream, bool operand_ready = false);
 // where the shifts start inside an operand of tc_operand_bytes(fmt, k, m)
 size_t tc_shift_offset(int fmt, int k, int m);
+
+// Tensor-core decode chain (fp8 weights, 9..64 token rows, one token tile):
+// the GEMM reads a block-scaled operand that the preceding GEMM's epilogue
+// wrote (operand.cuh) instead of a prepared one.  max_split: the widest K
+// split the plan may use (1 for a SwiGLU producer, whose 32-element blocks
+// span two warps of one CTA).
+bool tc_plan_bs(int n, int k, int m, int max_split, TcPlan& pl);
+size_t tc_bs_operand_bytes(int k, int m);
+int tc_launch_bs(const GemvParams& p, const void* w_tc, const void* operand, const TcPlan& pl, bool pdl,
+                 cudaStream_t stream);
 
 }  // namespace sb

@@ -69,6 +69,18 @@ struct GemvParams {
   // >= row_len[stream]; null: no padding
   const int32_t* row_len;
   int row_T, row_b0;
+  // tensor-core decode chain (gemm_tc.cu), null elsewhere.  Producer (EPI_RESID,
+  // EPI_SWIGLU): the epilogue also writes the next projection's block-scaled
+  // fp8 operand nx_op (np = nx_np rows, token m's terms in rows m and nx_mp + m)
+  // of its new rows times nx_g (the next RMSNorm weight; null: none) and, for
+  // EPI_RESID, nx_ssq[m * (n / 32) + j] = the sum of squares of token m's new
+  // rows 32 j .. 32 j + 31.  Consumer: ssq_in (the producer's nx_ssq) gives
+  // each token's RMSNorm 1 / rms, applied to its outputs; null: none.
+  uint8_t* nx_op;
+  const uint16_t* nx_g;
+  float* nx_ssq;
+  int nx_np, nx_mp;
+  const float* ssq_in;
 };
 
 template <int FMT>

@@ -9,6 +9,7 @@
 // gemv_epilogue (gemv_epi.cuh).
 #pragma once
 #include "gemv.cuh"
+#include "operand.cuh"
 
 namespace sb {
 
@@ -46,20 +47,25 @@ __device__ __forceinline__ void tc_epi(const GemvParams& p, int row, bool row_ok
     for (int i = 0; i < CNT; ++i)
       h[i] = (row_ok && m0 + i < M) ? u16_to_f(p.y[static_cast<size_t>(tok0 + m0 + i) * p.n + row]) : 0.f;
 #pragma unroll
-    for (int i = 0; i < CNT; ++i)
-      if (row_ok && m0 + i < M)
-        p.y[static_cast<size_t>(tok0 + m0 + i) * p.n + row] = f_to_bf16_bits(h[i] + bf(p.res_mult * bf(v[i])));
+    for (int i = 0; i < CNT; ++i) {
+      const bool ok = row_ok && m0 + i < M;
+      v[i] = ok ? bf(h[i] + bf(p.res_mult * bf(v[i]))) : 0.f;  // the new hidden value (decode chain)
+      if (ok) p.y[static_cast<size_t>(tok0 + m0 + i) * p.n + row] = f_to_bf16_bits(v[i]);
+    }
   } else if constexpr (EPI == EPI_SWIGLU) {
     // act = bf16(bf16(silu(gate)) * up) (llm_kernels.py:252-260); gate row 2i, up row 2i+1
     const int inter = p.n / 2;
 #pragma unroll
     for (int i = 0; i < CNT; ++i) {
       const float up = __shfl_down_sync(0xffffffffu, v[i], 1);
+      float act = 0.f;
       if (row_ok && !(row & 1) && m0 + i < M) {
         const float gv = bf(v[i]);
         const float sg = bf(gv / (1.f + expf(-gv)));
-        p.y[static_cast<size_t>(tok0 + m0 + i) * inter + row / 2] = f_to_bf16_bits(sg * bf(up));
+        act = bf(sg * bf(up));
+        p.y[static_cast<size_t>(tok0 + m0 + i) * inter + row / 2] = f_to_bf16_bits(act);
       }
+      v[i] = act;  // even lanes: the activation (for the next operand), odd lanes 0
     }
   } else if constexpr (EPI == EPI_QKV) {
     // q/k: RoPE with each product rounded to bf16 (llm_mega.py:539-543); k/v to
