@@ -67,11 +67,20 @@ def _peaks():
 
 # --------------------------------------------------------------------------- #
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    """SM clocks and clock-event reasons sampled during the timed region.
+
+    NVML is queried (read-only) every 5 ms from a thread, so that a timed
+    region of tens of milliseconds still holds samples; without NVML,
+    nvidia-smi's 200 ms loop.  Only samples taken between mark_start() and
+    mark_end() are summarised."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    # NVML clock-event reason bits of the names above, and of the power brake
+    BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+            "hw_power_brake_slowdown": 0x80}
 
     def __init__(self, device_index: int):
         try:  # address the GPU by UUID: robust to CUDA_VISIBLE_DEVICES remapping
@@ -79,9 +88,19 @@ class ClockSampler:
         except Exception:
             self.idx = str(device_index)
         self.proc = None
-        self.lines = []
+        self.stop = None
+        self.samples = []  # (time, sm MHz, max sm MHz, set of active reasons)
+        self.t0 = self.t1 = None
+
+    def mark_start(self):
+        self.t0 = time.perf_counter()
+
+    def mark_end(self):
+        self.t1 = time.perf_counter()
 
     def __enter__(self):
+        if self._start_nvml():
+            return self
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
@@ -92,11 +111,49 @@ class ClockSampler:
             self.proc = None
         return self
 
+    def _start_nvml(self) -> bool:
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByUUID(self.idx) if self.idx.startswith("GPU-") else \
+                pynvml.nvmlDeviceGetHandleByIndex(int(self.idx))
+            mx = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+        except Exception:
+            return False
+        self.stop = threading.Event()
+
+        def loop():
+            while not self.stop.is_set():
+                try:
+                    t = time.perf_counter()
+                    sm = float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+                    r = int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(h))
+                    self.samples.append((t, sm, mx, {n for n, b in self.BITS.items() if r & b}))
+                except Exception:
+                    return
+                self.stop.wait(0.005)
+
+        self._t = threading.Thread(target=loop, daemon=True)
+        self._t.start()
+        return True
+
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            parts = [x.strip() for x in line.strip().split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm, mx = float(parts[1]), float(parts[2])
+            except ValueError:
+                continue
+            self.samples.append((time.perf_counter(), sm, mx,
+                                 {n for n, v in zip(self.NAMES, parts[5:9]) if v.lower() == "active"}))
 
     def __exit__(self, *a):
+        if self.stop is not None:
+            self.stop.set()
+            self._t.join(timeout=5)
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -105,23 +162,14 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [x.strip() for x in ln.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, parts[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
-
+        t0 = self.t0 if self.t0 is not None else float("-inf")
+        t1 = self.t1 if self.t1 is not None else float("inf")
+        inside = [x for x in list(self.samples) if t0 <= x[0] <= t1]
+        sm = [x[1] for x in inside]
+        reasons = set().union(*[x[3] for x in inside]) if inside else set()
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": inside[-1][2] if inside else None,
+                "reasons": sorted(reasons), "samples": len(sm),
+                "source": "nvml" if self.stop is not None else "nvidia-smi"}
 
 
 # --------------------------------------------------------------------------- #
@@ -204,11 +252,13 @@ def decode_timing(eng, B, emb, prompt_lengths, T, K, W, kr, world, dev, local_ra
         _barrier(world)
         torch.cuda.synchronize()
         torch.cuda.nvtx.range_push("timed_steps")  # ncu --nvtx-include "timed_steps/" selects these launches
+        clk.mark_start()
         ev0.record(stream)
         run_steps(K)
         ev1.record(stream)
         torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
+        clk.mark_end()
         _barrier(world)
     ms = _max_over_ranks(ev0.elapsed_time(ev1), world, dev)
     reset()

@@ -780,7 +780,7 @@ __global__ void __launch_bounds__((NEPI + 2) * 32, NEPI == kTcEpiWarps ? 2 : 1)
       if constexpr (EPI == EPI_SWIGLU) {
         if (S == 1 && p.nx_op) {  // the tile's 64 activations of every token -> the down projection's operand
           epi_bar();
-          tc_bs_write_tile(p.nx_op, p.nx_np, p.nx_mp, t * 64, 64, s_stage, Mt, nullptr, nullptr, 0, tid, nepi * 32);
+          tc_bs_write_tile(p.nx_op, p.nx_np, p.nx_mp, tok0, t * 64, 64, s_stage, Mt, nullptr, nullptr, 0, tid, nepi * 32);
         }
       }
     }
@@ -809,19 +809,19 @@ __global__ void __launch_bounds__((NEPI + 2) * 32, NEPI == kTcEpiWarps ? 2 : 1)
       const int row = cid * 128 + r0 + lr;
       tc_epi<FMT, 4, EPI>(p, row, ok && row < p.n, v, m0, M, wb_val, wb_idx, warp, 0, tokpos);
       if constexpr (EPI == EPI_RESID) {
-        if (p.nx_op && ok)  // decode chain: stage the new hidden values for the next operand
+        if (p.nx_op) {
+          // decode chain: this item's 32 new rows of 4 tokens, times the next
+          // RMSNorm weight, as the next projection's operand (whole 32-element
+          // blocks: no other warp involved), plus their sums of squares
+          float* sv = reinterpret_cast<float*>(wb_val) + warp * 128;  // [4 tokens][32 rows]
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
-            if (m0 + i < M) reinterpret_cast<float*>(wb_val)[(m0 + i) * nr + lr] = v[i];
-      }
-    }
-    if constexpr (EPI == EPI_RESID) {
-      if (p.nx_op) {
-        // the rank's new rows of every token, times the next RMSNorm weight, as
-        // the next projection's operand, plus their sums of squares per 32 rows
-        __syncthreads();
-        tc_bs_write_tile(p.nx_op, p.nx_np, p.nx_mp, cid * 128 + r0, nr, reinterpret_cast<const float*>(wb_val), M,
-                         p.nx_g, p.nx_ssq, p.n >> 5, tid, blockDim.x);
+          for (int i = 0; i < 4; ++i) sv[i * 32 + lane] = ok ? v[i] : 0.f;
+          __syncwarp();
+          const int nt = M - m0 < 4 ? M - m0 : 4;
+          tc_bs_write_tile(p.nx_op, p.nx_np, p.nx_mp, m0, cid * 128 + r0 + rg * 32, 32, sv, nt, p.nx_g, p.nx_ssq,
+                           p.n >> 5, lane, 32);
+          __syncwarp();
+        }
       }
     }
   }

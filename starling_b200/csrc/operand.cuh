@@ -111,15 +111,15 @@ __device__ __forceinline__ void e4m3_split8(const float* f, int shift, uint2& w0
   w1 = make_uint2(b[0], b[1]);
 }
 
-// Token rows [0, M) x elements [k0, k0 + nk) of the block-scaled operand (k0,
-// nk multiples of 32), from shared memory sv[m * nk + j], each value first
-// multiplied by g[k0 + j] (bf16; null: by 1).  ssq (non-null) receives, per
-// (token, 32-element block), the sum of squares of the values before that
-// multiply: ssq[m * ssq_ld + (k0 + j) / 32].  Threads tid < nthr (a multiple
-// of 32) take part with uniform arguments; each takes 8 consecutive elements,
-// four consecutive lanes one 32-element block.
-__device__ __forceinline__ void tc_bs_write_tile(uint8_t* op, int np, int mp, int k0, int nk, const float* sv, int M,
-                                                 const uint16_t* g, float* ssq, int ssq_ld, int tid, int nthr) {
+// Token rows m0 + [0, M) x elements [k0, k0 + nk) of the block-scaled operand
+// (k0, nk multiples of 32), from shared memory sv[m * nk + j], each value
+// first multiplied by g[k0 + j] (bf16; null: by 1).  ssq (non-null) receives,
+// per (token, 32-element block), the sum of squares of the values before that
+// multiply: ssq[(m0 + m) * ssq_ld + (k0 + j) / 32].  Threads tid < nthr (a
+// multiple of 32: a warp or more) take part with uniform arguments; each
+// takes 8 consecutive elements, four consecutive lanes one 32-element block.
+__device__ __forceinline__ void tc_bs_write_tile(uint8_t* op, int np, int mp, int m0, int k0, int nk, const float* sv,
+                                                 int M, const uint16_t* g, float* ssq, int ssq_ld, int tid, int nthr) {
   const int ng = nk >> 3;  // 8-element groups per token row (a multiple of 4)
   const int U = M * ng;
   for (int base = 0; base < U; base += nthr) {
@@ -157,12 +157,13 @@ __device__ __forceinline__ void tc_bs_write_tile(uint8_t* op, int np, int mp, in
       uint2 w0, w1;
       e4m3_split8(x, sh, w0, w1);
       const int k = k0 + j8;
-      *reinterpret_cast<uint2*>(op + tc_bs_byte(np, m, k)) = w0;
-      *reinterpret_cast<uint2*>(op + tc_bs_byte(np, mp + m, k)) = w1;
+      const int n = m0 + m;
+      *reinterpret_cast<uint2*>(op + tc_bs_byte(np, n, k)) = w0;
+      *reinterpret_cast<uint2*>(op + tc_bs_byte(np, mp + n, k)) = w1;
       if ((j8 & 31) == 0) {
-        op[tc_bs_scale_byte(np, m, k)] = static_cast<uint8_t>(127 - sh);
-        op[tc_bs_scale_byte(np, mp + m, k)] = static_cast<uint8_t>(127 - sh);
-        if (ssq) ssq[static_cast<size_t>(m) * ssq_ld + (k >> 5)] = sq;
+        op[tc_bs_scale_byte(np, n, k)] = static_cast<uint8_t>(127 - sh);
+        op[tc_bs_scale_byte(np, mp + n, k)] = static_cast<uint8_t>(127 - sh);
+        if (ssq) ssq[static_cast<size_t>(n) * ssq_ld + (k >> 5)] = sq;
       }
     }
   }
