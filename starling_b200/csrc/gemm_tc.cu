@@ -797,6 +797,9 @@ __global__ void __launch_bounds__((NEPI + 2) * 32, NEPI == kTcEpiWarps ? 2 : 1)
       const int rg = item / nch, m0 = (item % nch) * 4;
       const int lr = rg * 32 + lane;
       const bool ok = lr < nr;
+      if constexpr (EPI == EPI_RESID)  // decode chain: the next RMSNorm weight of these 32 rows, into L1 now
+        if (p.nx_op && lane == 0)
+          asm volatile("prefetch.global.L1 [%0];" ::"l"(p.nx_g + cid * 128 + r0 + rg * 32));
       float v[4] = {0.f, 0.f, 0.f, 0.f};
       if (ok)
         for (int c = 0; c < S; ++c) {
