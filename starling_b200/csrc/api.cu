@@ -273,13 +273,14 @@ static LmWork lm_work(const SbModel* md, int tokens, void* base, bool exact = fa
 // scratch | decode-chain operands: hidden-wide, inter-wide, sums of squares].
 struct WsLayout {
   size_t lm_bytes, tc_off, tc_bytes, step_off, step_bytes, chain_off, chain_op1, chain_op2, chain_ssq, total;
+  ChainPlan chain;  // valid when chain_off != 0
 };
 static size_t tc_scratch_need(const SbLinear& l, int tokens) {
   TcPlan pl;
   return tc_plan_for(l, tokens, pl) ? tc_operand_bytes(l.fmt, l.k, tokens) : 0;
 }
 static WsLayout ws_layout(const SbModel* md, int tokens) {
-  WsLayout w;
+  WsLayout w{};
   w.lm_bytes = lm_work(md, tokens, nullptr).bytes;
   w.tc_off = (w.lm_bytes + 255) & ~size_t(255);
   size_t need = tc_scratch_need(md->lm_head, tokens);
@@ -297,8 +298,7 @@ static WsLayout ws_layout(const SbModel* md, int tokens) {
   w.step_off = (w.total + 255) & ~size_t(255);
   if (w.step_bytes) w.total = w.step_off + w.step_bytes;
   w.chain_off = w.chain_op1 = w.chain_op2 = w.chain_ssq = 0;
-  ChainPlan c;
-  if (chain_plan(md, tokens, c)) {
+  if (chain_plan(md, tokens, w.chain)) {
     const SbLayer& L = md->layers[0];
     w.chain_off = (w.total + 255) & ~size_t(255);
     w.chain_op1 = (tc_bs_operand_bytes(L.o.n, tokens) + 255) & ~size_t(255);
@@ -310,8 +310,9 @@ static WsLayout ws_layout(const SbModel* md, int tokens) {
 }
 // The state's workspace must hold ws_layout().total bytes; tc scratch is
 // null when no linear of the model takes the tensor-core path at this size.
-static int tc_scratch_of(const SbModel* md, const SbState* st, void*& ptr, size_t& bytes) {
+static int tc_scratch_of(const SbModel* md, const SbState* st, void*& ptr, size_t& bytes, WsLayout* out = nullptr) {
   const WsLayout w = ws_layout(md, st->batch * st->m);
+  if (out) *out = w;
   if (st->workspace_bytes < w.total) return fail(SB_ERR_ARG, "workspace too small (%zu < %zu)", st->workspace_bytes, w.total);
   ptr = w.tc_bytes ? static_cast<char*>(st->workspace) + w.tc_off : nullptr;
   bytes = w.tc_bytes ? st->workspace_bytes - w.tc_off : 0;
@@ -324,15 +325,12 @@ struct ChainBufs {
   uint8_t* op2;  // inter-wide operand: down's (from gate/up)
   float* ssq;    // [64 tokens][hidden / 32] sums of squares of the last residual's rows
 };
-static int chain_bufs(const SbModel* md, const SbState* st, ChainBufs& b) {
-  const WsLayout w = ws_layout(md, st->batch * st->m);
-  if (!w.chain_off) return fail(SB_ERR_CONFIG, "no decode chain for this model / token count");
-  if (st->workspace_bytes < w.total) return fail(SB_ERR_ARG, "workspace too small (%zu < %zu)", st->workspace_bytes, w.total);
+// (w: the state's ws_layout, its workspace already checked against w.total)
+static void chain_bufs(const SbState* st, const WsLayout& w, ChainBufs& b) {
   char* base = static_cast<char*>(st->workspace) + w.chain_off;
   b.op1 = reinterpret_cast<uint8_t*>(base);
   b.op2 = reinterpret_cast<uint8_t*>(base + w.chain_op1);
   b.ssq = reinterpret_cast<float*>(base + w.chain_op1 + w.chain_op2);
-  return 0;
 }
 
 // Token rows above which RMSNorm runs as its own kernel instead of the GEMV
@@ -481,11 +479,12 @@ static int launch_op(const SbModel* md, const SbState* st, int l, int op, int st
     return fail(SB_ERR_ARG, "layer %d: bad packed linear", l);
   size_t tcb = 0;
   void* tcs = nullptr;
-  SB_TRY(tc_scratch_of(md, st, tcs, tcb));
-  ChainPlan cp;
+  WsLayout ws;
+  SB_TRY(tc_scratch_of(md, st, tcs, tcb, &ws));
+  const bool chain = ws.chain_off != 0;
+  const ChainPlan& cp = ws.chain;
   ChainBufs cb;
-  const bool chain = chain_plan(md, T, cp);
-  if (chain) SB_TRY(chain_bufs(md, st, cb));
+  if (chain) chain_bufs(st, ws, cb);
   auto launch_bs = [&](const char* what, const GemvParams& p, const SbLinear& lin, const void* operand,
                        const TcPlan& pl) {
     const int rc = tc_launch_bs(p, lin.w_tc, operand, pl, pdl, s);
