@@ -23,6 +23,21 @@
 //    of e4m3 values are exact, so the result differs from the dequantised
 //    fp32 reference only by fp32 accumulation order.
 //
+// Decode chain (OPB = 1, fp8 weights, 9..64 token rows): no preparation.
+// The preceding GEMM's epilogue wrote a block-scaled operand (operand.cuh):
+// the same two e4m3 terms, with one UE8M0 scale per (token, 32 elements) in
+// place of a whole-row shift, and the RMSNorm weight already applied.
+//  * The MMA is kind::mxf8f6f4.block_scale.  Each stage's 512 bytes of B
+//    scales go to the stage's own four TMEM columns (tcgen05.cp), the
+//    weight's scales are a constant 1.0, and MMA kk of a stage selects byte
+//    kk of the scale words through the descriptor's scale ids.
+//  * The epilogue applies the token's RMSNorm 1 / rms, summed from the
+//    producer's per-32-row sums of squares.
+//  * Producers: the residual epilogue (o, down) stages each finishing warp's
+//    32 new rows x 4 tokens in shared memory and writes whole blocks; the
+//    SwiGLU epilogue (gate/up, no K split) stages its tile's 64 activations
+//    of every token and writes them with all epilogue warps.
+//
 // Kernel (NEPI epilogue warps + 2: 16 + 2 with one CTA per SM, 8 + 2 with two):
 //  * warp NEPI (one thread) streams (A block, B block) pairs into a ring of
 //    shared-memory stages with bulk copies completing on mbarriers; the weight
